@@ -1,0 +1,394 @@
+"""furnace-b200: the furnace decode token loop on B200 (sm_100a).
+
+Python mirror of the reference's internal API (the reference is a Rust
+binary crate; these names follow its modules), bound to libfurnace_cuda.so
+through its C ABI (include/furnace.h):
+
+    GgufFile.open(path)                      src/gguf.rs:366
+    GgufFile.tensor(name)                    src/gguf.rs:412
+    Config.from_gguf(file)                   src/model.rs:41
+    Model.load(file)                         src/model.rs:520
+    KvCache(model, max_ctx)                  src/model.rs:330
+    Model.forward_cached(tokens, cache)      src/model.rs:579
+    quant.dequantize / quant.matmul_quant    src/quant.rs:261, :170
+    generate(model, prompt, max_new, ...)    src/generate.rs:83 (greedy)
+
+Errors raise FurnaceError carrying the library's status code and message.
+There is no CPU fallback: when the CUDA library cannot be loaded or a call
+needs a GPU that is absent, the call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import build as _build
+
+F32, F16, Q5_0, Q8_0, Q4_K, Q6_K = 0, 1, 6, 8, 12, 14
+BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q5_0: (32, 22), Q4_K: (256, 144), Q6_K: (256, 210)}
+TYPE_NAMES = {F32: "F32", F16: "F16", Q5_0: "Q5_0", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
+
+FZ_OK, FZ_EINVAL, FZ_EFORMAT, FZ_EIO, FZ_ECUDA, FZ_ENOMEM, FZ_ETIMEOUT = range(7)
+
+# Every symbol include/furnace.h declares.
+EXPORTS = [
+    "fz_last_error", "fz_version", "fz_open", "fz_open_bytes", "fz_file_free", "fz_file_info", "fz_tensor_at",
+    "fz_tensor", "fz_meta_u32", "fz_meta_f32", "fz_meta_str", "fz_meta_array_len", "fz_config_from_gguf",
+    "fz_model_load", "fz_model_free", "fz_model_config", "fz_model_bytes", "fz_kv_new", "fz_kv_free", "fz_kv_len",
+    "fz_kv_set_len", "fz_kv_read", "fz_forward", "fz_decode_greedy", "fz_dequant", "fz_matmul_quant",
+    "fz_weight_upload", "fz_weight_free", "fz_matmul_quant_dev",
+]
+
+
+class FurnaceError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+class _Config(C.Structure):
+    _fields_ = [("n_layers", C.c_uint32), ("n_heads", C.c_uint32), ("n_kv_heads", C.c_uint32),
+                ("hidden", C.c_uint32), ("ffn", C.c_uint32), ("head_dim", C.c_uint32), ("rope_theta", C.c_float),
+                ("rms_eps", C.c_float), ("vocab", C.c_uint32), ("context_length", C.c_uint32)]
+
+
+class _TensorInfo(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("dtype", C.c_uint32), ("n_dims", C.c_uint32), ("dims", C.c_uint64 * 4),
+                ("offset", C.c_uint64), ("nbytes", C.c_uint64)]
+
+
+_lib = None
+
+
+def lib_path() -> str:
+    return _build.LIB
+
+
+def load_library(build_if_missing: bool = True):
+    """Load libfurnace_cuda.so (building it in-tree first if needed)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = _build.LIB
+    if not os.path.exists(path):
+        if not build_if_missing:
+            raise FurnaceError(FZ_ECUDA, f"CUDA library missing: {path}")
+        _build.build_cuda()
+    L = C.CDLL(path)
+    P, S, U32, U64, I = C.c_void_p, C.c_size_t, C.c_uint32, C.c_uint64, C.c_int
+    fp, u32p = C.POINTER(C.c_float), C.POINTER(C.c_uint32)
+    pp = C.POINTER(C.c_void_p)
+    sig = {
+        "fz_last_error": (C.c_char_p, []),
+        "fz_version": (C.c_char_p, []),
+        "fz_open": (I, [C.c_char_p, pp]),
+        "fz_open_bytes": (I, [P, S, pp]),
+        "fz_file_free": (None, [P]),
+        "fz_file_info": (I, [P, u32p, C.POINTER(S), C.POINTER(S), C.POINTER(S)]),
+        "fz_tensor_at": (I, [P, S, C.POINTER(_TensorInfo)]),
+        "fz_tensor": (I, [P, C.c_char_p, C.POINTER(_TensorInfo), pp]),
+        "fz_meta_u32": (I, [P, C.c_char_p, u32p]),
+        "fz_meta_f32": (I, [P, C.c_char_p, fp]),
+        "fz_meta_str": (I, [P, C.c_char_p, C.POINTER(C.c_char_p)]),
+        "fz_meta_array_len": (I, [P, C.c_char_p, C.POINTER(S)]),
+        "fz_config_from_gguf": (I, [P, C.POINTER(_Config)]),
+        "fz_model_load": (I, [P, I, C.POINTER(I), pp]),
+        "fz_model_free": (None, [P]),
+        "fz_model_config": (I, [P, C.POINTER(_Config)]),
+        "fz_model_bytes": (I, [P, C.POINTER(U64), C.POINTER(U64)]),
+        "fz_kv_new": (I, [P, U32, I, pp]),
+        "fz_kv_free": (None, [P]),
+        "fz_kv_len": (I, [P, u32p]),
+        "fz_kv_set_len": (I, [P, U32]),
+        "fz_kv_read": (I, [P, U32, I, U32, fp]),
+        "fz_forward": (I, [P, P, u32p, U32, fp, u32p]),
+        "fz_decode_greedy": (I, [P, P, U32, U32, u32p, U32, u32p, fp, u32p]),
+        "fz_dequant": (I, [U32, P, S, S, fp]),
+        "fz_matmul_quant": (I, [fp, U32, P, S, U32, U32, U32, fp]),
+        "fz_weight_upload": (I, [U32, P, S, U32, U32, pp]),
+        "fz_weight_free": (None, [P]),
+        "fz_matmul_quant_dev": (I, [P, P, U32, P, P]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def _check(rc: int):
+    if rc != FZ_OK:
+        raise FurnaceError(rc, load_library().fz_last_error().decode(errors="replace"))
+
+
+def _fp(a):
+    return a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+def _u32p(a):
+    return a.ctypes.data_as(C.POINTER(C.c_uint32))
+
+
+def version() -> str:
+    return load_library().fz_version().decode()
+
+
+# ---------------------------------------------------------------------------
+# GGUF (src/gguf.rs)
+# ---------------------------------------------------------------------------
+@dataclass
+class TensorInfo:
+    """TensorInfo (src/gguf.rs:246-254): dims in ggml order."""
+    name: str
+    dims: list
+    dtype: int
+    offset: int
+    nbytes: int
+
+    def n_elements(self) -> int:
+        return int(np.prod(self.dims)) if self.dims else 1
+
+
+class GgufFile:
+    def __init__(self, handle):
+        self._h = handle
+        L = load_library()
+        v = C.c_uint32()
+        nt, nm, ds = C.c_size_t(), C.c_size_t(), C.c_size_t()
+        _check(L.fz_file_info(self._h, C.byref(v), C.byref(nt), C.byref(nm), C.byref(ds)))
+        self.version, self.n_metadata, self.data_start = v.value, nm.value, ds.value
+        self.tensors = []
+        for i in range(nt.value):
+            ti = _TensorInfo()
+            _check(L.fz_tensor_at(self._h, i, C.byref(ti)))
+            self.tensors.append(TensorInfo(ti.name.decode(), [ti.dims[k] for k in range(ti.n_dims)], ti.dtype,
+                                           ti.offset, ti.nbytes))
+
+    @classmethod
+    def open(cls, path: str) -> "GgufFile":
+        h = C.c_void_p()
+        _check(load_library().fz_open(os.fsencode(path), C.byref(h)))
+        return cls(h)
+
+    @classmethod
+    def from_bytes(cls, data: bytes) -> "GgufFile":
+        h = C.c_void_p()
+        buf = C.create_string_buffer(bytes(data), len(data)) if data else None
+        _check(load_library().fz_open_bytes(buf, len(data), C.byref(h)))
+        return cls(h)
+
+    def close(self):
+        if self._h:
+            load_library().fz_file_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def tensor(self, name: str):
+        """(TensorInfo, raw bytes) -- GgufFile::tensor (src/gguf.rs:412-434)."""
+        ti = _TensorInfo()
+        ptr = C.c_void_p()
+        _check(load_library().fz_tensor(self._h, name.encode(), C.byref(ti), C.byref(ptr)))
+        info = TensorInfo(ti.name.decode(), [ti.dims[k] for k in range(ti.n_dims)], ti.dtype, ti.offset, ti.nbytes)
+        return info, C.string_at(ptr.value, ti.nbytes)
+
+    def meta_u32(self, key: str) -> int:
+        v = C.c_uint32()
+        _check(load_library().fz_meta_u32(self._h, key.encode(), C.byref(v)))
+        return v.value
+
+    def meta_f32(self, key: str) -> float:
+        v = C.c_float()
+        _check(load_library().fz_meta_f32(self._h, key.encode(), C.byref(v)))
+        return v.value
+
+    def meta_str(self, key: str) -> str:
+        v = C.c_char_p()
+        _check(load_library().fz_meta_str(self._h, key.encode(), C.byref(v)))
+        return v.value.decode()
+
+    def meta_array_len(self, key: str) -> int:
+        v = C.c_size_t()
+        _check(load_library().fz_meta_array_len(self._h, key.encode(), C.byref(v)))
+        return v.value
+
+
+@dataclass
+class Config:
+    """Config (src/model.rs:27-38)."""
+    n_layers: int
+    n_heads: int
+    n_kv_heads: int
+    hidden: int
+    ffn: int
+    head_dim: int
+    rope_theta: float
+    rms_eps: float
+    vocab: int
+    context_length: int
+
+    @classmethod
+    def _from_c(cls, c: _Config) -> "Config":
+        return cls(c.n_layers, c.n_heads, c.n_kv_heads, c.hidden, c.ffn, c.head_dim, c.rope_theta, c.rms_eps, c.vocab,
+                   c.context_length)
+
+    @classmethod
+    def from_gguf(cls, f: GgufFile) -> "Config":
+        c = _Config()
+        _check(load_library().fz_config_from_gguf(f._h, C.byref(c)))
+        return cls._from_c(c)
+
+
+# ---------------------------------------------------------------------------
+# Model / KvCache (src/model.rs)
+# ---------------------------------------------------------------------------
+class Model:
+    def __init__(self, handle):
+        self._h = handle
+        c = _Config()
+        _check(load_library().fz_model_config(self._h, C.byref(c)))
+        self.config = Config._from_c(c)
+
+    @classmethod
+    def load(cls, f: GgufFile, tp: int = 1, devices=None) -> "Model":
+        """Model::load (src/model.rs:520-552): weights uploaded to HBM."""
+        h = C.c_void_p()
+        dev = (C.c_int * len(devices))(*devices) if devices else None
+        _check(load_library().fz_model_load(f._h, tp, dev, C.byref(h)))
+        return cls(h)
+
+    def close(self):
+        if self._h:
+            load_library().fz_model_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def param_bytes(self):
+        """(resident device bytes, GGUF bytes streamed per decode token)."""
+        r, s = C.c_uint64(), C.c_uint64()
+        _check(load_library().fz_model_bytes(self._h, C.byref(r), C.byref(s)))
+        return r.value, s.value
+
+    def forward_cached(self, tokens, cache: "KvCache", want_logits: bool = True):
+        """Model::forward_cached (src/model.rs:579-592) -> logits [vocab]
+        (or the argmax id when want_logits is False)."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32).reshape(-1)
+        am = C.c_uint32()
+        if want_logits:
+            out = np.zeros(self.config.vocab, np.float32)
+            _check(load_library().fz_forward(self._h, cache._h, _u32p(t), t.size, _fp(out), C.byref(am)))
+            return out
+        _check(load_library().fz_forward(self._h, cache._h, _u32p(t), t.size, None, C.byref(am)))
+        return am.value
+
+    def forward(self, tokens, cache: "KvCache", want_logits: bool = True):
+        """forward_cached returning (logits or None, device argmax id)."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32).reshape(-1)
+        am = C.c_uint32()
+        out = np.zeros(self.config.vocab, np.float32) if want_logits else None
+        _check(load_library().fz_forward(self._h, cache._h, _u32p(t), t.size, _fp(out) if want_logits else None,
+                                         C.byref(am)))
+        return out, am.value
+
+    def decode_greedy(self, first: int, n_steps: int, cache: "KvCache", stop_ids=(), keep_logits=False):
+        """The greedy loop of generate (src/generate.rs:122-141) on the device.
+        Returns (ids, logits [n-1, vocab] or None)."""
+        ids = np.zeros(max(1, n_steps), np.uint32)
+        st = np.ascontiguousarray(list(stop_ids) or [0], dtype=np.uint32)
+        lg = np.zeros((max(1, n_steps - 1), self.config.vocab), np.float32) if keep_logits else None
+        n = C.c_uint32()
+        _check(load_library().fz_decode_greedy(self._h, cache._h, first, n_steps, _u32p(st), len(stop_ids), _u32p(ids),
+                                               _fp(lg) if keep_logits else None, C.byref(n)))
+        k = n.value
+        return ids[:k].copy(), (lg[: max(0, k - 1)] if keep_logits else None)
+
+
+class KvCache:
+    """KvCache (src/model.rs:321-363), resident in HBM."""
+
+    def __init__(self, model: Model, max_ctx: int):
+        self.model = model
+        self.max_ctx = max_ctx
+        h = C.c_void_p()
+        _check(load_library().fz_kv_new(model._h, max_ctx, 0, C.byref(h)))
+        self._h = h
+
+    def close(self):
+        if self._h:
+            load_library().fz_kv_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def len(self) -> int:
+        v = C.c_uint32()
+        _check(load_library().fz_kv_len(self._h, C.byref(v)))
+        return v.value
+
+    @len.setter
+    def len(self, n: int):
+        _check(load_library().fz_kv_set_len(self._h, n))
+
+    def read(self, layer: int, which_v: bool, n: int) -> np.ndarray:
+        c = self.model.config
+        out = np.zeros((n, c.n_kv_heads * c.head_dim), np.float32)
+        _check(load_library().fz_kv_read(self._h, layer, int(which_v), n, _fp(out)))
+        return out
+
+
+# ---------------------------------------------------------------------------
+# quant (src/quant.rs)
+# ---------------------------------------------------------------------------
+class quant:
+    @staticmethod
+    def dequantize(dtype: int, raw: bytes, n: int) -> np.ndarray:
+        """quant::dequantize (src/quant.rs:261-281), on the device."""
+        buf = np.frombuffer(bytes(raw), dtype=np.uint8) if len(raw) else np.zeros(1, np.uint8)
+        out = np.zeros(max(n, 1), np.float32)
+        _check(load_library().fz_dequant(dtype, buf.ctypes.data, len(raw), n, _fp(out)))
+        return out[:n]
+
+    @staticmethod
+    def matmul_quant(a, raw: bytes, d_out: int, d_in: int, dtype: int) -> np.ndarray:
+        """quant::matmul_quant (src/quant.rs:170-193), on the device."""
+        a = np.ascontiguousarray(a, dtype=np.float32).reshape(-1, d_in)
+        buf = np.frombuffer(bytes(raw), dtype=np.uint8)
+        out = np.zeros((a.shape[0], d_out), np.float32)
+        _check(load_library().fz_matmul_quant(_fp(a), a.shape[0], buf.ctypes.data, buf.size, d_out, d_in, dtype,
+                                              _fp(out)))
+        return out
+
+
+def generate(model: Model, prompt_ids, max_new: int, stop_ids=(), max_ctx: int | None = None, keep_logits=False):
+    """generate (src/generate.rs:83-157) with the greedy sampler
+    (temperature 0): prefill once, then decode on the device.  Returns
+    (ids, per-step logits or None)."""
+    p = np.ascontiguousarray(prompt_ids, dtype=np.uint32)
+    max_ctx = max_ctx or min(model.config.context_length, 4096)
+    if p.size + max_new > max_ctx:
+        raise FurnaceError(FZ_EINVAL, f"prompt ({p.size}) + max tokens ({max_new}) exceeds context cap {max_ctx}")
+    cache = KvCache(model, max_ctx)
+    logits, first = model.forward(p, cache, want_logits=keep_logits)
+    ids, lg = model.decode_greedy(first, max_new, cache, stop_ids, keep_logits)
+    if keep_logits:
+        lg = np.concatenate([logits[None], lg], axis=0)[: len(ids)]
+    return ids, lg

@@ -1,0 +1,94 @@
+// Kernel launch interface (host side).  Device layouts and algorithms are
+// described in kernels.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace fz {
+
+// A matmul weight [rows, cols] resident in HBM in the device layout.
+struct DevMat {
+  uint32_t dtype = 0;
+  uint32_t rows = 0, cols = 0;
+  uint64_t stride = 0;      // bytes per row (multiple of 16)
+  uint8_t* ptr = nullptr;   // device
+  uint64_t gguf_bytes = 0;  // bytes of the same rows in GGUF encoding
+};
+
+// Device-layout row stride for `cols` elements of `dtype`.
+uint64_t dev_row_stride(uint32_t dtype, uint32_t cols);
+
+// Repack `rows` GGUF rows (raw, device memory) into the device layout at
+// dst (row stride dev_row_stride).  Same values, different byte order.
+void launch_repack(uint32_t dtype, const uint8_t* raw, uint8_t* dst, uint32_t rows, uint32_t cols, cudaStream_t s);
+
+// Dequantize device-layout rows [r0, r0+rows) of m to f32 [rows, cols],
+// bit-exact with the reference's block decoders.
+void launch_dequant(const DevMat& m, uint32_t r0, uint32_t rows, float* out, cudaStream_t s);
+
+// Dynamic per-step scalars read by the kernels (so that one captured graph
+// serves every position).
+struct StepState {
+  uint32_t pos;        // position of the token being processed
+  uint32_t token;      // token id being processed
+  uint32_t step;       // index into ids_out / forced
+  uint32_t n_forced;   // tokens [0, n_forced) of `forced` are fed in order
+  unsigned long long argmax_key;
+  uint32_t error;      // nonzero: a kernel rejected its input (see kernels.cu)
+  uint32_t pad[3];
+};
+
+enum GemvPrologue : int { PRO_COPY = 0, PRO_RMSNORM = 1 };
+enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_LOGITS = 3 };
+
+// Up to 3 weight segments sharing one input vector (q|k|v).
+struct GemvSeg {
+  DevMat w;
+  const float* bias;   // [rows] or null
+  float* out;          // destination base for this segment
+};
+
+struct GemvLaunch {
+  GemvSeg seg[3];
+  int nseg = 1;
+  const float* x = nullptr;         // input vector [cols]
+  const float* norm_w = nullptr;    // PRO_RMSNORM weight
+  float eps = 0.f;
+  int prologue = PRO_COPY;
+  int epilogue = EPI_STORE;
+  StepState* state = nullptr;       // EPI_LOGITS argmax key
+  int nseq = 1;                     // number of input vectors (x rows), output rows likewise
+};
+
+void launch_gemv(const GemvLaunch& g, cudaStream_t s);
+
+// Embedding row of state->token (or tokens[i]) dequantized to f32.
+void launch_embed(const DevMat& emb, const StepState* st, float* x, cudaStream_t s);
+
+// RoPE on q and k (cos/sin table [max_ctx][hd/2] x 2), K/V append at
+// state->pos into a cache laid out [n_kv][max_ctx][hd].
+void launch_rope_append(float* qkv, const float* rope_cs, uint32_t n_heads, uint32_t n_kv, uint32_t hd,
+                        float* kcache, float* vcache, uint32_t max_ctx, const StepState* st, cudaStream_t s);
+
+// Split-K flash-decode over positions [0, state->pos].
+struct AttnLaunch {
+  const float* q;        // [nh*hd]
+  const float* kcache;   // [nkv][max_ctx][hd]
+  const float* vcache;
+  float* ctx;            // [nh*hd]
+  float* partials;       // [nkv][splits][G][hd+2]
+  unsigned int* counters;  // [nkv], zero between launches
+  uint32_t n_heads, n_kv, hd, max_ctx, splits;
+  const StepState* state;
+};
+void launch_attention(const AttnLaunch& a, cudaStream_t s);
+uint32_t attention_splits(uint32_t n_kv, uint32_t max_ctx, int num_sms);
+
+// Step bookkeeping after the logits (argmax -> ids_out, next token, pos++).
+void launch_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, bool has_logits, cudaStream_t s);
+
+int num_sms();
+
+}  // namespace fz

@@ -1,0 +1,789 @@
+// Host runtime: model upload (Model::load, src/model.rs:520-552), device KV
+// cache (src/model.rs:321-363), the decode step as one captured CUDA graph,
+// and the C ABI declared in include/furnace.h.
+
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <vector>
+
+#include "fz_internal.h"
+#include "kernels.h"
+
+namespace fz {
+const std::string& last_error();
+}
+
+using namespace fz;
+
+#define CK(x)                                                                               \
+  do {                                                                                      \
+    cudaError_t e_ = (x);                                                                   \
+    if (e_ != cudaSuccess) fail(FZ_ECUDA, "%s failed: %s", #x, cudaGetErrorString(e_));     \
+  } while (0)
+
+namespace {
+
+// Device allocation that frees itself.
+struct DevBuf {
+  void* p = nullptr;
+  size_t n = 0;
+  DevBuf() = default;
+  explicit DevBuf(size_t bytes) { alloc(bytes); }
+  void alloc(size_t bytes) {
+    release();
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+      p = nullptr;
+      cudaGetLastError();
+      fail(FZ_ENOMEM, "cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(e));
+    }
+    n = bytes;
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+  }
+  ~DevBuf() { release(); }
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  template <class T>
+  T* as() const {
+    return reinterpret_cast<T*>(p);
+  }
+};
+
+struct Layer {
+  float *attn_norm, *ffn_norm, *bqkv;  // bqkv = [bq | bk | bv]
+  DevMat wq, wk, wv, wo, wgu, wd;      // wgu: gate/up rows interleaved
+};
+
+}  // namespace
+
+struct fz_model {
+  fz_config cfg{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  DevBuf weights;         // every quantized matrix
+  DevBuf smalls;          // norms and biases (f32)
+  DevMat embd, lm_head;
+  float* out_norm = nullptr;
+  std::vector<Layer> layers;
+  uint64_t resident = 0, streamed = 0;
+  // activations
+  DevBuf x, qkv, ctx, h, logits;
+};
+
+struct fz_kv {
+  fz_model* m = nullptr;
+  uint32_t max_ctx = 0, len = 0, splits = 0;
+  DevBuf k, v, rope_cs, partials, counters, state, forced, ids;
+  cudaGraphExec_t g_full = nullptr, g_layers = nullptr;
+  ~fz_kv() {
+    if (g_full) cudaGraphExecDestroy(g_full);
+    if (g_layers) cudaGraphExecDestroy(g_layers);
+  }
+};
+
+struct fz_weight {
+  DevBuf buf;
+  DevMat m;
+};
+
+namespace {
+
+template <class F>
+int guard(F&& f) {
+  try {
+    f();
+    return FZ_OK;
+  } catch (const Error& e) {
+    set_last_error(e.what());
+    return e.code;
+  } catch (const std::bad_alloc&) {
+    set_last_error("host allocation failed");
+    return FZ_ENOMEM;
+  } catch (const std::exception& e) {
+    set_last_error(e.what());
+    return FZ_EINVAL;
+  }
+}
+
+void need(bool cond, const char* fmt, ...) {
+  if (cond) return;
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  throw Error(FZ_EINVAL, buf);
+}
+
+uint64_t gguf_bytes(uint32_t dtype, uint64_t rows, uint32_t cols) {
+  uint32_t be, bb;
+  block_geom(dtype, &be, &bb);
+  return rows * (cols / be) * bb;
+}
+
+// Upload `rows` GGUF rows of a [rows, cols] weight (raw host bytes) into the
+// device layout at dst, through a bounded device staging buffer.
+void upload_rows(uint32_t dtype, const uint8_t* raw, uint64_t rows, uint32_t cols, uint8_t* dst, DevBuf& staging,
+                 cudaStream_t s) {
+  uint64_t row_raw = gguf_bytes(dtype, 1, cols);
+  uint64_t stride = dev_row_stride(dtype, cols);
+  uint64_t chunk_rows = staging.n / row_raw;
+  need(chunk_rows > 0, "staging buffer too small");
+  for (uint64_t r0 = 0; r0 < rows; r0 += chunk_rows) {
+    uint64_t nr = std::min(chunk_rows, rows - r0);
+    CK(cudaMemcpyAsync(staging.p, raw + r0 * row_raw, nr * row_raw, cudaMemcpyHostToDevice, s));
+    launch_repack(dtype, staging.as<uint8_t>(), dst + r0 * stride, (uint32_t)nr, cols, s);
+    CK(cudaStreamSynchronize(s));
+  }
+}
+
+const TensorEntry& tensor2d(const GgufFile& f, const std::string& name, uint64_t out, uint64_t in) {
+  const TensorEntry* t = f.find(name);
+  if (!t) fail(FZ_EFORMAT, "no tensor named '%s'", name.c_str());
+  if (t->dims.size() != 2) fail(FZ_EFORMAT, "weight '%s' is not 2-D", name.c_str());
+  if (t->dims[1] != out || t->dims[0] != in)
+    fail(FZ_EFORMAT, "weight '%s' is [%llu, %llu], expected [%llu, %llu]", name.c_str(), (unsigned long long)t->dims[1],
+         (unsigned long long)t->dims[0], (unsigned long long)out, (unsigned long long)in);
+  if (!is_quant(t->dtype))
+    fail(FZ_EFORMAT, "weight '%s' has dtype %u; the device path needs Q8_0, Q5_0, Q4_K or Q6_K", name.c_str(), t->dtype);
+  return *t;
+}
+
+// f32 vector (norm or bias) of n elements, dequantized on the host if needed.
+std::vector<float> vec_f32(const GgufFile& f, const std::string& name, uint64_t n) {
+  const TensorEntry* t = f.find(name);
+  if (!t) fail(FZ_EFORMAT, "no tensor named '%s'", name.c_str());
+  if (t->n_elements() != n) fail(FZ_EFORMAT, "tensor '%s' has %llu elements, expected %llu", name.c_str(),
+                                 (unsigned long long)t->n_elements(), (unsigned long long)n);
+  uint64_t nb;
+  const uint8_t* d = f.tensor_data(*t, &nb);
+  if (t->dtype != FZ_F32) fail(FZ_EFORMAT, "tensor '%s' must be F32 (got dtype %u)", name.c_str(), t->dtype);
+  std::vector<float> v(n);
+  memcpy(v.data(), d, n * 4);
+  return v;
+}
+
+void build_graphs(fz_kv* kv);
+
+// One decode step: embed -> layers -> [norm + lm_head + argmax] -> finalize.
+void record_step(fz_kv* kv, bool with_logits, cudaStream_t s) {
+  fz_model* m = kv->m;
+  const fz_config& c = m->cfg;
+  StepState* st = kv->state.as<StepState>();
+  uint32_t hd = c.head_dim, qd = c.n_heads * hd, kd = c.n_kv_heads * hd;
+  float* x = m->x.as<float>();
+  float* qkv = m->qkv.as<float>();
+  launch_embed(m->embd, st, x, s);
+  for (uint32_t li = 0; li < c.n_layers; li++) {
+    Layer& L = m->layers[li];
+    GemvLaunch g;
+    g.nseg = 3;
+    g.seg[0] = GemvSeg{L.wq, L.bqkv, qkv};
+    g.seg[1] = GemvSeg{L.wk, L.bqkv + qd, qkv + qd};
+    g.seg[2] = GemvSeg{L.wv, L.bqkv + qd + kd, qkv + qd + kd};
+    g.x = x;
+    g.norm_w = L.attn_norm;
+    g.eps = c.rms_eps;
+    g.prologue = PRO_RMSNORM;
+    g.epilogue = EPI_STORE;
+    launch_gemv(g, s);
+    float* kc = kv->k.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
+    float* vc = kv->v.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
+    launch_rope_append(qkv, kv->rope_cs.as<float>(), c.n_heads, c.n_kv_heads, hd, kc, vc, kv->max_ctx, st, s);
+    AttnLaunch a{qkv, kc, vc, m->ctx.as<float>(), kv->partials.as<float>(), kv->counters.as<unsigned int>(),
+                 c.n_heads, c.n_kv_heads, hd, kv->max_ctx, kv->splits, st};
+    launch_attention(a, s);
+    GemvLaunch go;
+    go.seg[0] = GemvSeg{L.wo, nullptr, x};
+    go.x = m->ctx.as<float>();
+    go.prologue = PRO_COPY;
+    go.epilogue = EPI_RESID;
+    launch_gemv(go, s);
+    GemvLaunch gu;
+    gu.seg[0] = GemvSeg{L.wgu, nullptr, m->h.as<float>()};
+    gu.x = x;
+    gu.norm_w = L.ffn_norm;
+    gu.eps = c.rms_eps;
+    gu.prologue = PRO_RMSNORM;
+    gu.epilogue = EPI_SWIGLU;
+    launch_gemv(gu, s);
+    GemvLaunch gd;
+    gd.seg[0] = GemvSeg{L.wd, nullptr, x};
+    gd.x = m->h.as<float>();
+    gd.prologue = PRO_COPY;
+    gd.epilogue = EPI_RESID;
+    launch_gemv(gd, s);
+  }
+  if (with_logits) {
+    GemvLaunch gl;
+    gl.seg[0] = GemvSeg{m->lm_head, nullptr, m->logits.as<float>()};
+    gl.x = x;
+    gl.norm_w = m->out_norm;
+    gl.eps = c.rms_eps;
+    gl.prologue = PRO_RMSNORM;
+    gl.epilogue = EPI_LOGITS;
+    gl.state = st;
+    launch_gemv(gl, s);
+  }
+  launch_finalize(st, kv->forced.as<uint32_t>(), kv->ids.as<uint32_t>(), with_logits, s);
+}
+
+void build_graphs(fz_kv* kv) {
+  if (kv->g_full) return;
+  cudaStream_t s = kv->m->stream;
+  for (int variant = 0; variant < 2; variant++) {
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    try {
+      record_step(kv, variant == 0, s);
+    } catch (...) {
+      cudaStreamEndCapture(s, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    CK(cudaStreamEndCapture(s, &g));
+    cudaGraphExec_t ge;
+    CK(cudaGraphInstantiate(&ge, g, 0));
+    cudaGraphDestroy(g);
+    (variant == 0 ? kv->g_full : kv->g_layers) = ge;
+  }
+}
+
+void set_state(fz_kv* kv, uint32_t pos, uint32_t token, uint32_t n_forced) {
+  StepState st{};
+  st.pos = pos;
+  st.token = token;
+  st.step = 0;
+  st.n_forced = n_forced;
+  st.argmax_key = 0;
+  CK(cudaMemcpyAsync(kv->state.p, &st, sizeof st, cudaMemcpyHostToDevice, kv->m->stream));
+}
+
+void check_state(fz_kv* kv) {
+  StepState st;
+  CK(cudaMemcpyAsync(&st, kv->state.p, sizeof st, cudaMemcpyDeviceToHost, kv->m->stream));
+  CK(cudaStreamSynchronize(kv->m->stream));
+  if (st.error) fail(FZ_EINVAL, "device step rejected its input (code %u)", st.error);
+}
+
+void use_device(const fz_model* m) { CK(cudaSetDevice(m->device)); }
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+const char* fz_last_error(void) { return fz::last_error().c_str(); }
+const char* fz_version(void) { return "furnace-b200 0.1 sm_100a"; }
+
+int fz_open(const char* path, fz_file** out) {
+  return guard([&] {
+    need(path && out, "null argument");
+    auto f = new fz_file();
+    try {
+      f->g = open_gguf(path);
+    } catch (...) {
+      delete f;
+      throw;
+    }
+    *out = f;
+  });
+}
+
+int fz_open_bytes(const void* data, size_t n, fz_file** out) {
+  return guard([&] {
+    need(out && (data || n == 0), "null argument");
+    auto f = new fz_file();
+    try {
+      f->g = open_gguf_bytes(data, n);
+    } catch (...) {
+      delete f;
+      throw;
+    }
+    *out = f;
+  });
+}
+
+void fz_file_free(fz_file* f) { delete f; }
+
+int fz_file_info(const fz_file* f, uint32_t* version, size_t* n_tensors, size_t* n_meta, size_t* data_start) {
+  return guard([&] {
+    need(f != nullptr, "null file");
+    if (version) *version = f->g->version;
+    if (n_tensors) *n_tensors = f->g->tensors.size();
+    if (n_meta) *n_meta = f->g->meta.size();
+    if (data_start) *data_start = f->g->data_start;
+  });
+}
+
+static void fill_info(const GgufFile& g, const TensorEntry& t, fz_tensor_info* out) {
+  out->name = t.name.c_str();
+  out->dtype = t.dtype;
+  out->n_dims = (uint32_t)t.dims.size();
+  for (int i = 0; i < 4; i++) out->dims[i] = i < (int)t.dims.size() ? t.dims[i] : 1;
+  out->offset = t.offset;
+  uint32_t be, bb;
+  out->nbytes = block_geom(t.dtype, &be, &bb) && t.n_elements() % be == 0 ? t.n_elements() / be * bb : 0;
+  (void)g;
+}
+
+int fz_tensor_at(const fz_file* f, size_t i, fz_tensor_info* out) {
+  return guard([&] {
+    need(f && out, "null argument");
+    need(i < f->g->tensors.size(), "tensor index %zu out of range", i);
+    fill_info(*f->g, f->g->tensors[i], out);
+  });
+}
+
+int fz_tensor(const fz_file* f, const char* name, fz_tensor_info* info, const void** data) {
+  return guard([&] {
+    need(f && name, "null argument");
+    const TensorEntry* t = f->g->find(name);
+    if (!t) fail(FZ_EFORMAT, "no tensor named '%s'", name);
+    uint64_t nb;
+    const uint8_t* d = f->g->tensor_data(*t, &nb);
+    if (info) fill_info(*f->g, *t, info);
+    if (data) *data = d;
+  });
+}
+
+int fz_meta_u32(const fz_file* f, const char* key, uint32_t* out) {
+  return guard([&] { *out = f->g->meta_u32(key); });
+}
+int fz_meta_f32(const fz_file* f, const char* key, float* out) {
+  return guard([&] { *out = f->g->meta_f32(key); });
+}
+int fz_meta_str(const fz_file* f, const char* key, const char** out) {
+  return guard([&] { *out = f->g->meta_str(key).c_str(); });
+}
+int fz_meta_array_len(const fz_file* f, const char* key, size_t* out) {
+  return guard([&] { *out = f->g->meta_array_len(key); });
+}
+
+int fz_config_from_gguf(const fz_file* f, fz_config* out) {
+  return guard([&] {
+    need(f && out, "null argument");
+    *out = config_from_gguf(*f->g);
+  });
+}
+
+int fz_model_load(const fz_file* f, int tp, const int* device_ids, fz_model** out) {
+  return guard([&] {
+    need(f && out, "null argument");
+    need(tp == 1, "tensor parallel degree %d not supported by this build (1 only)", tp);
+    const GgufFile& g = *f->g;
+    auto m = std::make_unique<fz_model>();
+    m->cfg = config_from_gguf(g);
+    const fz_config& c = m->cfg;
+    m->device = device_ids ? device_ids[0] : 0;
+    CK(cudaSetDevice(m->device));
+    need(c.head_dim == 64 || c.head_dim == 128, "head_dim %u unsupported (64 or 128)", c.head_dim);
+    need(c.n_kv_heads && c.n_heads % c.n_kv_heads == 0, "%u heads not divisible by %u kv heads", c.n_heads, c.n_kv_heads);
+    need(c.n_heads / c.n_kv_heads <= 8, "GQA group %u > 8 unsupported", c.n_heads / c.n_kv_heads);
+    need(c.hidden % 32 == 0 && c.ffn % 32 == 0, "hidden/ffn must be multiples of 32");
+    CK(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    uint32_t H = c.hidden, F = c.ffn, qd = c.n_heads * c.head_dim, kd = c.n_kv_heads * c.head_dim;
+
+    // tensor table and device sizes
+    struct Plan {
+      const TensorEntry* t;
+      uint64_t rows;
+      uint32_t cols;
+      DevMat* dst;
+      uint64_t row_offset;  // rows already placed (gate/up interleave handled separately)
+    };
+    m->layers.resize(c.n_layers);
+    std::vector<std::pair<const TensorEntry*, DevMat*>> mats;
+    auto add = [&](const std::string& name, uint64_t out_d, uint64_t in_d, DevMat* dst) {
+      const TensorEntry& t = tensor2d(g, name, out_d, in_d);
+      dst->dtype = t.dtype;
+      dst->rows = (uint32_t)out_d;
+      dst->cols = (uint32_t)in_d;
+      dst->stride = dev_row_stride(t.dtype, (uint32_t)in_d);
+      dst->gguf_bytes = gguf_bytes(t.dtype, out_d, (uint32_t)in_d);
+      mats.push_back({&t, dst});
+    };
+    add("token_embd.weight", c.vocab, H, &m->embd);
+    bool tied = g.find("output.weight") == nullptr;
+    if (!tied) add("output.weight", c.vocab, H, &m->lm_head);
+    std::vector<const TensorEntry*> gates(c.n_layers), ups(c.n_layers);
+    for (uint32_t i = 0; i < c.n_layers; i++) {
+      std::string p = "blk." + std::to_string(i) + ".";
+      Layer& L = m->layers[i];
+      add(p + "attn_q.weight", qd, H, &L.wq);
+      add(p + "attn_k.weight", kd, H, &L.wk);
+      add(p + "attn_v.weight", kd, H, &L.wv);
+      add(p + "attn_output.weight", H, qd, &L.wo);
+      add(p + "ffn_down.weight", H, F, &L.wd);
+      gates[i] = &tensor2d(g, p + "ffn_gate.weight", F, H);
+      ups[i] = &tensor2d(g, p + "ffn_up.weight", F, H);
+      need(gates[i]->dtype == ups[i]->dtype, "blk.%u ffn_gate/ffn_up dtypes differ (%u vs %u)", i, gates[i]->dtype,
+           ups[i]->dtype);
+      L.wgu.dtype = gates[i]->dtype;
+      L.wgu.rows = 2 * F;
+      L.wgu.cols = H;
+      L.wgu.stride = dev_row_stride(L.wgu.dtype, H);
+      L.wgu.gguf_bytes = 2 * gguf_bytes(L.wgu.dtype, F, H);
+    }
+    // one pool for every matrix, 256-byte aligned
+    uint64_t total = 0;
+    auto reserve = [&](DevMat& d) {
+      uint64_t off = total;
+      total = (total + (uint64_t)d.rows * d.stride + 255) & ~uint64_t(255);
+      return off;
+    };
+    std::vector<uint64_t> offs;
+    for (auto& pm : mats) offs.push_back(reserve(*pm.second));
+    std::vector<uint64_t> gu_off(c.n_layers);
+    for (uint32_t i = 0; i < c.n_layers; i++) gu_off[i] = reserve(m->layers[i].wgu);
+    m->weights.alloc(total);
+    CK(cudaMemset(m->weights.p, 0, total));
+    uint8_t* base = m->weights.as<uint8_t>();
+    uint64_t max_raw = 0;
+    for (auto& pm : mats) max_raw = std::max<uint64_t>(max_raw, pm.second->gguf_bytes);
+    DevBuf staging(std::min<uint64_t>(max_raw, 256ull << 20));
+    for (size_t k = 0; k < mats.size(); k++) {
+      DevMat& d = *mats[k].second;
+      d.ptr = base + offs[k];
+      uint64_t nb;
+      const uint8_t* raw = g.tensor_data(*mats[k].first, &nb);
+      upload_rows(d.dtype, raw, d.rows, d.cols, d.ptr, staging, m->stream);
+    }
+    // gate/up interleaved by row: row 2i = gate_i, row 2i+1 = up_i
+    {
+      DevBuf tmp(2 * gguf_bytes(gates[0]->dtype, 1, H) * 1024 + 16);
+      for (uint32_t i = 0; i < c.n_layers; i++) {
+        DevMat& d = m->layers[i].wgu;
+        d.ptr = base + gu_off[i];
+        uint64_t nb;
+        const uint8_t* graw = g.tensor_data(*gates[i], &nb);
+        const uint8_t* uraw = g.tensor_data(*ups[i], &nb);
+        uint64_t rb = gguf_bytes(d.dtype, 1, H);
+        // host-side interleave in chunks, then repack
+        std::vector<uint8_t> hbuf(rb * 2 * 512);
+        for (uint32_t r0 = 0; r0 < F; r0 += 512) {
+          uint32_t nr = std::min<uint32_t>(512, F - r0);
+          for (uint32_t r = 0; r < nr; r++) {
+            memcpy(&hbuf[(2 * r) * rb], graw + (uint64_t)(r0 + r) * rb, rb);
+            memcpy(&hbuf[(2 * r + 1) * rb], uraw + (uint64_t)(r0 + r) * rb, rb);
+          }
+          CK(cudaMemcpyAsync(tmp.p, hbuf.data(), 2 * nr * rb, cudaMemcpyHostToDevice, m->stream));
+          launch_repack(d.dtype, tmp.as<uint8_t>(), d.ptr + (uint64_t)2 * r0 * d.stride, 2 * nr, H, m->stream);
+          CK(cudaStreamSynchronize(m->stream));
+        }
+      }
+    }
+    if (tied) m->lm_head = m->embd;
+    // norms and biases
+    std::vector<float> smalls;
+    std::vector<std::pair<size_t, float**>> fix;
+    auto push = [&](const std::vector<float>& v, float** where) {
+      fix.push_back({smalls.size(), where});
+      smalls.insert(smalls.end(), v.begin(), v.end());
+      while (smalls.size() % 64) smalls.push_back(0.f);
+    };
+    for (uint32_t i = 0; i < c.n_layers; i++) {
+      std::string p = "blk." + std::to_string(i) + ".";
+      Layer& L = m->layers[i];
+      push(vec_f32(g, p + "attn_norm.weight", H), &L.attn_norm);
+      push(vec_f32(g, p + "ffn_norm.weight", H), &L.ffn_norm);
+      std::vector<float> b = vec_f32(g, p + "attn_q.bias", qd);
+      std::vector<float> bk = vec_f32(g, p + "attn_k.bias", kd), bv = vec_f32(g, p + "attn_v.bias", kd);
+      b.insert(b.end(), bk.begin(), bk.end());
+      b.insert(b.end(), bv.begin(), bv.end());
+      push(b, &L.bqkv);
+    }
+    push(vec_f32(g, "output_norm.weight", H), &m->out_norm);
+    m->smalls.alloc(smalls.size() * 4);
+    CK(cudaMemcpy(m->smalls.p, smalls.data(), smalls.size() * 4, cudaMemcpyHostToDevice));
+    for (auto& fx : fix) *fx.second = m->smalls.as<float>() + fx.first;
+    // activations
+    m->x.alloc(H * 4);
+    m->qkv.alloc((qd + 2 * kd) * 4);
+    m->ctx.alloc(qd * 4);
+    m->h.alloc(F * 4);
+    m->logits.alloc((uint64_t)c.vocab * 4);
+    // byte accounting
+    m->resident = total + smalls.size() * 4;
+    uint64_t per_tok = m->lm_head.gguf_bytes + m->embd.gguf_bytes / c.vocab + (uint64_t)H * 4;
+    for (auto& L : m->layers)
+      per_tok += L.wq.gguf_bytes + L.wk.gguf_bytes + L.wv.gguf_bytes + L.wo.gguf_bytes + L.wgu.gguf_bytes +
+                 L.wd.gguf_bytes + (uint64_t)(2 * H + qd + 2 * kd) * 4;
+    m->streamed = per_tok;
+    CK(cudaStreamSynchronize(m->stream));
+    *out = m.release();
+  });
+}
+
+void fz_model_free(fz_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  if (m->stream) {
+    cudaStreamSynchronize(m->stream);
+    cudaStreamDestroy(m->stream);
+  }
+  delete m;
+}
+
+int fz_model_config(const fz_model* m, fz_config* out) {
+  return guard([&] {
+    need(m && out, "null argument");
+    *out = m->cfg;
+  });
+}
+
+int fz_model_bytes(const fz_model* m, uint64_t* resident, uint64_t* streamed) {
+  return guard([&] {
+    need(m != nullptr, "null model");
+    if (resident) *resident = m->resident;
+    if (streamed) *streamed = m->streamed;
+  });
+}
+
+int fz_kv_new(fz_model* m, uint32_t max_ctx, int kv_dtype, fz_kv** out) {
+  return guard([&] {
+    need(m && out, "null argument");
+    need(kv_dtype == FZ_KV_F32, "kv dtype %d unsupported (f32 only)", kv_dtype);
+    need(max_ctx > 0, "max_ctx must be positive");
+    use_device(m);
+    const fz_config& c = m->cfg;
+    auto kv = std::make_unique<fz_kv>();
+    kv->m = m;
+    kv->max_ctx = max_ctx;
+    uint64_t per = (uint64_t)c.n_layers * c.n_kv_heads * max_ctx * c.head_dim * 4;
+    kv->k.alloc(per);
+    kv->v.alloc(per);
+    CK(cudaMemset(kv->k.p, 0, per));
+    CK(cudaMemset(kv->v.p, 0, per));
+    // RoPE factors with the reference's arithmetic (src/model.rs:207-210):
+    // freq = theta^(-2i/hd), angle = pos * freq, (sin, cos) via libm.
+    uint32_t half = c.head_dim / 2;
+    std::vector<float> cs((uint64_t)max_ctx * half * 2);
+    for (uint32_t i = 0; i < half; i++) {
+      volatile float expo = -2.0f * (float)i / (float)c.head_dim;
+      float freq = powf(c.rope_theta, expo);
+      for (uint32_t p = 0; p < max_ctx; p++) {
+        volatile float angle = (float)p * freq;
+        cs[((uint64_t)p * half + i) * 2] = cosf(angle);
+        cs[((uint64_t)p * half + i) * 2 + 1] = sinf(angle);
+      }
+    }
+    kv->rope_cs.alloc(cs.size() * 4);
+    CK(cudaMemcpy(kv->rope_cs.p, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    kv->splits = attention_splits(c.n_kv_heads, max_ctx, num_sms());
+    uint32_t G = c.n_heads / c.n_kv_heads;
+    kv->partials.alloc((uint64_t)c.n_kv_heads * kv->splits * G * (c.head_dim + 2) * 4);
+    kv->counters.alloc(c.n_kv_heads * 4 + 16);
+    CK(cudaMemset(kv->counters.p, 0, c.n_kv_heads * 4 + 16));
+    kv->state.alloc(sizeof(StepState));
+    CK(cudaMemset(kv->state.p, 0, sizeof(StepState)));
+    kv->forced.alloc((uint64_t)max_ctx * 4 + 16);
+    kv->ids.alloc((uint64_t)max_ctx * 4 + 16);
+    *out = kv.release();
+  });
+}
+
+void fz_kv_free(fz_kv* kv) {
+  if (!kv) return;
+  cudaSetDevice(kv->m->device);
+  cudaStreamSynchronize(kv->m->stream);
+  delete kv;
+}
+
+int fz_kv_len(const fz_kv* kv, uint32_t* len) {
+  return guard([&] {
+    need(kv && len, "null argument");
+    *len = kv->len;
+  });
+}
+
+int fz_kv_set_len(fz_kv* kv, uint32_t len) {
+  return guard([&] {
+    need(kv != nullptr, "null kv");
+    need(len <= kv->max_ctx, "kv len %u > max_ctx %u", len, kv->max_ctx);
+    kv->len = len;
+  });
+}
+
+int fz_kv_read(const fz_kv* kv, uint32_t layer, int which_v, uint32_t n, float* out) {
+  return guard([&] {
+    need(kv && out, "null argument");
+    const fz_config& c = kv->m->cfg;
+    need(layer < c.n_layers && n <= kv->max_ctx, "kv read out of range");
+    use_device(kv->m);
+    uint32_t hd = c.head_dim;
+    const float* base = (which_v ? kv->v : kv->k).as<float>() + (uint64_t)layer * c.n_kv_heads * kv->max_ctx * hd;
+    // device [kvh][pos][hd] -> host [pos][kvh*hd]
+    for (uint32_t h = 0; h < c.n_kv_heads; h++)
+      CK(cudaMemcpy2D(out + h * hd, (size_t)c.n_kv_heads * hd * 4, base + (uint64_t)h * kv->max_ctx * hd, hd * 4,
+                      hd * 4, n, cudaMemcpyDeviceToHost));
+  });
+}
+
+int fz_forward(fz_model* m, fz_kv* kv, const uint32_t* tokens, uint32_t n, float* logits, uint32_t* argmax) {
+  return guard([&] {
+    need(m && kv && kv->m == m, "null or mismatched handles");
+    need(tokens && n > 0, "forward with no tokens");
+    need((uint64_t)kv->len + n <= kv->max_ctx, "context overflow: %u + %u > max_ctx %u", kv->len, n, kv->max_ctx);
+    for (uint32_t i = 0; i < n; i++)
+      need(tokens[i] < m->cfg.vocab, "token id %u out of range (vocab %u)", tokens[i], m->cfg.vocab);
+    use_device(m);
+    build_graphs(kv);
+    cudaStream_t s = m->stream;
+    CK(cudaMemcpyAsync(kv->forced.p, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+    set_state(kv, kv->len, tokens[0], n);
+    for (uint32_t i = 0; i + 1 < n; i++) CK(cudaGraphLaunch(kv->g_layers, s));
+    CK(cudaGraphLaunch(kv->g_full, s));
+    if (logits) CK(cudaMemcpyAsync(logits, m->logits.p, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, s));
+    uint32_t id = 0;
+    CK(cudaMemcpyAsync(&id, kv->ids.as<uint32_t>() + (n - 1), 4, cudaMemcpyDeviceToHost, s));
+    check_state(kv);
+    kv->len += n;
+    if (argmax) *argmax = id;
+  });
+}
+
+int fz_decode_greedy(fz_model* m, fz_kv* kv, uint32_t first, uint32_t n_steps, const uint32_t* stop_ids,
+                     uint32_t n_stop, uint32_t* ids_out, float* logits_out, uint32_t* n_out) {
+  return guard([&] {
+    need(m && kv && kv->m == m && ids_out, "null or mismatched handles");
+    need(first < m->cfg.vocab, "token id %u out of range (vocab %u)", first, m->cfg.vocab);
+    if (n_out) *n_out = 0;
+    if (n_steps == 0) return;
+    uint32_t fwd = n_steps - 1;
+    need((uint64_t)kv->len + fwd <= kv->max_ctx, "context overflow: %u + %u > max_ctx %u", kv->len, fwd, kv->max_ctx);
+    for (uint32_t i = 0; i < n_stop; i++)
+      if (stop_ids[i] == first) return;  // src/generate.rs:125-127
+    ids_out[0] = first;
+    uint32_t written = 1;
+    if (fwd) {
+      use_device(m);
+      build_graphs(kv);
+      cudaStream_t s = m->stream;
+      CK(cudaMemcpyAsync(kv->forced.p, &first, 4, cudaMemcpyHostToDevice, s));
+      set_state(kv, kv->len, first, 1);
+      for (uint32_t i = 0; i < fwd; i++) {
+        CK(cudaGraphLaunch(kv->g_full, s));
+        if (logits_out)
+          CK(cudaMemcpyAsync(logits_out + (uint64_t)i * m->cfg.vocab, m->logits.p, (size_t)m->cfg.vocab * 4,
+                             cudaMemcpyDeviceToHost, s));
+      }
+      CK(cudaMemcpyAsync(ids_out + 1, kv->ids.p, (size_t)fwd * 4, cudaMemcpyDeviceToHost, s));
+      check_state(kv);
+      // Stop at the first stop id (src/generate.rs:124-127): it is not
+      // emitted.  Forward i processed ids_out[i]; when ids_out[i] stops the
+      // loop, forwards 0..i-1 are the ones the reference would have run.
+      uint32_t used = fwd;
+      for (uint32_t i = 1; i <= fwd; i++) {
+        bool stop = false;
+        for (uint32_t k = 0; k < n_stop; k++) stop |= ids_out[i] == stop_ids[k];
+        if (stop) {
+          used = i;
+          break;
+        }
+        written++;
+      }
+      kv->len += used;
+    }
+    if (n_out) *n_out = written;
+  });
+}
+
+// ---- kernel-level entry points -------------------------------------------
+int fz_weight_upload(uint32_t dtype, const void* raw, size_t nbytes, uint32_t d_out, uint32_t d_in, fz_weight** out) {
+  return guard([&] {
+    need(raw && out, "null argument");
+    need(is_quant(dtype), "no fused matmul kernel for dtype %u", dtype);
+    uint32_t be, bb;
+    block_geom(dtype, &be, &bb);
+    need(d_in % be == 0, "matmul: in dim %u not a multiple of %u", d_in, be);
+    need(nbytes == gguf_bytes(dtype, d_out, d_in), "matmul: bad weight byte count");
+    auto w = std::make_unique<fz_weight>();
+    w->m.dtype = dtype;
+    w->m.rows = d_out;
+    w->m.cols = d_in;
+    w->m.stride = dev_row_stride(dtype, d_in);
+    w->m.gguf_bytes = nbytes;
+    w->buf.alloc((uint64_t)d_out * w->m.stride + 256);
+    CK(cudaMemset(w->buf.p, 0, w->buf.n));
+    w->m.ptr = w->buf.as<uint8_t>();
+    DevBuf staging(std::min<uint64_t>(nbytes + 16, 256ull << 20));
+    upload_rows(dtype, (const uint8_t*)raw, d_out, d_in, w->m.ptr, staging, 0);
+    *out = w.release();
+  });
+}
+
+void fz_weight_free(fz_weight* w) { delete w; }
+
+int fz_matmul_quant_dev(const fz_weight* w, const float* a_dev, uint32_t seq, float* out_dev, void* stream) {
+  return guard([&] {
+    need(w && a_dev && out_dev, "null argument");
+    cudaStream_t s = (cudaStream_t)stream;
+    for (uint32_t i = 0; i < seq; i++) {
+      GemvLaunch g;
+      g.seg[0] = GemvSeg{w->m, nullptr, out_dev + (uint64_t)i * w->m.rows};
+      g.x = a_dev + (uint64_t)i * w->m.cols;
+      g.prologue = PRO_COPY;
+      g.epilogue = EPI_STORE;
+      launch_gemv(g, s);
+    }
+  });
+}
+
+int fz_matmul_quant(const float* a, uint32_t seq, const void* raw, size_t nbytes, uint32_t d_out, uint32_t d_in,
+                    uint32_t dtype, float* out) {
+  fz_weight* w = nullptr;
+  int rc = fz_weight_upload(dtype, raw, nbytes, d_out, d_in, &w);
+  if (rc) return rc;
+  rc = guard([&] {
+    need(a && out, "null argument");
+    DevBuf da((uint64_t)seq * d_in * 4), dout((uint64_t)seq * d_out * 4);
+    CK(cudaMemcpy(da.p, a, (uint64_t)seq * d_in * 4, cudaMemcpyHostToDevice));
+    int r = fz_matmul_quant_dev(w, da.as<float>(), seq, dout.as<float>(), nullptr);
+    if (r) throw Error(r, fz::last_error());
+    CK(cudaMemcpy(out, dout.p, (uint64_t)seq * d_out * 4, cudaMemcpyDeviceToHost));
+  });
+  fz_weight_free(w);
+  return rc;
+}
+
+int fz_dequant(uint32_t dtype, const void* raw, size_t nbytes, size_t n, float* out) {
+  return guard([&] {
+    need(raw && out, "null argument");
+    uint32_t be, bb;
+    need(block_geom(dtype, &be, &bb), "dequantization for type %u is not implemented", dtype);
+    if (dtype == FZ_F32) {
+      need(nbytes == n * 4, "F32 data is %zu bytes, expected %zu", nbytes, n * 4);
+      memcpy(out, raw, n * 4);
+      return;
+    }
+    need(is_quant(dtype), "dequantization for type %u is not implemented", dtype);
+    need(n % be == 0, "element count %zu is not a multiple of %u", n, be);
+    need(nbytes == n / be * bb, "data is %zu bytes, expected %zu (%zu blocks of %u)", nbytes, n / be * bb, n / be, bb);
+    // one device row of `be` elements per block keeps any block count legal
+    DevMat m;
+    m.dtype = dtype;
+    m.rows = (uint32_t)(n / be);
+    m.cols = be;
+    m.stride = dev_row_stride(dtype, be);
+    DevBuf raw_d(nbytes + 16), lay((uint64_t)m.rows * m.stride + 256), outd(n * 4 + 16);
+    CK(cudaMemset(lay.p, 0, lay.n));
+    CK(cudaMemcpy(raw_d.p, raw, nbytes, cudaMemcpyHostToDevice));
+    launch_repack(dtype, raw_d.as<uint8_t>(), lay.as<uint8_t>(), m.rows, m.cols, 0);
+    m.ptr = lay.as<uint8_t>();
+    launch_dequant(m, 0, m.rows, outd.as<float>(), 0);
+    CK(cudaMemcpy(out, outd.p, n * 4, cudaMemcpyDeviceToHost));
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,166 @@
+/* furnace.h -- C ABI of libfurnace_cuda.so, the B200 (sm_100a) implementation
+ * of the furnace decode token loop.
+ *
+ * The reference (a Rust binary crate) has no FFI of its own; its internal
+ * API is the boundary this library replaces.  Each entry point names the
+ * reference function it stands in for (paths inside the furnace project).
+ *
+ * Conventions
+ *   - Every call returns FZ_OK (0) or a nonzero FZ_E* status; fz_last_error()
+ *     returns a thread-local message for the last failure on this thread.
+ *     Where the reference panics on misuse (kv overflow, token >= vocab), the
+ *     library returns FZ_EINVAL instead and leaves its state unchanged.
+ *   - Handles are opaque.  The caller owns every host buffer it passes; the
+ *     library owns all device memory and frees it in fz_*_free.
+ *   - Matrices follow the reference convention: weights are [out, in] with
+ *     each row a contiguous run of GGUF blocks, activations [seq, in] f32,
+ *     outputs [seq, out] f32 (src/tensor.rs:1-10).
+ *   - One model handle is used from one host thread at a time, like the
+ *     reference's single caller thread (src/main.rs:162-270).
+ */
+#ifndef FURNACE_H
+#define FURNACE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+enum {
+  FZ_OK = 0,
+  FZ_EINVAL = 1,   /* bad argument, shape or state (reference: assert!/ensure!) */
+  FZ_EFORMAT = 2,  /* malformed or unsupported GGUF (reference: anyhow bail!) */
+  FZ_EIO = 3,      /* cannot open / map the file */
+  FZ_ECUDA = 4,    /* CUDA runtime or kernel error */
+  FZ_ENOMEM = 5,   /* device allocation failed */
+  FZ_ETIMEOUT = 6  /* a bounded device-side wait ran out */
+};
+
+/* ggml tensor types the decode path computes on (src/gguf.rs:180-201). */
+enum { FZ_F32 = 0, FZ_F16 = 1, FZ_Q5_0 = 6, FZ_Q8_0 = 8, FZ_Q4_K = 12, FZ_Q6_K = 14 };
+
+/* KV cache element types.  F32 is the reference's (src/model.rs:321-327). */
+enum { FZ_KV_F32 = 0 };
+
+typedef struct fz_file fz_file;   /* GgufFile (src/gguf.rs:297-304) */
+typedef struct fz_model fz_model; /* Model (src/model.rs:511-517), resident in HBM */
+typedef struct fz_kv fz_kv;       /* KvCache (src/model.rs:321-327), resident in HBM */
+
+/* Config (src/model.rs:27-38). */
+typedef struct fz_config {
+  uint32_t n_layers, n_heads, n_kv_heads, hidden, ffn, head_dim;
+  float rope_theta, rms_eps;
+  uint32_t vocab, context_length;
+} fz_config;
+
+/* Tensor table entry (TensorInfo, src/gguf.rs:246-254). dims in ggml order. */
+typedef struct fz_tensor_info {
+  const char* name;
+  uint32_t dtype;
+  uint32_t n_dims;
+  uint64_t dims[4];
+  uint64_t offset;  /* relative to the data blob */
+  uint64_t nbytes;  /* GGUF byte size of the tensor data */
+} fz_tensor_info;
+
+const char* fz_last_error(void);
+/* Library version string, e.g. "furnace-b200 0.1 sm_100a". */
+const char* fz_version(void);
+
+/* ---- GGUF file (src/gguf.rs) ------------------------------------------ */
+/* GgufFile::open (src/gguf.rs:366-380): mmap + parse with the reference's
+ * checks (magic, version 2|3, bounds, power-of-two alignment). */
+int fz_open(const char* path, fz_file** out);
+/* Parse an in-memory GGUF image (parse, src/gguf.rs:315-363).  The bytes are
+ * copied. */
+int fz_open_bytes(const void* data, size_t n, fz_file** out);
+void fz_file_free(fz_file* f);
+/* version, tensor count, metadata count, data_start (src/gguf.rs:297-304) */
+int fz_file_info(const fz_file* f, uint32_t* version, size_t* n_tensors, size_t* n_meta, size_t* data_start);
+/* TensorInfo by index (src/gguf.rs:246-291). */
+int fz_tensor_at(const fz_file* f, size_t i, fz_tensor_info* out);
+/* GgufFile::tensor (src/gguf.rs:412-434): info plus a zero-copy pointer into
+ * the mapping; fails when the data runs past the end of the file. */
+int fz_tensor(const fz_file* f, const char* name, fz_tensor_info* info, const void** data);
+/* meta_u32 / meta_f32 / meta_str (src/gguf.rs:382-401); meta_array length
+ * (src/gguf.rs:403-408). */
+int fz_meta_u32(const fz_file* f, const char* key, uint32_t* out);
+int fz_meta_f32(const fz_file* f, const char* key, float* out);
+int fz_meta_str(const fz_file* f, const char* key, const char** out);
+int fz_meta_array_len(const fz_file* f, const char* key, size_t* out);
+/* Config::from_gguf (src/model.rs:41-60). */
+int fz_config_from_gguf(const fz_file* f, fz_config* out);
+
+/* ---- Model and KV cache (src/model.rs) ----------------------------------- */
+/* Model::load (src/model.rs:520-552) with use_f32 = false: uploads the raw
+ * quantized blocks of every matmul weight to HBM (repacked into the
+ * device layout, same byte count up to 16-byte row padding) and the norms
+ * and biases as f32.  tp must be 1 in this release; device_ids may be NULL
+ * (device 0). */
+int fz_model_load(const fz_file* f, int tp, const int* device_ids, fz_model** out);
+void fz_model_free(fz_model* m);
+int fz_model_config(const fz_model* m, fz_config* out);
+/* Bytes of weights resident on the device (Model::param_bytes,
+ * src/model.rs:555-563), and the GGUF bytes one decode step streams. */
+int fz_model_bytes(const fz_model* m, uint64_t* resident, uint64_t* streamed_per_token);
+
+/* KvCache::new (src/model.rs:330-339): max_ctx positions, f32 elements. */
+int fz_kv_new(fz_model* m, uint32_t max_ctx, int kv_dtype, fz_kv** out);
+void fz_kv_free(fz_kv* kv);
+/* KvCache::len (src/model.rs:324).  set_len rewinds (or restores) the
+ * filled length; positions >= len are overwritten by later forwards. */
+int fz_kv_len(const fz_kv* kv, uint32_t* len);
+int fz_kv_set_len(fz_kv* kv, uint32_t len);
+/* Copy layer `layer`'s cached K (which_v = 0) or V rows [0, n) to the host
+ * as [n, n_kv_heads*head_dim] f32 (the reference's row layout). */
+int fz_kv_read(const fz_kv* kv, uint32_t layer, int which_v, uint32_t n, float* out);
+
+/* Model::forward_cached (src/model.rs:579-592): run the tokens at positions
+ * kv.len .. kv.len+n, advance kv.len by n, and return the last position's
+ * logits [vocab] (logits may be NULL) and their argmax (first max wins,
+ * src/generate.rs:69-77; argmax may be NULL). */
+int fz_forward(fz_model* m, fz_kv* kv, const uint32_t* tokens, uint32_t n, float* logits, uint32_t* argmax);
+
+/* Greedy decode loop of generate (src/generate.rs:122-141) at temperature 0
+ * (Sampler::sample's argmax short-circuit, src/sampler.rs:92-94): starting
+ * from `first` (the token sampled from the previous logits), runs up to
+ * n_steps-1 decode forwards on the device with the token fed back on the
+ * device, and writes the n_steps greedy ids to ids_out (ids_out[0] = first).
+ * Stops early at any of stop_ids (not written), like src/generate.rs:125-127.
+ * logits_out, when non-NULL, receives [n_steps-1, vocab]: the logits each
+ * later id was taken from.  *n_out = ids written. */
+int fz_decode_greedy(fz_model* m, fz_kv* kv, uint32_t first, uint32_t n_steps, const uint32_t* stop_ids,
+                     uint32_t n_stop, uint32_t* ids_out, float* logits_out, uint32_t* n_out);
+
+/* ---- Kernel-level entry points (src/quant.rs) ---------------------------- */
+/* quant::dequantize (src/quant.rs:261-281) on the device: raw GGUF blocks
+ * -> f32, bit-exact with the reference. */
+int fz_dequant(uint32_t dtype, const void* raw, size_t nbytes, size_t n, float* out);
+/* quant::matmul_quant (src/quant.rs:170-193) on the device: a [seq, d_in]
+ * times the quantized weight [d_out, d_in] (raw GGUF bytes) -> [seq, d_out]. */
+int fz_matmul_quant(const float* a, uint32_t seq, const void* raw, size_t nbytes, uint32_t d_out, uint32_t d_in,
+                    uint32_t dtype, float* out);
+
+/* ---- Device-resident variants (inputs already in HBM) --------------------- */
+/* Same as fz_matmul_quant with device pointers and a CUDA stream
+ * (cudaStream_t passed as void*).  `w_dev` must come from fz_weight_upload. */
+typedef struct fz_weight fz_weight;
+int fz_weight_upload(uint32_t dtype, const void* raw, size_t nbytes, uint32_t d_out, uint32_t d_in, fz_weight** out);
+void fz_weight_free(fz_weight* w);
+int fz_matmul_quant_dev(const fz_weight* w, const float* a_dev, uint32_t seq, float* out_dev, void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FURNACE_H */
