@@ -1,0 +1,373 @@
+"""Benchmark: batch-1 greedy decode tokens/s (and achieved HBM GB/s) of the
+furnace decode loop on B200, BASELINE.json's metric.
+
+Workload (N=1): configs[2], the Qwen2.5-7B shape in the Q4_K_M mix
+(synthetic seeded weights, same shapes/dtypes), 2048 random prompt ids
+prefilled, then greedy decode at positions 2048.. .  A "step" is STEP_TOKENS
+(16) decode tokens; --steps K times K steps (default 32 -> the config's 512
+decode tokens).  Weights streamed per token (4.4 GB) exceed L2 (126 MB), so no
+L2 flush is needed between steps.
+
+value : decode tok/s with inputs resident in HBM, CUDA events on the
+        library's stream around all K steps (max over ranks).
+e2e   : the same metric through the public C-ABI call (fz_decode_greedy)
+        with host buffers, one call per step, host->device token and
+        device->host ids inside the timed region.
+--impl reference : the reference path's CPU implementation (the C++
+        restatement in oracle/, the reference itself cannot be built here)
+        timed on the host cores, one decode token per step.
+
+With --gpus N > 1 (torchrun, one process per GPU) every rank decodes its own
+replica of the model (tensor parallelism is not in this build yet), so the
+scaling is weak: value = total tokens/s of all ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+STEP_TOKENS = 16
+CONFIG = "c3"
+PREFILL = 2048
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default=CONFIG)
+    ap.add_argument("--prefill", type=int, default=PREFILL)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+class Dist:
+    """torch.distributed (gloo) only for the barrier and the max-over-ranks."""
+
+    def __init__(self, n):
+        self.rank = int(os.environ.get("RANK", 0))
+        self.world = int(os.environ.get("WORLD_SIZE", 1))
+        self.local = int(os.environ.get("LOCAL_RANK", 0))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as td
+
+            td.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+            self.pg = td
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+
+        t = torch.tensor([v], dtype=torch.float64)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+class Cudart:
+    """CUDA events on the library's stream (the same libcudart it links)."""
+
+    def __init__(self):
+        import ctypes as C
+
+        for name in ("libcudart.so.12", "libcudart.so"):
+            try:
+                self.L = C.CDLL(name)
+                break
+            except OSError:
+                continue
+        else:
+            self.L = C.CDLL("/usr/local/cuda/lib64/libcudart.so")
+        self.C = C
+
+    def event(self):
+        e = self.C.c_void_p()
+        assert self.L.cudaEventCreate(self.C.byref(e)) == 0
+        return e
+
+    def record(self, e, stream):
+        assert self.L.cudaEventRecord(e, self.C.c_void_p(stream)) == 0
+
+    def elapsed_ms(self, a, b):
+        assert self.L.cudaEventSynchronize(b) == 0
+        t = self.C.c_float()
+        assert self.L.cudaEventElapsedTime(self.C.byref(t), a, b) == 0
+        return t.value
+
+    def set_device(self, d):
+        self.L.cudaSetDevice(d)
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        mhz, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                mhz.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    """DRAM bytes per GEMV launch from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "gemv_traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p))
+        except Exception:
+            return None
+    return None
+
+
+def cpu_baseline(path, vocab, budget_s=15.0):
+    """The reference path's CPU restatement (oracle/) on all host cores: a
+    short prefill, then decode tokens until ~budget_s of decode time."""
+    from furnace_b200 import synth
+    from oracle import oracle
+
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+    m = oracle.Model(path)
+    ids = synth.prompt_ids(vocab, 8, seed=1)
+    kv = m.kv_new(64)
+    t0 = time.perf_counter()
+    lg = m.forward_cached(ids, kv)
+    prefill_s = time.perf_counter() - t0
+    n, dec = 0, 0.0
+    tok = int(lg.argmax())
+    while n < 32 and (dec < budget_s or n < 2):
+        t0 = time.perf_counter()
+        lg = m.forward_cached([tok], kv)
+        dec += time.perf_counter() - t0
+        tok = int(lg.argmax())
+        n += 1
+    m.close()
+    return {"value": n / dec, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{n} greedy decode tokens after an 8-token prefill ({prefill_s:.1f} s) at context 8-{8 + n}, "
+                      f"same synthetic GGUF, oracle/ C++ restatement of the reference CPU path, {cores} threads"}
+
+
+def run_reference(args, dist):
+    """--impl reference: the reference's CPU path (restated) on host cores."""
+    from furnace_b200 import synth
+    from oracle import oracle
+
+    if dist.rank != 0:
+        return
+    path = synth.ensure(args.config)
+    spec = synth.spec(args.config)
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+    m = oracle.Model(path)
+    ids = synth.prompt_ids(spec.vocab, 8, seed=1)
+    kv = m.kv_new(16 + args.warmup + args.steps)
+    tok = int(m.forward_cached(ids, kv).argmax())
+    for _ in range(args.warmup):
+        tok = int(m.forward_cached([tok], kv).argmax())
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok = int(m.forward_cached([tok], kv).argmax())
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    sample = (f"one greedy decode token per step (a sample of the {STEP_TOKENS}-token step) after an 8-token prefill, "
+              f"oracle/ C++ restatement of the reference CPU path (Rust toolchain absent), {cores} threads")
+    line = {"metric": "decode_tok_per_s", "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt * 1000 / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"{spec.name} batch-1 greedy decode (CPU sample)", "context": "8+"},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, dist):
+    import numpy as np
+
+    import furnace_b200 as fz
+    from furnace_b200 import synth
+
+    spec = synth.spec(args.config)
+    if dist.rank == 0:
+        path = synth.ensure(args.config)
+    dist.barrier()
+    path = synth.ensure(args.config)
+    dev = dist.local
+    cud = Cudart()
+    cud.set_device(dev)
+    f = fz.GgufFile.open(path)
+    model = fz.Model.load(f, devices=[dev])
+    cfg = model.config
+    resident, per_tok = model.param_bytes()
+    stream, _ = model.stream()
+    T = STEP_TOKENS
+    total_tokens = args.steps * T
+    max_ctx = args.prefill + max(args.warmup * T, 2 * T) + total_tokens + 8
+    kv = fz.KvCache(model, max_ctx)
+    prompt = synth.prompt_ids(cfg.vocab, args.prefill, seed=dist.rank)
+    t0 = time.perf_counter()
+    _, first = model.forward(prompt, kv, want_logits=False)
+    prefill_s = time.perf_counter() - t0
+    base = kv.len
+    # warm-up steps (untimed), then rewind so the timed tokens sit at base..
+    tok = first
+    for _ in range(args.warmup):
+        ids, _ = model.decode_greedy(tok, T + 1, kv)
+        tok = int(ids[-1])
+    kv.len = base
+    # ---- device-timed region: K steps enqueued back to back -------------
+    sampler = ClockSampler(dev)
+    sampler.start()
+    time.sleep(0.3)
+    dist.barrier()
+    e0, e1 = cud.event(), cud.event()
+    cud.record(e0, stream)
+    ids, _ = model.decode_greedy(first, total_tokens + 1, kv)
+    cud.record(e1, stream)
+    ms = cud.elapsed_ms(e0, e1)
+    dist.barrier()
+    clocks = sampler.stop()
+    ms = dist.max(ms)
+    tok_s = total_tokens * dist.world / (ms / 1000.0)
+    # ---- e2e: public API, one call per step, host buffers ---------------
+    kv.len = base
+    dist.barrier()
+    t0 = time.perf_counter()
+    tok = first
+    for _ in range(args.steps):
+        ids2, _ = model.decode_greedy(tok, T + 1, kv)
+        tok = int(ids2[-1])
+    e2e_s = dist.max(time.perf_counter() - t0)
+    e2e = {"value": total_tokens * dist.world / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 + 32,
+           "d2h_bytes_per_step": 4 * (T + 1) + 32,
+           "note": "fz_decode_greedy per step; h2d = seed token + step state, d2h = ids + status"}
+    # ---- per-op timing of one step's kernels (roofline of the GEMV) -----
+    kv.len = base
+    prof = model.step_profile(first, T, kv)
+    gemv_ops = ["qkv", "o_proj", "gate_up", "down", "lm_head"]
+    g_ms = sum(prof[o][0] for o in gemv_ops)
+    g_b = sum(prof[o][1] for o in gemv_ops)
+    g_n = sum(prof[o][2] for o in gemv_ops)
+    peak, peak_src = measured_peaks()
+    achieved = (g_b / g_n) / (g_ms / g_n / 1000.0) / 1e9
+    traffic = ncu_traffic()
+    roofline = {"kernel": "k_gemv (all GEMV launches of a decode step)", "bound": "hbm", "achieved": achieved,
+                "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_src} hbm_gbs",
+                "bytes_per_launch": g_b / g_n, "avg_launch_us": g_ms / g_n * 1000,
+                "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
+                "traffic_source": traffic.get("source") if traffic else None}
+    step_ms_sum = sum(v[0] for v in prof.values())
+    ops = {o: {"ms_per_token": prof[o][0] / T, "share": prof[o][0] / step_ms_sum,
+               "gbs": (prof[o][1] / (prof[o][0] / 1000.0) / 1e9) if prof[o][0] else None} for o in prof}
+    hbm = per_tok * tok_s / dist.world / 1e9
+    launches_per_token = 6 * cfg.n_layers + 3
+    out = {
+        "metric": "decode_tok_per_s", "value": tok_s, "unit": "tok/s", "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{spec.name}: {args.prefill}-token prefill then {total_tokens} greedy decode tokens "
+                               f"(batch 1), {T} tokens per step", "model": spec.name, "global_batch": dist.world,
+                   "seq_len": args.prefill + total_tokens, "parallelism": f"replicas{dist.world}",
+                   "l2": "inputs larger than L2: %.2f GB of weights streamed per token" % (per_tok / 1e9),
+                   "kv": "f32"},
+        "hbm_gbs_per_gpu": hbm, "hbm_frac_of_8tbs": hbm / 8000.0, "hbm_frac_of_measured": hbm / peak,
+        "bytes_per_token": per_tok, "ms_per_token": ms / total_tokens, "prefill_s": prefill_s,
+        "gpu_launches": launches_per_token * total_tokens, "clocks": clocks, "e2e": e2e, "roofline": roofline,
+        "ops": ops,
+    }
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(path, cfg.vocab)
+    if dist.rank == 0:
+        print(json.dumps(out), flush=True)
+    kv.close()
+    model.close()
+
+
+def main():
+    args = parse()
+    dist = Dist(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, dist)
+        else:
+            run_ours(args, dist)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

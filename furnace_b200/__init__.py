@@ -40,8 +40,10 @@ EXPORTS = [
     "fz_tensor", "fz_meta_u32", "fz_meta_f32", "fz_meta_str", "fz_meta_array_len", "fz_config_from_gguf",
     "fz_model_load", "fz_model_free", "fz_model_config", "fz_model_bytes", "fz_kv_new", "fz_kv_free", "fz_kv_len",
     "fz_kv_set_len", "fz_kv_read", "fz_forward", "fz_decode_greedy", "fz_dequant", "fz_matmul_quant",
-    "fz_weight_upload", "fz_weight_free", "fz_matmul_quant_dev",
+    "fz_weight_upload", "fz_weight_free", "fz_matmul_quant_dev", "fz_step_profile", "fz_model_stream",
 ]
+
+OPS = ["embed", "qkv", "rope_append", "attention", "o_proj", "gate_up", "down", "lm_head", "finalize"]
 
 
 class FurnaceError(RuntimeError):
@@ -112,6 +114,8 @@ def load_library(build_if_missing: bool = True):
         "fz_weight_upload": (I, [U32, P, S, U32, U32, pp]),
         "fz_weight_free": (None, [P]),
         "fz_matmul_quant_dev": (I, [P, P, U32, P, P]),
+        "fz_model_stream": (I, [P, pp, C.POINTER(I)]),
+        "fz_step_profile": (I, [P, P, U32, U32, C.POINTER(C.c_double), C.POINTER(C.c_double), u32p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -303,6 +307,20 @@ class Model:
         _check(load_library().fz_forward(self._h, cache._h, _u32p(t), t.size, _fp(out) if want_logits else None,
                                          C.byref(am)))
         return out, am.value
+
+    def stream(self):
+        """(cudaStream_t as int, device ordinal) the model runs on."""
+        st, dev = C.c_void_p(), C.c_int()
+        _check(load_library().fz_model_stream(self._h, C.byref(st), C.byref(dev)))
+        return st.value or 0, dev.value
+
+    def step_profile(self, first: int, reps: int, cache: "KvCache"):
+        """Per-op decode timings (src/perf.rs counterpart): {op: (ms, bytes, launches)}."""
+        ms = (C.c_double * len(OPS))()
+        by = (C.c_double * len(OPS))()
+        ln = np.zeros(len(OPS), np.uint32)
+        _check(load_library().fz_step_profile(self._h, cache._h, first, reps, ms, by, _u32p(ln)))
+        return {op: (ms[i], by[i], int(ln[i])) for i, op in enumerate(OPS)}
 
     def decode_greedy(self, first: int, n_steps: int, cache: "KvCache", stop_ids=(), keep_logits=False):
         """The greedy loop of generate (src/generate.rs:122-141) on the device.

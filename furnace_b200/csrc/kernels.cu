@@ -500,6 +500,18 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(GemvParams p) {
   }
 }
 
+constexpr size_t GEMV_MAX_SMEM = 200 * 1024;
+
+// Opt the GEMV kernels into large dynamic shared memory (once per device,
+// outside any stream capture).
+void kernels_init() {
+  CK(cudaFuncSetAttribute(k_gemv<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM));
+  CK(cudaFuncSetAttribute(k_gemv<EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM));
+  CK(cudaFuncSetAttribute(k_gemv<EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM));
+  CK(cudaFuncSetAttribute(k_gemv<EPI_LOGITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM));
+  num_sms();
+}
+
 void launch_gemv(const GemvLaunch& g, cudaStream_t st) {
   GemvParams p{};
   uint32_t cols = g.seg[0].w.cols;
@@ -526,14 +538,8 @@ void launch_gemv(const GemvLaunch& g, cudaStream_t st) {
   p.eps = g.eps;
   p.prologue = g.prologue;
   p.state = g.state;
-  static bool attr_set[4] = {false, false, false, false};
-  auto run = [&](auto kern, int idx) {
-    if (!attr_set[idx]) {
-      CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-      attr_set[idx] = true;
-    }
-    kern<<<begin, GEMV_THREADS, smem, st>>>(p);
-  };
+  if (smem > GEMV_MAX_SMEM) fail(FZ_EINVAL, "gemv: %u input columns exceed the shared-memory vector", cols);
+  auto run = [&](auto kern, int) { kern<<<begin, GEMV_THREADS, smem, st>>>(p); };
   switch (g.epilogue) {
     case EPI_STORE: run(k_gemv<EPI_STORE>, 0); break;
     case EPI_RESID: run(k_gemv<EPI_RESID>, 1); break;
@@ -615,7 +621,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
   __shared__ int s_last;
   const uint32_t G = nh / nkv, kvh = blockIdx.y, split = blockIdx.x, S = gridDim.x;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t total = st->pos + 1;
+  // the host keeps pos < max_ctx; the clamp keeps every read in bounds regardless
+  const uint32_t total = min(st->pos + 1, max_ctx);
   const uint32_t t0 = (uint32_t)((uint64_t)total * split / S), t1 = (uint32_t)((uint64_t)total * (split + 1) / S);
   const uint32_t n = t1 - t0;
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));

@@ -90,5 +90,6 @@ uint32_t attention_splits(uint32_t n_kv, uint32_t max_ctx, int num_sms);
 void launch_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, bool has_logits, cudaStream_t s);
 
 int num_sms();
+void kernels_init();
 
 }  // namespace fz

@@ -173,15 +173,27 @@ std::vector<float> vec_f32(const GgufFile& f, const std::string& name, uint64_t 
 
 void build_graphs(fz_kv* kv);
 
+// Optional per-launch instrumentation (fz_step_profile): called with the op
+// kind before (begin = true) and after each launch.
+struct OpHook {
+  virtual void at(int op, bool begin) = 0;
+  virtual ~OpHook() = default;
+};
+
 // One decode step: embed -> layers -> [norm + lm_head + argmax] -> finalize.
-void record_step(fz_kv* kv, bool with_logits, cudaStream_t s) {
+void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nullptr) {
+  auto H = [&](int op, bool b) {
+    if (hook) hook->at(op, b);
+  };
   fz_model* m = kv->m;
   const fz_config& c = m->cfg;
   StepState* st = kv->state.as<StepState>();
   uint32_t hd = c.head_dim, qd = c.n_heads * hd, kd = c.n_kv_heads * hd;
   float* x = m->x.as<float>();
   float* qkv = m->qkv.as<float>();
+  H(FZ_OP_EMBED, true);
   launch_embed(m->embd, st, x, s);
+  H(FZ_OP_EMBED, false);
   for (uint32_t li = 0; li < c.n_layers; li++) {
     Layer& L = m->layers[li];
     GemvLaunch g;
@@ -194,19 +206,27 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s) {
     g.eps = c.rms_eps;
     g.prologue = PRO_RMSNORM;
     g.epilogue = EPI_STORE;
+    H(FZ_OP_QKV, true);
     launch_gemv(g, s);
+    H(FZ_OP_QKV, false);
     float* kc = kv->k.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
     float* vc = kv->v.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
+    H(FZ_OP_ROPE, true);
     launch_rope_append(qkv, kv->rope_cs.as<float>(), c.n_heads, c.n_kv_heads, hd, kc, vc, kv->max_ctx, st, s);
+    H(FZ_OP_ROPE, false);
     AttnLaunch a{qkv, kc, vc, m->ctx.as<float>(), kv->partials.as<float>(), kv->counters.as<unsigned int>(),
                  c.n_heads, c.n_kv_heads, hd, kv->max_ctx, kv->splits, st};
+    H(FZ_OP_ATTN, true);
     launch_attention(a, s);
+    H(FZ_OP_ATTN, false);
     GemvLaunch go;
     go.seg[0] = GemvSeg{L.wo, nullptr, x};
     go.x = m->ctx.as<float>();
     go.prologue = PRO_COPY;
     go.epilogue = EPI_RESID;
+    H(FZ_OP_OPROJ, true);
     launch_gemv(go, s);
+    H(FZ_OP_OPROJ, false);
     GemvLaunch gu;
     gu.seg[0] = GemvSeg{L.wgu, nullptr, m->h.as<float>()};
     gu.x = x;
@@ -214,13 +234,17 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s) {
     gu.eps = c.rms_eps;
     gu.prologue = PRO_RMSNORM;
     gu.epilogue = EPI_SWIGLU;
+    H(FZ_OP_GATEUP, true);
     launch_gemv(gu, s);
+    H(FZ_OP_GATEUP, false);
     GemvLaunch gd;
     gd.seg[0] = GemvSeg{L.wd, nullptr, x};
     gd.x = m->h.as<float>();
     gd.prologue = PRO_COPY;
     gd.epilogue = EPI_RESID;
+    H(FZ_OP_DOWN, true);
     launch_gemv(gd, s);
+    H(FZ_OP_DOWN, false);
   }
   if (with_logits) {
     GemvLaunch gl;
@@ -231,9 +255,13 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s) {
     gl.prologue = PRO_RMSNORM;
     gl.epilogue = EPI_LOGITS;
     gl.state = st;
+    H(FZ_OP_LMHEAD, true);
     launch_gemv(gl, s);
+    H(FZ_OP_LMHEAD, false);
   }
+  H(FZ_OP_FINALIZE, true);
   launch_finalize(st, kv->forced.as<uint32_t>(), kv->ids.as<uint32_t>(), with_logits, s);
+  H(FZ_OP_FINALIZE, false);
 }
 
 void build_graphs(fz_kv* kv) {
@@ -392,6 +420,7 @@ int fz_model_load(const fz_file* f, int tp, const int* device_ids, fz_model** ou
     need(c.n_heads / c.n_kv_heads <= 8, "GQA group %u > 8 unsupported", c.n_heads / c.n_kv_heads);
     need(c.hidden % 32 == 0 && c.ffn % 32 == 0, "hidden/ffn must be multiples of 32");
     CK(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    kernels_init();
     uint32_t H = c.hidden, F = c.ffn, qd = c.n_heads * c.head_dim, kd = c.n_kv_heads * c.head_dim;
 
     // tensor table and device sizes
@@ -550,6 +579,14 @@ int fz_model_bytes(const fz_model* m, uint64_t* resident, uint64_t* streamed) {
   });
 }
 
+int fz_model_stream(const fz_model* m, void** stream, int* device) {
+  return guard([&] {
+    need(m != nullptr, "null model");
+    if (stream) *stream = (void*)m->stream;
+    if (device) *device = m->device;
+  });
+}
+
 int fz_kv_new(fz_model* m, uint32_t max_ctx, int kv_dtype, fz_kv** out) {
   return guard([&] {
     need(m && out, "null argument");
@@ -699,6 +736,66 @@ int fz_decode_greedy(fz_model* m, fz_kv* kv, uint32_t first, uint32_t n_steps, c
   });
 }
 
+int fz_step_profile(fz_model* m, fz_kv* kv, uint32_t first, uint32_t reps, double* ms, double* bytes,
+                    uint32_t* launches) {
+  return guard([&] {
+    need(m && kv && kv->m == m && ms && bytes && launches, "null or mismatched handles");
+    need(first < m->cfg.vocab, "token id %u out of range (vocab %u)", first, m->cfg.vocab);
+    need((uint64_t)kv->len + reps <= kv->max_ctx, "context overflow: %u + %u > max_ctx %u", kv->len, reps, kv->max_ctx);
+    use_device(m);
+    cudaStream_t s = m->stream;
+    struct Hook : OpHook {
+      std::vector<cudaEvent_t> ev;
+      std::vector<int> ops;
+      cudaStream_t s;
+      void at(int op, bool begin) override {
+        cudaEvent_t e;
+        CK(cudaEventCreate(&e));
+        CK(cudaEventRecord(e, s));
+        ev.push_back(e);
+        if (begin) ops.push_back(op);
+      }
+      ~Hook() override {
+        for (auto e : ev) cudaEventDestroy(e);
+      }
+    } hook;
+    hook.s = s;
+    for (int k = 0; k < FZ_OP_COUNT; k++) {
+      ms[k] = 0;
+      bytes[k] = 0;
+      launches[k] = 0;
+    }
+    CK(cudaMemcpyAsync(kv->forced.p, &first, 4, cudaMemcpyHostToDevice, s));
+    set_state(kv, kv->len, first, 1);
+    for (uint32_t r = 0; r < reps; r++) record_step(kv, true, s, &hook);
+    CK(cudaStreamSynchronize(s));
+    for (size_t i = 0; i < hook.ops.size(); i++) {
+      float t = 0;
+      CK(cudaEventElapsedTime(&t, hook.ev[2 * i], hook.ev[2 * i + 1]));
+      ms[hook.ops[i]] += t;
+      launches[hook.ops[i]] += 1;
+    }
+    check_state(kv);
+    // algorithmic bytes per op kind
+    const fz_config& c = m->cfg;
+    uint64_t H = c.hidden, F = c.ffn, qd = (uint64_t)c.n_heads * c.head_dim, kd = (uint64_t)c.n_kv_heads * c.head_dim;
+    for (uint32_t r = 0; r < reps; r++) {
+      uint64_t pos = kv->len + r;
+      bytes[FZ_OP_EMBED] += m->embd.gguf_bytes / c.vocab + H * 4;
+      for (auto& L : m->layers) {
+        bytes[FZ_OP_QKV] += L.wq.gguf_bytes + L.wk.gguf_bytes + L.wv.gguf_bytes + (2 * H + qd + 2 * kd) * 4;
+        bytes[FZ_OP_ROPE] += (qd + 2 * kd) * 4 + (qd + 2 * kd) * 4;
+        bytes[FZ_OP_ATTN] += 2 * (pos + 1) * kd * 4 + 2 * qd * 4;
+        bytes[FZ_OP_OPROJ] += L.wo.gguf_bytes + (qd + 2 * H) * 4;
+        bytes[FZ_OP_GATEUP] += L.wgu.gguf_bytes + (2 * H + F) * 4;
+        bytes[FZ_OP_DOWN] += L.wd.gguf_bytes + (F + 2 * H) * 4;
+      }
+      bytes[FZ_OP_LMHEAD] += m->lm_head.gguf_bytes + (2 * H + (uint64_t)c.vocab) * 4;
+    }
+    kv->len += reps;
+  });
+}
+
 // ---- kernel-level entry points -------------------------------------------
 int fz_weight_upload(uint32_t dtype, const void* raw, size_t nbytes, uint32_t d_out, uint32_t d_in, fz_weight** out) {
   return guard([&] {
@@ -708,6 +805,7 @@ int fz_weight_upload(uint32_t dtype, const void* raw, size_t nbytes, uint32_t d_
     block_geom(dtype, &be, &bb);
     need(d_in % be == 0, "matmul: in dim %u not a multiple of %u", d_in, be);
     need(nbytes == gguf_bytes(dtype, d_out, d_in), "matmul: bad weight byte count");
+    kernels_init();
     auto w = std::make_unique<fz_weight>();
     w->m.dtype = dtype;
     w->m.rows = d_out;

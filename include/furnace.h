@@ -109,6 +109,9 @@ int fz_model_config(const fz_model* m, fz_config* out);
 /* Bytes of weights resident on the device (Model::param_bytes,
  * src/model.rs:555-563), and the GGUF bytes one decode step streams. */
 int fz_model_bytes(const fz_model* m, uint64_t* resident, uint64_t* streamed_per_token);
+/* The CUDA stream (cudaStream_t) and device ordinal the model's work runs on,
+ * so a caller can order its own work or record timing events on it. */
+int fz_model_stream(const fz_model* m, void** stream, int* device);
 
 /* KvCache::new (src/model.rs:330-339): max_ctx positions, f32 elements. */
 int fz_kv_new(fz_model* m, uint32_t max_ctx, int kv_dtype, fz_kv** out);
@@ -137,6 +140,19 @@ int fz_forward(fz_model* m, fz_kv* kv, const uint32_t* tokens, uint32_t n, float
  * later id was taken from.  *n_out = ids written. */
 int fz_decode_greedy(fz_model* m, fz_kv* kv, uint32_t first, uint32_t n_steps, const uint32_t* stop_ids,
                      uint32_t n_stop, uint32_t* ids_out, float* logits_out, uint32_t* n_out);
+
+/* Per-op decode timings, the device counterpart of the reference's perf
+ * counters (src/perf.rs:25-39, reported by `run --timings`): runs `reps`
+ * greedy decode steps from kv.len WITHOUT the graph, with CUDA events around
+ * every launch, and accumulates per op kind (FZ_OP_*) the milliseconds, the
+ * launches and the algorithmic bytes (GGUF weight bytes, KV bytes, vectors).
+ * Advances kv.len by reps like fz_decode_greedy. */
+enum {
+  FZ_OP_EMBED = 0, FZ_OP_QKV, FZ_OP_ROPE, FZ_OP_ATTN, FZ_OP_OPROJ, FZ_OP_GATEUP, FZ_OP_DOWN, FZ_OP_LMHEAD,
+  FZ_OP_FINALIZE, FZ_OP_COUNT
+};
+int fz_step_profile(fz_model* m, fz_kv* kv, uint32_t first, uint32_t reps, double* ms, double* bytes,
+                    uint32_t* launches);
 
 /* ---- Kernel-level entry points (src/quant.rs) ---------------------------- */
 /* quant::dequantize (src/quant.rs:261-281) on the device: raw GGUF blocks

@@ -1,0 +1,218 @@
+"""CUDA path vs the CPU oracle, through the C ABI (libfurnace_cuda.so).
+
+Bars:
+  * dequantized blocks bit-exact;
+  * GEMV outputs within 1e-4 relative error: max|gpu - oracle| <= 1e-4 * max|oracle|;
+  * logits within 1e-3 max-abs, argmax and top-5 identical at every step;
+  * greedy ids identical over 128 decode steps.
+"""
+
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+import furnace_b200 as fz
+from furnace_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+TYPES = {"Q8_0": (8, 32, 34), "Q5_0": (6, 32, 22), "Q4_K": (12, 256, 144), "Q6_K": (14, 256, 210)}
+GEMV_REL = 1e-4
+LOGIT_ABS = 1e-3
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    from tests.conftest import gpu_available
+
+    if not gpu_available():
+        pytest.fail("GPU tests need a CUDA device")
+    fz.load_library()
+
+
+# --------------------------------------------------------------------------
+# dequantization: bit-exact
+# --------------------------------------------------------------------------
+@pytest.mark.parametrize("name", list(TYPES))
+def test_dequant_bitexact_vs_gguf_py_golden(name):
+    g = np.load(os.path.join(GOLD, "dequant_gguf_py.npz"))
+    dt = TYPES[name][0]
+    for key in (name, f"{name}_quantized"):
+        if f"{key}_raw" not in g:
+            continue
+        raw, want = g[f"{key}_raw"], g[f"{key}_f32"]
+        got = fz.quant.dequantize(dt, raw.tobytes(), want.size)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), key
+
+
+@pytest.mark.parametrize("name", list(TYPES))
+def test_dequant_bitexact_vs_oracle_random(orc, name):
+    dt = TYPES[name][0]
+    raw = synth.random_tensor(48, 1024, dt, seed=11)
+    want = orc.dequantize(dt, raw, 48 * 1024)
+    got = fz.quant.dequantize(dt, raw, 48 * 1024)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_dequant_known_answers():
+    kat = json.load(open(os.path.join(GOLD, "reference_kat.json")))
+    for case, dt, bb, n in (("q4_k_hand", 12, 144, 256), ("q6_k_hand", 14, 210, 256), ("q5_0_hand", 6, 22, 32)):
+        b = bytearray(bb)
+        for k, v in kat[case]["bytes"].items():
+            b[int(k)] = v
+        out = fz.quant.dequantize(dt, bytes(b), n)
+        for idx, v in kat[case]["expect"].items():
+            assert out[int(idx)] == v, (case, idx)
+    raw = struct.pack("<e", 0.5) + bytes((i - 16) & 0xFF for i in range(32))
+    assert fz.quant.dequantize(8, raw, 32).tolist() == kat["q8_0_one_block"]["expect"]
+
+
+def test_dequant_rejects_bad_sizes():
+    raw = struct.pack("<e", 1.0) + bytes(32)
+    for data, n in ((raw[:33], 32), (raw, 64), (raw, 31)):
+        with pytest.raises(fz.FurnaceError) as e:
+            fz.quant.dequantize(8, data, n)
+        assert e.value.code == fz.FZ_EINVAL
+
+
+# --------------------------------------------------------------------------
+# GEMV
+# --------------------------------------------------------------------------
+@pytest.mark.parametrize("name", list(TYPES))
+@pytest.mark.parametrize("rows,cols", [(3, 256), (67, 512), (520, 3584), (64, 18944)])
+def test_gemv_vs_oracle(orc, name, rows, cols):
+    dt = TYPES[name][0]
+    raw = synth.random_tensor(rows, cols, dt, seed=rows * 7 + cols)
+    x = np.random.default_rng(rows + cols).normal(0, 1, size=(2, cols)).astype(np.float32)
+    want = orc.matmul_quant(x, raw, rows, cols, dt)
+    got = fz.quant.matmul_quant(x, raw, rows, cols, dt)
+    err = np.abs(got - want).max() / np.abs(want).max()
+    assert err <= GEMV_REL, err
+
+
+def test_fused_q8_matmul_reference_case():
+    """src/quant.rs:331-357 on the device."""
+    raw = b""
+    for o in range(3):
+        for b in range(2):
+            q = bytes(((j * 7 + o * 13 + b * 5) % 255 - 127) & 0xFF for j in range(32))
+            raw += struct.pack("<e", 0.5 + o * 0.25) + q
+    x = np.sin(np.arange(128, dtype=np.float32) * np.float32(0.31)).reshape(2, 64)
+    w = fz.quant.dequantize(8, raw, 192).reshape(3, 64).astype(np.float64)
+    ref = x.astype(np.float64) @ w.T
+    got = fz.quant.matmul_quant(x, raw, 3, 64, 8)
+    assert np.all(np.abs(got - ref) < 1e-4)
+
+
+def test_gemv_rejects_bad_shapes():
+    raw = synth.random_tensor(4, 256, fz.Q4_K, seed=1)
+    with pytest.raises(fz.FurnaceError):
+        fz.quant.matmul_quant(np.zeros((1, 256), np.float32), raw[:-1], 4, 256, fz.Q4_K)
+    with pytest.raises(fz.FurnaceError):
+        fz.quant.matmul_quant(np.zeros((1, 128), np.float32), raw, 4, 128, fz.Q4_K)
+
+
+# --------------------------------------------------------------------------
+# whole model
+# --------------------------------------------------------------------------
+def _paths():
+    return {}
+
+
+@pytest.fixture(scope="module")
+def tiny(tmp_path_factory):
+    return synth.write(synth.spec("tiny"), str(tmp_path_factory.mktemp("m") / "tiny.gguf"))
+
+
+def _models(path):
+    from oracle import oracle
+
+    f = fz.GgufFile.open(path)
+    return f, fz.Model.load(f), oracle.Model(path)
+
+
+def _check_logits(got, want, where=""):
+    err = np.abs(got - want).max()
+    assert err <= LOGIT_ABS, f"{where}: logits max-abs {err}"
+    assert int(np.argmax(got)) == int(np.argmax(want)), where
+    gt, wt = np.argsort(-got, kind="stable")[:5], np.argsort(-want, kind="stable")[:5]
+    assert gt.tolist() == wt.tolist(), f"{where}: top-5 {gt} vs {wt}"
+    return err
+
+
+def test_forward_and_kv_cache_match_oracle(tiny):
+    f, dev, ref = _models(tiny)
+    ids = synth.prompt_ids(ref.vocab, 7, seed=3)
+    kd, kr = fz.KvCache(dev, 64), ref.kv_new(64)
+    got, am = dev.forward(ids, kd)
+    want = ref.forward_cached(ids, kr)
+    _check_logits(got, want, "prefill")
+    assert am == int(np.argmax(want)) and kd.len == 7
+    for layer in range(ref.n_layers):
+        for which in (0, 1):
+            a, b = kd.read(layer, which, 7), kr.read(layer, which, 7)
+            assert np.abs(a - b).max() <= 1e-4 * max(1.0, np.abs(b).max()), (layer, which)
+    # one more token through forward_cached
+    got = dev.forward_cached([int(am)], kd)
+    want = ref.forward_cached([int(am)], kr)
+    _check_logits(got, want, "decode")
+
+
+def test_forward_rejects_bad_input(tiny):
+    f, dev, _ = _models(tiny)
+    kv = fz.KvCache(dev, 8)
+    with pytest.raises(fz.FurnaceError) as e:
+        dev.forward_cached([dev.config.vocab], kv)  # token >= vocab (src/model.rs:489)
+    assert e.value.code == fz.FZ_EINVAL and kv.len == 0
+    with pytest.raises(fz.FurnaceError, match="context overflow"):
+        dev.forward_cached(list(range(9)), kv)  # src/model.rs:581-585
+    dev.forward_cached([1, 2, 3], kv)
+    assert kv.len == 3
+
+
+def _greedy_parity(path, n_prompt, n_new, seed=0, n_layers=None, stop_ids=()):
+    from oracle import oracle
+
+    f = fz.GgufFile.open(path)
+    dev = fz.Model.load(f)
+    ref = oracle.Model(path)
+    ids = synth.prompt_ids(ref.vocab, n_prompt, seed=seed)
+    want_ids, want_lg, _, _ = ref.generate(ids, n_new, stop_ids=stop_ids, keep_logits=True)
+    got_ids, got_lg = fz.generate(dev, ids, n_new, stop_ids=stop_ids, max_ctx=n_prompt + n_new, keep_logits=True)
+    assert got_ids.tolist() == want_ids.tolist()
+    worst = 0.0
+    for s in range(len(want_ids)):
+        worst = max(worst, _check_logits(got_lg[s], want_lg[s], f"step {s}"))
+    return worst
+
+
+def test_greedy_128_steps_tiny(tiny):
+    _greedy_parity(tiny, 9, 128, seed=4)
+
+
+def test_greedy_stop_ids(tiny, orc):
+    ref = orc.Model(tiny)
+    ids = synth.prompt_ids(ref.vocab, 5, seed=6)
+    free, _, _, _ = ref.generate(ids, 12)
+    stop = [int(free[5])]
+    want, _, _, _ = ref.generate(ids, 12, stop_ids=stop)
+    f = fz.GgufFile.open(tiny)
+    dev = fz.Model.load(f)
+    got, _ = fz.generate(dev, ids, 12, stop_ids=stop, max_ctx=32)
+    assert got.tolist() == want.tolist()
+
+
+@pytest.mark.slow
+def test_greedy_128_steps_c1():
+    """Qwen2.5-0.5B shape, Q8_0, 32-token prompt, 128 greedy steps."""
+    _greedy_parity(synth.ensure("c1"), 32, 128)
+
+
+@pytest.mark.slow
+def test_greedy_128_steps_c2():
+    """Qwen2.5-1.5B shape, Q4_K_M mix, 128-token prompt, 128 steps."""
+    _greedy_parity(synth.ensure("c2"), 128, 128)
