@@ -18,7 +18,7 @@ SYNTH = os.path.join(OUT, "libfzsynth.so")
 
 CUDA_SOURCES = ["kernels.cu", "runtime.cu"]
 CXX_SOURCES = ["gguf.cpp"]
-HEADERS = ["fz_internal.h", "kernels.h", os.path.join("..", "..", "include", "furnace.h")]
+HEADERS = sorted(f for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))) + [os.path.join("..", "..", "include", "furnace.h")]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

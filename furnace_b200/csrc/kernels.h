@@ -20,9 +20,11 @@ struct DevMat {
 // Device-layout row stride for `cols` elements of `dtype`.
 uint64_t dev_row_stride(uint32_t dtype, uint32_t cols);
 
-// Repack `rows` GGUF rows (raw, device memory) into the device layout at
-// dst (row stride dev_row_stride).  Same values, different byte order.
-void launch_repack(uint32_t dtype, const uint8_t* raw, uint8_t* dst, uint32_t rows, uint32_t cols, cudaStream_t s);
+// Repack `rows` GGUF rows (raw, device memory) into the chunked device
+// layout (layout.cuh) at dst.  Same bytes, different order.
+// raw holds GGUF rows [r0, r0 + nrows) of a matrix of total_rows rows.
+void launch_repack(uint32_t dtype, const uint8_t* raw, uint8_t* dst, uint32_t r0, uint32_t nrows, uint32_t total_rows,
+                   uint32_t cols, cudaStream_t s);
 
 // Dequantize device-layout rows [r0, r0+rows) of m to f32 [rows, cols],
 // bit-exact with the reference's block decoders.
@@ -59,37 +61,36 @@ struct GemvLaunch {
   int prologue = PRO_COPY;
   int epilogue = EPI_STORE;
   StepState* state = nullptr;       // EPI_LOGITS argmax key
-  int nseq = 1;                     // number of input vectors (x rows), output rows likewise
+  const GemvLaunch* next = nullptr; // the next GEMV of the step (L2 prefetch)
 };
 
 void launch_gemv(const GemvLaunch& g, cudaStream_t s);
 
-// Embedding row of state->token (or tokens[i]) dequantized to f32.
-void launch_embed(const DevMat& emb, const StepState* st, float* x, cudaStream_t s);
+// Embedding row of state->token dequantized to f32.
+void launch_embed(const DevMat& emb, StepState* st, float* x, cudaStream_t s);
 
-// RoPE on q and k (cos/sin table [max_ctx][hd/2] x 2), K/V append at
-// state->pos into a cache laid out [n_kv][max_ctx][hd].
-void launch_rope_append(float* qkv, const float* rope_cs, uint32_t n_heads, uint32_t n_kv, uint32_t hd,
-                        float* kcache, float* vcache, uint32_t max_ctx, const StepState* st, cudaStream_t s);
-
-// Split-K flash-decode over positions [0, state->pos].
+// Split-K attention over positions [0, state->pos] with RoPE on q and the new
+// k, and the K/V append at pos.  Caches are laid out [n_kv][max_ctx][hd];
+// rope_cs is [max_ctx][hd/2] of (cos, sin).
 struct AttnLaunch {
-  const float* q;        // [nh*hd]
-  const float* kcache;   // [nkv][max_ctx][hd]
-  const float* vcache;
+  const float* qkv;      // [q | k | v] after bias
+  const float* rope_cs;
+  float* kcache;
+  float* vcache;
   float* ctx;            // [nh*hd]
-  float* partials;       // [nkv][splits][G][hd+2]
-  unsigned int* counters;  // [nkv], zero between launches
+  float* partials;       // attention_partial_floats(...) floats
   uint32_t n_heads, n_kv, hd, max_ctx, splits;
-  const StepState* state;
+  StepState* state;
 };
 void launch_attention(const AttnLaunch& a, cudaStream_t s);
-uint32_t attention_splits(uint32_t n_kv, uint32_t max_ctx, int num_sms);
+uint32_t attention_splits(uint32_t hd, uint32_t max_ctx);
+uint64_t attention_partial_floats(uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t splits);
 
 // Step bookkeeping after the logits (argmax -> ids_out, next token, pos++).
 void launch_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, bool has_logits, cudaStream_t s);
 
 int num_sms();
 void kernels_init();
+void attention_init();
 
 }  // namespace fz

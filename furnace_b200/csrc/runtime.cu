@@ -81,7 +81,7 @@ struct fz_model {
 struct fz_kv {
   fz_model* m = nullptr;
   uint32_t max_ctx = 0, len = 0, splits = 0;
-  DevBuf k, v, rope_cs, partials, counters, state, forced, ids;
+  DevBuf k, v, rope_cs, partials, state, forced, ids;
   cudaGraphExec_t g_full = nullptr, g_layers = nullptr;
   ~fz_kv() {
     if (g_full) cudaGraphExecDestroy(g_full);
@@ -134,13 +134,12 @@ uint64_t gguf_bytes(uint32_t dtype, uint64_t rows, uint32_t cols) {
 void upload_rows(uint32_t dtype, const uint8_t* raw, uint64_t rows, uint32_t cols, uint8_t* dst, DevBuf& staging,
                  cudaStream_t s) {
   uint64_t row_raw = gguf_bytes(dtype, 1, cols);
-  uint64_t stride = dev_row_stride(dtype, cols);
   uint64_t chunk_rows = staging.n / row_raw;
   need(chunk_rows > 0, "staging buffer too small");
   for (uint64_t r0 = 0; r0 < rows; r0 += chunk_rows) {
     uint64_t nr = std::min(chunk_rows, rows - r0);
     CK(cudaMemcpyAsync(staging.p, raw + r0 * row_raw, nr * row_raw, cudaMemcpyHostToDevice, s));
-    launch_repack(dtype, staging.as<uint8_t>(), dst + r0 * stride, (uint32_t)nr, cols, s);
+    launch_repack(dtype, staging.as<uint8_t>(), dst, (uint32_t)r0, (uint32_t)nr, (uint32_t)rows, cols, s);
     CK(cudaStreamSynchronize(s));
   }
 }
@@ -191,12 +190,11 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
   uint32_t hd = c.head_dim, qd = c.n_heads * hd, kd = c.n_kv_heads * hd;
   float* x = m->x.as<float>();
   float* qkv = m->qkv.as<float>();
-  H(FZ_OP_EMBED, true);
-  launch_embed(m->embd, st, x, s);
-  H(FZ_OP_EMBED, false);
+  // every GEMV of the step, in order, so each can prefetch the next one's weights
+  std::vector<GemvLaunch> gl(4 * c.n_layers + 1);
   for (uint32_t li = 0; li < c.n_layers; li++) {
     Layer& L = m->layers[li];
-    GemvLaunch g;
+    GemvLaunch& g = gl[4 * li];
     g.nseg = 3;
     g.seg[0] = GemvSeg{L.wq, L.bqkv, qkv};
     g.seg[1] = GemvSeg{L.wk, L.bqkv + qd, qkv + qd};
@@ -206,57 +204,62 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
     g.eps = c.rms_eps;
     g.prologue = PRO_RMSNORM;
     g.epilogue = EPI_STORE;
-    H(FZ_OP_QKV, true);
-    launch_gemv(g, s);
-    H(FZ_OP_QKV, false);
-    float* kc = kv->k.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
-    float* vc = kv->v.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
-    H(FZ_OP_ROPE, true);
-    launch_rope_append(qkv, kv->rope_cs.as<float>(), c.n_heads, c.n_kv_heads, hd, kc, vc, kv->max_ctx, st, s);
-    H(FZ_OP_ROPE, false);
-    AttnLaunch a{qkv, kc, vc, m->ctx.as<float>(), kv->partials.as<float>(), kv->counters.as<unsigned int>(),
-                 c.n_heads, c.n_kv_heads, hd, kv->max_ctx, kv->splits, st};
-    H(FZ_OP_ATTN, true);
-    launch_attention(a, s);
-    H(FZ_OP_ATTN, false);
-    GemvLaunch go;
+    GemvLaunch& go = gl[4 * li + 1];
     go.seg[0] = GemvSeg{L.wo, nullptr, x};
     go.x = m->ctx.as<float>();
     go.prologue = PRO_COPY;
     go.epilogue = EPI_RESID;
-    H(FZ_OP_OPROJ, true);
-    launch_gemv(go, s);
-    H(FZ_OP_OPROJ, false);
-    GemvLaunch gu;
+    GemvLaunch& gu = gl[4 * li + 2];
     gu.seg[0] = GemvSeg{L.wgu, nullptr, m->h.as<float>()};
     gu.x = x;
     gu.norm_w = L.ffn_norm;
     gu.eps = c.rms_eps;
     gu.prologue = PRO_RMSNORM;
     gu.epilogue = EPI_SWIGLU;
-    H(FZ_OP_GATEUP, true);
-    launch_gemv(gu, s);
-    H(FZ_OP_GATEUP, false);
-    GemvLaunch gd;
+    GemvLaunch& gd = gl[4 * li + 3];
     gd.seg[0] = GemvSeg{L.wd, nullptr, x};
     gd.x = m->h.as<float>();
     gd.prologue = PRO_COPY;
     gd.epilogue = EPI_RESID;
+  }
+  GemvLaunch& lm = gl[4 * c.n_layers];
+  lm.seg[0] = GemvSeg{m->lm_head, nullptr, m->logits.as<float>()};
+  lm.x = x;
+  lm.norm_w = m->out_norm;
+  lm.eps = c.rms_eps;
+  lm.prologue = PRO_RMSNORM;
+  lm.epilogue = EPI_LOGITS;
+  lm.state = st;
+  size_t last = with_logits ? gl.size() - 1 : gl.size() - 2;
+  for (size_t i = 0; i <= last; i++) gl[i].next = i < last ? &gl[i + 1] : &gl[0];
+
+  H(FZ_OP_EMBED, true);
+  launch_embed(m->embd, st, x, s);
+  H(FZ_OP_EMBED, false);
+  for (uint32_t li = 0; li < c.n_layers; li++) {
+    H(FZ_OP_QKV, true);
+    launch_gemv(gl[4 * li], s);
+    H(FZ_OP_QKV, false);
+    float* kc = kv->k.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
+    float* vc = kv->v.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
+    AttnLaunch a{qkv, kv->rope_cs.as<float>(), kc, vc, m->ctx.as<float>(), kv->partials.as<float>(),
+                 c.n_heads, c.n_kv_heads, hd, kv->max_ctx, kv->splits, st};
+    H(FZ_OP_ATTN, true);
+    launch_attention(a, s);
+    H(FZ_OP_ATTN, false);
+    H(FZ_OP_OPROJ, true);
+    launch_gemv(gl[4 * li + 1], s);
+    H(FZ_OP_OPROJ, false);
+    H(FZ_OP_GATEUP, true);
+    launch_gemv(gl[4 * li + 2], s);
+    H(FZ_OP_GATEUP, false);
     H(FZ_OP_DOWN, true);
-    launch_gemv(gd, s);
+    launch_gemv(gl[4 * li + 3], s);
     H(FZ_OP_DOWN, false);
   }
   if (with_logits) {
-    GemvLaunch gl;
-    gl.seg[0] = GemvSeg{m->lm_head, nullptr, m->logits.as<float>()};
-    gl.x = x;
-    gl.norm_w = m->out_norm;
-    gl.eps = c.rms_eps;
-    gl.prologue = PRO_RMSNORM;
-    gl.epilogue = EPI_LOGITS;
-    gl.state = st;
     H(FZ_OP_LMHEAD, true);
-    launch_gemv(gl, s);
+    launch_gemv(lm, s);
     H(FZ_OP_LMHEAD, false);
   }
   H(FZ_OP_FINALIZE, true);
@@ -421,6 +424,7 @@ int fz_model_load(const fz_file* f, int tp, const int* device_ids, fz_model** ou
     need(c.hidden % 32 == 0 && c.ffn % 32 == 0, "hidden/ffn must be multiples of 32");
     CK(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
     kernels_init();
+    attention_init();
     uint32_t H = c.hidden, F = c.ffn, qd = c.n_heads * c.head_dim, kd = c.n_kv_heads * c.head_dim;
 
     // tensor table and device sizes
@@ -464,36 +468,39 @@ int fz_model_load(const fz_file* f, int tp, const int* device_ids, fz_model** ou
       L.wgu.stride = dev_row_stride(L.wgu.dtype, H);
       L.wgu.gguf_bytes = 2 * gguf_bytes(L.wgu.dtype, F, H);
     }
-    // one pool for every matrix, 256-byte aligned
+    // one pool for every matrix, 256-byte aligned, in the order a decode step
+    // streams them (L2 prefetch runs from one matrix into the next)
     uint64_t total = 0;
     auto reserve = [&](DevMat& d) {
       uint64_t off = total;
       total = (total + (uint64_t)d.rows * d.stride + 255) & ~uint64_t(255);
       return off;
     };
-    std::vector<uint64_t> offs;
-    for (auto& pm : mats) offs.push_back(reserve(*pm.second));
-    std::vector<uint64_t> gu_off(c.n_layers);
-    for (uint32_t i = 0; i < c.n_layers; i++) gu_off[i] = reserve(m->layers[i].wgu);
+    std::vector<std::pair<DevMat*, uint64_t>> order;
+    order.push_back({&m->embd, reserve(m->embd)});
+    for (uint32_t i = 0; i < c.n_layers; i++) {
+      Layer& L = m->layers[i];
+      for (DevMat* d : {&L.wq, &L.wk, &L.wv, &L.wo, &L.wgu, &L.wd}) order.push_back({d, reserve(*d)});
+    }
+    if (!tied) order.push_back({&m->lm_head, reserve(m->lm_head)});
     m->weights.alloc(total);
     CK(cudaMemset(m->weights.p, 0, total));
     uint8_t* base = m->weights.as<uint8_t>();
+    for (auto& o : order) o.first->ptr = base + o.second;
     uint64_t max_raw = 0;
     for (auto& pm : mats) max_raw = std::max<uint64_t>(max_raw, pm.second->gguf_bytes);
-    DevBuf staging(std::min<uint64_t>(max_raw, 256ull << 20));
+    DevBuf staging(std::min<uint64_t>(max_raw + 16, 256ull << 20));
     for (size_t k = 0; k < mats.size(); k++) {
       DevMat& d = *mats[k].second;
-      d.ptr = base + offs[k];
       uint64_t nb;
       const uint8_t* raw = g.tensor_data(*mats[k].first, &nb);
       upload_rows(d.dtype, raw, d.rows, d.cols, d.ptr, staging, m->stream);
     }
     // gate/up interleaved by row: row 2i = gate_i, row 2i+1 = up_i
     {
-      DevBuf tmp(2 * gguf_bytes(gates[0]->dtype, 1, H) * 1024 + 16);
+      DevBuf tmp(2 * gguf_bytes(gates[0]->dtype, 1, H) * 512 + 16);
       for (uint32_t i = 0; i < c.n_layers; i++) {
         DevMat& d = m->layers[i].wgu;
-        d.ptr = base + gu_off[i];
         uint64_t nb;
         const uint8_t* graw = g.tensor_data(*gates[i], &nb);
         const uint8_t* uraw = g.tensor_data(*ups[i], &nb);
@@ -507,7 +514,7 @@ int fz_model_load(const fz_file* f, int tp, const int* device_ids, fz_model** ou
             memcpy(&hbuf[(2 * r + 1) * rb], uraw + (uint64_t)(r0 + r) * rb, rb);
           }
           CK(cudaMemcpyAsync(tmp.p, hbuf.data(), 2 * nr * rb, cudaMemcpyHostToDevice, m->stream));
-          launch_repack(d.dtype, tmp.as<uint8_t>(), d.ptr + (uint64_t)2 * r0 * d.stride, 2 * nr, H, m->stream);
+          launch_repack(d.dtype, tmp.as<uint8_t>(), d.ptr, 2 * r0, 2 * nr, d.rows, H, m->stream);
           CK(cudaStreamSynchronize(m->stream));
         }
       }
@@ -617,11 +624,10 @@ int fz_kv_new(fz_model* m, uint32_t max_ctx, int kv_dtype, fz_kv** out) {
     }
     kv->rope_cs.alloc(cs.size() * 4);
     CK(cudaMemcpy(kv->rope_cs.p, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
-    kv->splits = attention_splits(c.n_kv_heads, max_ctx, num_sms());
+    kv->splits = attention_splits(c.head_dim, max_ctx);
     uint32_t G = c.n_heads / c.n_kv_heads;
-    kv->partials.alloc((uint64_t)c.n_kv_heads * kv->splits * G * (c.head_dim + 2) * 4);
-    kv->counters.alloc(c.n_kv_heads * 4 + 16);
-    CK(cudaMemset(kv->counters.p, 0, c.n_kv_heads * 4 + 16));
+    (void)G;
+    kv->partials.alloc(attention_partial_floats(c.n_heads, c.n_kv_heads, c.head_dim, kv->splits) * 4);
     kv->state.alloc(sizeof(StepState));
     CK(cudaMemset(kv->state.p, 0, sizeof(StepState)));
     kv->forced.alloc((uint64_t)max_ctx * 4 + 16);
@@ -868,16 +874,23 @@ int fz_dequant(uint32_t dtype, const void* raw, size_t nbytes, size_t n, float* 
     need(is_quant(dtype), "dequantization for type %u is not implemented", dtype);
     need(n % be == 0, "element count %zu is not a multiple of %u", n, be);
     need(nbytes == n / be * bb, "data is %zu bytes, expected %zu (%zu blocks of %u)", nbytes, n / be * bb, n / be, bb);
-    // one device row of `be` elements per block keeps any block count legal
+    // view the blob as rows of k blocks, k the largest divisor of the block
+    // count that keeps a row within one chunk of the device layout
+    uint64_t nblk = n / be, kmax = be == 256 ? 8 : 64, k = 1;
+    for (uint64_t t = kmax; t >= 1; t--)
+      if (nblk % t == 0) {
+        k = t;
+        break;
+      }
     DevMat m;
     m.dtype = dtype;
-    m.rows = (uint32_t)(n / be);
-    m.cols = be;
-    m.stride = dev_row_stride(dtype, be);
+    m.rows = (uint32_t)(nblk / k);
+    m.cols = (uint32_t)(k * be);
+    m.stride = dev_row_stride(dtype, m.cols);
     DevBuf raw_d(nbytes + 16), lay((uint64_t)m.rows * m.stride + 256), outd(n * 4 + 16);
     CK(cudaMemset(lay.p, 0, lay.n));
     CK(cudaMemcpy(raw_d.p, raw, nbytes, cudaMemcpyHostToDevice));
-    launch_repack(dtype, raw_d.as<uint8_t>(), lay.as<uint8_t>(), m.rows, m.cols, 0);
+    launch_repack(dtype, raw_d.as<uint8_t>(), lay.as<uint8_t>(), 0, m.rows, m.rows, m.cols, 0);
     m.ptr = lay.as<uint8_t>();
     launch_dequant(m, 0, m.rows, outd.as<float>(), 0);
     CK(cudaMemcpy(out, outd.p, n * 4, cudaMemcpyDeviceToHost));
