@@ -133,20 +133,27 @@ __global__ void k_repack(uint32_t dt, const uint8_t* __restrict__ raw, uint8_t* 
     uint32_t j = u & 3;  // each of the 4 units copies 36 bytes of its super-block
     for (int i = 0; i < 36; i++) b[36 * j + i] = src[36 * j + i];
   } else if (dt == FZ_Q6_K) {
+    // one thread per 64-element unit k of a super-block: regroup its quants
+    // (src/quant.rs:114-133 gives element e = 128h + 32g + l its bits)
     const uint8_t* src = raw + r * (cols / 256) * 210 + (uint64_t)(u >> 2) * 210;
     uint8_t* body = ch + 208 * (lu >> 2);
-    uint32_t uu = u & 3, h = uu >> 1, is = uu & 1, l0 = 16 * is;
-    for (int i = 0; i < 16; i++) {
-      body[48 * uu + i] = src[64 * h + l0 + i];             // ql run a (groups 0, 2)
-      body[48 * uu + 16 + i] = src[64 * h + 32 + l0 + i];   // ql run b (groups 1, 3)
-      body[48 * uu + 32 + i] = src[128 + 32 * h + l0 + i];  // qh run
+    const uint32_t k = u & 3;
+    auto q6 = [&](uint32_t e) -> uint32_t {
+      uint32_t h = e >> 7, g = (e & 127) >> 5, l = e & 31;
+      uint32_t b = src[64 * h + l + 32 * (g & 1)];
+      uint32_t lo = g < 2 ? (b & 0x0F) : (b >> 4);
+      return lo | (((src[128 + 32 * h + l] >> (2 * g)) & 3) << 4);
+    };
+    for (uint32_t i = 0; i < 32; i++)
+      body[32 * k + i] = (uint8_t)((q6(64 * k + i) & 15) | ((q6(64 * k + 32 + i) & 15) << 4));
+    for (uint32_t i = 0; i < 16; i++)
+      body[128 + 16 * k + i] = (uint8_t)((q6(64 * k + i) >> 4) | ((q6(64 * k + 16 + i) >> 4) << 2) |
+                                         ((q6(64 * k + 32 + i) >> 4) << 4) | ((q6(64 * k + 48 + i) >> 4) << 6));
+    for (uint32_t t = 0; t < 4; t++) {
+      uint32_t e = 64 * k + 16 * t, h = e >> 7, g = (e & 127) >> 5, l = e & 31;
+      body[192 + 4 * k + t] = src[192 + 8 * h + l / 16 + 2 * g];
     }
-    const uint8_t* sc = src + 192;
-    body[192 + 4 * uu + 0] = sc[8 * h + is];      // group 0
-    body[192 + 4 * uu + 1] = sc[8 * h + is + 4];  // group 2
-    body[192 + 4 * uu + 2] = sc[8 * h + is + 2];  // group 1
-    body[192 + 4 * uu + 3] = sc[8 * h + is + 6];  // group 3
-    if (uu == 0) {
+    if (k == 0) {
       uint8_t* d = ch + 208 * (nu >> 2) + 2 * (lu >> 2);
       d[0] = src[208];
       d[1] = src[209];
@@ -218,22 +225,17 @@ __device__ void dequant_unit(uint32_t dt, const uint8_t* base, uint32_t rows, ui
       oa[32 + l] = __fsub_rn(__fmul_rn(d2, (float)(q[l] >> 4)), min2);
     }
   } else if (dt == FZ_Q6_K) {
-    uint32_t sb = u >> 2, uu = u & 3, h = uu >> 1, l0 = (uu & 1) << 4;
+    const uint32_t k = u & 3;
     const uint8_t* body = ch + 208 * (lu >> 2);
     const uint8_t* dp = ch + 208 * (nu >> 2) + 2 * (lu >> 2);
     float d = h2f(dp[0] | (dp[1] << 8));
-    const uint8_t* qh = body + 48 * uu + 32;
-    const int scpos[4] = {0, 2, 1, 3};
-    for (int g = 0; g < 4; g++) {
-      const uint8_t* ql = body + 48 * uu + 16 * (g & 1);
-      float sc = (float)(int8_t)body[192 + 4 * uu + scpos[g]];
-      float ds = __fmul_rn(d, sc);
-      int sh = g >= 2 ? 4 : 0;
-      float* og = o + 256 * sb + 128 * h + 32 * g + l0;
-      for (int i = 0; i < 16; i++) {
-        int q = (int)(((ql[i] >> sh) & 0x0F) | (((qh[i] >> (2 * g)) & 3) << 4)) - 32;
-        og[i] = __fmul_rn(ds, (float)q);
-      }
+    float* ou = o + 64 * u;
+    for (uint32_t i = 0; i < 64; i++) {
+      uint32_t nib = (body[32 * k + (i & 31)] >> (i < 32 ? 0 : 4)) & 15;
+      uint32_t hb = (body[128 + 16 * k + (i & 15)] >> (2 * (i >> 4))) & 3;
+      int q = (int)(nib | (hb << 4)) - 32;
+      float sc = (float)(int8_t)body[192 + 4 * k + (i >> 4)];
+      ou[i] = __fmul_rn(__fmul_rn(d, sc), (float)q);  // (d * sc) * q, src/quant.rs:127-130
     }
   } else {
     uint32_t nb = cols / 32;
@@ -297,36 +299,127 @@ static void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   CK(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...));
 }
 
-// Embedding lookup of state->token (src/model.rs:482-506): one dequantized row.
-__global__ void k_embed(uint32_t dt, const uint8_t* __restrict__ base, uint32_t cols, uint32_t vocab,
-                        StepState* __restrict__ st, float* __restrict__ x) {
-  pdl_trigger();
-  pdl_wait();
-  uint32_t tok = st->token;
-  uint32_t u = blockIdx.x * blockDim.x + threadIdx.x;
-  if (u >= (cols + 63) / 64) return;
-  if (tok >= vocab) {
-    // the host validates ids before they reach the device; this is a guard
-    for (uint32_t i = 64 * u; i < 64 * u + 64 && i < cols; i++) x[i] = 0.f;
-    st->error = 1;
-    return;
-  }
-  dequant_unit(dt, base, vocab, tok, cols, u, x);
+// ---------------------------------------------------------------------------
+// Activation runs.  A GEMV input vector is handed between kernels as one
+// 64-byte record per 16 elements: the elements as 24-bit fixed point with a
+// shared power-of-two scale, split into three signed 8-bit limbs (a, b, c:
+// X = a*2^16 + b*2^8 + c, x = X * scale), plus the run's f32 sum.  The
+// kernel that produces a vector writes its records in its epilogue, so a
+// consuming GEMV never converts activations; RMSNorm inputs are recorded as
+// x (.) w_norm and the 1/rms factor is applied to each dot product at the end
+// (from per-CTA sum-of-squares partials).
+// ---------------------------------------------------------------------------
+struct XRun {  // one 16-element activation run in limb form (== a run record)
+  uint4 a, b, c;
+  float scale, sum;
+  uint32_t pad[2];
+};
+static_assert(sizeof(XRun) == 64, "run record");
+
+// Records are stored unit by unit (4 runs = 64 elements = 256 bytes, the
+// span one weight unit multiplies).  Inside a unit the sixteen 16-byte pieces
+// -- run j's limbs a, b, c and then (scale, sum) -- sit at piece index
+// (4j + f) ^ (unit & 7): the 8 lanes of a quarter warp, which read the same
+// piece of 8 consecutive units, then hit 8 different groups of 4 banks.
+__host__ __device__ __forceinline__ uint32_t run_piece_off(uint32_t run, uint32_t f) {
+  const uint32_t u = run >> 2;
+  return 256 * u + 16 * ((4 * (run & 3) + f) ^ (u & 7));
 }
 
-void launch_embed(const DevMat& emb, StepState* st, float* x, cudaStream_t s) {
-  uint32_t units = (emb.cols + 63) / 64;
-  launch_pdl(k_embed, dim3((units + 63) / 64), dim3(64), 0, s, emb.dtype, (const uint8_t*)emb.ptr, emb.cols,
-             emb.rows, st, x);
+// Four consecutive lanes (a quad) convert one run, 4 elements each; every lane
+// of the warp must call this (shuffles).  The record goes to run `run` of the
+// record array at `base`; `base` = null for an idle quad.
+__device__ __forceinline__ void quad_to_run(const float* v, uint32_t q, XRun* base, uint32_t run) {
+  float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+  float sm = (v[0] + v[1]) + (v[2] + v[3]);
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+  sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+  if (!base) return;
+  int e = 0;
+  if (m > 0.f) frexpf(m, &e);
+  uint32_t wa = 0, wb = 0, wc = 0;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    int X = __float2int_rn(ldexpf(v[i], 22 - e));
+    int c = ((X + 128) & 255) - 128;
+    int X1 = (X - c) >> 8;
+    int b = ((X1 + 128) & 255) - 128;
+    int a = (X1 - b) >> 8;
+    wa |= (uint32_t)(a & 255) << (8 * i);
+    wb |= (uint32_t)(b & 255) << (8 * i);
+    wc |= (uint32_t)(c & 255) << (8 * i);
+  }
+  uint8_t* b8 = reinterpret_cast<uint8_t*>(base);
+  reinterpret_cast<uint32_t*>(b8 + run_piece_off(run, 0))[q] = wa;
+  reinterpret_cast<uint32_t*>(b8 + run_piece_off(run, 1))[q] = wb;
+  reinterpret_cast<uint32_t*>(b8 + run_piece_off(run, 2))[q] = wc;
+  if (q == 0) *reinterpret_cast<float2*>(b8 + run_piece_off(run, 3)) = make_float2(ldexpf(1.0f, e - 22), sm);
 }
+
+// Run j (< 4) of unit u from a unit-swizzled record array.
+__device__ __forceinline__ XRun load_run(const XRun* base, uint32_t u, uint32_t j) {
+  const uint8_t* b8 = reinterpret_cast<const uint8_t*>(base) + 256 * u;
+  const uint32_t s = u & 7;
+  XRun r;
+  r.a = *reinterpret_cast<const uint4*>(b8 + 16 * ((4 * j) ^ s));
+  r.b = *reinterpret_cast<const uint4*>(b8 + 16 * ((4 * j + 1) ^ s));
+  r.c = *reinterpret_cast<const uint4*>(b8 + 16 * ((4 * j + 2) ^ s));
+  const float2 ss = *reinterpret_cast<const float2*>(b8 + 16 * ((4 * j + 3) ^ s));
+  r.scale = ss.x;
+  r.sum = ss.y;
+  return r;
+}
+
+// Records for n values (n % 16 == 0) held in shared memory, optionally scaled
+// elementwise by w (global), written to runs run0 .. run0 + n/16 of the record
+// array `out`.  Called by `nthreads` threads (whole warps) with thread index t.
+__device__ void values_to_runs(const float* vals, uint32_t n, const float* w, XRun* out, uint32_t run0, uint32_t t,
+                               uint32_t nthreads) {
+  const uint32_t n4 = n / 4, iters = (n4 + nthreads - 1) / nthreads;
+  for (uint32_t it = 0; it < iters; it++) {
+    uint32_t i4 = t + it * nthreads;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    bool act = i4 < n4;
+    if (act) {
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        v[i] = vals[4 * i4 + i];
+        if (w) v[i] = __fmul_rn(v[i], w[4 * i4 + i]);
+      }
+    }
+    quad_to_run(v, i4 & 3, act ? out : nullptr, run0 + (i4 >> 2));
+  }
+}
+
+// f32 vector -> run records (fz_matmul_quant_dev and tests).  One warp per 8 runs.
+__global__ void k_to_runs(const float* __restrict__ x, uint32_t cols, XRun* __restrict__ out, uint32_t nruns) {
+  uint32_t i4 = blockIdx.x * blockDim.x + threadIdx.x;
+  float v[4] = {0.f, 0.f, 0.f, 0.f};
+  bool act = i4 < 4 * nruns;
+  if (act)
+    for (int i = 0; i < 4; i++) v[i] = 4 * i4 + i < cols ? x[4 * i4 + i] : 0.f;
+  quad_to_run(v, i4 & 3, act ? out : nullptr, i4 >> 2);
+}
+
+void launch_to_runs(const float* x, uint32_t cols, void* runs, uint32_t nruns, cudaStream_t s) {
+  uint32_t n4 = 4 * nruns;
+  k_to_runs<<<(n4 + 255) / 256, 256, 0, s>>>(x, cols, reinterpret_cast<XRun*>(runs), nruns);
+  CK(cudaGetLastError());
+}
+
+__host__ __device__ __forceinline__ uint32_t runs_for_dev(uint32_t cols) { return 4 * ((cols + 63) / 64); }
+uint32_t runs_for(uint32_t cols) { return runs_for_dev(cols); }
 
 // ---------------------------------------------------------------------------
 // GEMV
 // ---------------------------------------------------------------------------
-constexpr int GV_CWARPS = 15;                      // consumer warps (16 warps/CTA incl. producer)
+constexpr int GV_CWARPS = 15;                      // consumer warps (16 warps per block with the producer)
 constexpr int GV_RPW = 2;                          // rows per consumer warp per stage
 constexpr int GV_ROWS = GV_CWARPS * GV_RPW;        // rows per stage
 constexpr int GV_THREADS = (GV_CWARPS + 1) * 32;   // + one producer warp
+constexpr int GV_NT = GV_CWARPS * 32;              // consumer threads
 constexpr int GV_MAX_SLOTS = 8;
 constexpr int GV_MAX_CH = 32;                      // chunks per row (cols <= 65536)
 
@@ -335,7 +428,7 @@ struct GvSeg {
   uint32_t rows, dtype, cols;
   const float* bias;
   float* out;
-  uint32_t cta_begin, cta_end;
+  uint32_t cta_begin, cta_end, align;
 };
 
 struct GvNext {
@@ -348,26 +441,23 @@ struct GvParams {
   GvSeg seg[3];
   int nseg;
   uint32_t cols;
-  const float* x;
-  const float* norm_w;
+  const XRun* in_runs;   // activation as run records (one bulk copy), or
+  const float* x;        // activation as f32, converted in the prologue
+  const float* norm_w;   //   optionally RMS-normalised (src/tensor.rs:164-186)
   float eps;
-  int prologue, epilogue;
+  int epilogue;
   StepState* state;
-  uint32_t slots, slot_bytes, max_rows;
-  uint32_t pf_ahead;
+  XRun* out_runs;        // SWIGLU: records of the next GEMV's input
+  uint32_t slots, slot_bytes, max_rows, pf_ahead;
   GvNext next;
 };
 
-// This CTA's row range within its segment (even boundaries for gate/up pairs).
+// This CTA's row range within its segment: whole multiples of seg.align rows
+// (pairs for gate/up, 16-row runs where the epilogue writes run records).
 __device__ __forceinline__ void cta_rows(const GvSeg& s, uint32_t b, uint32_t* r0, uint32_t* r1) {
-  uint32_t n = s.cta_end - s.cta_begin, lb = b - s.cta_begin, half = s.rows / 2;
-  if (s.rows & 1) {
-    *r0 = (uint32_t)((uint64_t)s.rows * lb / n);
-    *r1 = (uint32_t)((uint64_t)s.rows * (lb + 1) / n);
-  } else {
-    *r0 = 2 * (uint32_t)((uint64_t)half * lb / n);
-    *r1 = 2 * (uint32_t)((uint64_t)half * (lb + 1) / n);
-  }
+  uint32_t n = s.cta_end - s.cta_begin, lb = b - s.cta_begin, units = s.rows / s.align;
+  *r0 = s.align * (uint32_t)((uint64_t)units * lb / n);
+  *r1 = lb + 1 == n ? s.rows : s.align * (uint32_t)((uint64_t)units * (lb + 1) / n);
 }
 
 __device__ __forceinline__ int seg_of(const GvSeg* seg, int nseg, uint32_t b) {
@@ -394,6 +484,7 @@ struct StageIter {
     s = &seg[si];
     if (b < s->cta_begin || b >= s->cta_end) return;
     cta_rows(*s, b, &r0, &r1);
+    if (r1 <= r0) return;
     cols = s->cols;
     dt = s->dtype;
     nch = lay_nch(cols);
@@ -428,12 +519,6 @@ __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
   asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
   return d;
 }
-
-struct XRun {  // one 16-element activation run in limb form
-  uint4 a, b, c;
-  float scale, sum;
-};
-
 // sum_i q_i * X_i for 16 unsigned quants of <= 5 bits as one f32, the limbs
 // combined in integer arithmetic (|total| < 2^31 for |limb a| <= 65).
 __device__ __forceinline__ float dot_u_int(const uint32_t* q, const XRun& x) {
@@ -514,26 +599,26 @@ __device__ __forceinline__ float unit_dot(const uint8_t* tp, uint32_t lu, uint32
            dmin * ((float)ma * (x[0].sum + x[1].sum) + (float)mb * (x[2].sum + x[3].sum));
   } else if (DT == FZ_Q6_K) {
     const uint8_t* body = tp + 208 * (lu >> 2);
-    uint32_t uu = lu & 3;
-    uint4 qa = lds128(body + 48 * uu), qb = lds128(body + 48 * uu + 16), qh = lds128(body + 48 * uu + 32);
-    uint32_t sc4 = lds32(body + 192 + 4 * uu);
+    const uint32_t k = lu & 3;
+    uint4 n0 = lds128(body + 32 * k), n1 = lds128(body + 32 * k + 16), qh = lds128(body + 128 + 16 * k);
+    uint32_t sc4 = lds32(body + 192 + 4 * k);
     float d = h2f(lds16(tp + 208 * (nu >> 2) + 2 * (lu >> 2)));
-    const uint32_t qav[4] = {qa.x, qa.y, qa.z, qa.w}, qbv[4] = {qb.x, qb.y, qb.z, qb.w};
-    const uint32_t qhv[4] = {qh.x, qh.y, qh.z, qh.w};
+    const uint32_t a0[4] = {n0.x, n0.y, n0.z, n0.w}, a1[4] = {n1.x, n1.y, n1.z, n1.w};
+    const uint32_t hv[4] = {qh.x, qh.y, qh.z, qh.w};
     uint32_t g0[4], g1[4], g2[4], g3[4];
 #pragma unroll
-    for (int k = 0; k < 4; k++) {
-      g0[k] = (qav[k] & M4) | ((qhv[k] << 4) & M30);
-      g1[k] = (qbv[k] & M4) | ((qhv[k] << 2) & M30);
-      g2[k] = ((qav[k] >> 4) & M4) | (qhv[k] & M30);
-      g3[k] = ((qbv[k] >> 4) & M4) | ((qhv[k] >> 2) & M30);
+    for (int w = 0; w < 4; w++) {
+      g0[w] = (a0[w] & M4) | ((hv[w] << 4) & M30);
+      g1[w] = (a1[w] & M4) | ((hv[w] << 2) & M30);
+      g2[w] = ((a0[w] >> 4) & M4) | (hv[w] & M30);
+      g3[w] = ((a1[w] >> 4) & M4) | ((hv[w] >> 2) & M30);
     }
     float s0 = fmaf(dot_f<false>(g0, x[0]), x[0].scale, -32.0f * x[0].sum);
     float s1 = fmaf(dot_f<false>(g1, x[1]), x[1].scale, -32.0f * x[1].sum);
     float s2 = fmaf(dot_f<false>(g2, x[2]), x[2].scale, -32.0f * x[2].sum);
     float s3 = fmaf(dot_f<false>(g3, x[3]), x[3].scale, -32.0f * x[3].sum);
-    float c0 = (float)(int8_t)(sc4 & 0xff), c2 = (float)(int8_t)((sc4 >> 8) & 0xff);
-    float c1 = (float)(int8_t)((sc4 >> 16) & 0xff), c3 = (float)(int8_t)(sc4 >> 24);
+    float c0 = (float)(int8_t)(sc4 & 0xff), c1 = (float)(int8_t)((sc4 >> 8) & 0xff);
+    float c2 = (float)(int8_t)((sc4 >> 16) & 0xff), c3 = (float)(int8_t)(sc4 >> 24);
     return d * (c0 * s0 + c1 * s1 + c2 * s2 + c3 * s3);
   } else if (DT == FZ_Q8_0) {
     const uint8_t* q = tp + 64 * lu;
@@ -577,30 +662,22 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
 }
 
 // Consumer side of one CTA: all stages of the CTA's rows for format DT.
-// Warp w takes rows ra + w + GV_CWARPS*j (j < GV_RPW) of every stage.
+// Warp w takes rows ra + w + GV_CWARPS*j (j < GV_RPW) of every stage; the
+// activation records of the whole input sit in shared memory (rec).
 template <uint32_t DT>
 __device__ bool gv_consume(const GvParams& p, const StageIter& it, const ChunkInfo* chunks, uint8_t* ring,
-                           uint64_t* full, uint64_t* empty, const uint8_t* limbs, const float* xsc, const float* xsum,
-                           float* acc) {
+                           uint64_t* full, uint64_t* empty, const XRun* rec, float* acc) {
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  uint32_t i = 0, slot = 0, phase = 0;
+  uint32_t slot = 0, phase = 0;
   for (uint32_t c = 0; c < it.nch; c++) {
     const uint32_t nu = chunks[c].nu, tb = chunks[c].tb;
     XRun xr[4];
     if (lane < nu) {
-      uint32_t u = chunks[c].cu0 + lane;
+      const uint32_t u = chunks[c].cu0 + lane;
 #pragma unroll
-      for (uint32_t j = 0; j < 4; j++) {
-        uint32_t xc = x_chunk_of(DT, u, j);
-        const uint8_t* lp = limbs + 48 * xc;
-        xr[j].a = lds128(lp);
-        xr[j].b = lds128(lp + 16);
-        xr[j].c = lds128(lp + 32);
-        xr[j].scale = xsc[xc];
-        xr[j].sum = xsum[xc];
-      }
+      for (uint32_t j = 0; j < 4; j++) xr[j] = load_run(rec, u, j);
     }
-    for (uint32_t ra = it.r0; ra < it.r1; ra += GV_ROWS, i++) {
+    for (uint32_t ra = it.r0; ra < it.r1; ra += GV_ROWS) {
       if (!mbar_wait(&full[slot], phase)) return false;
       const uint8_t* tile = ring + (size_t)slot * p.slot_bytes;
       float v[GV_RPW];
@@ -634,17 +711,14 @@ __device__ bool gv_consume(const GvParams& p, const StageIter& it, const ChunkIn
 __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ GvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t U = (p.cols + 63) / 64, NX = 4 * U;
+  const uint32_t NX = runs_for_dev(p.cols);
   uint8_t* ring = smem;
-  uint8_t* limbs = ring + (size_t)p.slots * p.slot_bytes;
-  float* xsc = reinterpret_cast<float*>(limbs + 48 * NX);
-  float* xsum = xsc + NX;
-  float* acc = xsum + NX;
-  uint64_t* full = reinterpret_cast<uint64_t*>(((uintptr_t)(acc + p.max_rows) + 15) & ~uintptr_t(15));
-  uint64_t* empty = full + GV_MAX_SLOTS;
+  XRun* rec = reinterpret_cast<XRun*>(ring + (size_t)p.slots * p.slot_bytes);
+  float* acc = reinterpret_cast<float*>(rec + NX);
   __shared__ float red[GV_CWARPS];
   __shared__ unsigned long long kred[GV_CWARPS];
   __shared__ ChunkInfo chunks[GV_MAX_CH];
+  __shared__ __align__(8) uint64_t full[GV_MAX_SLOTS], empty[GV_MAX_SLOTS], recbar;
 
   StageIter it;
   it.init(p.seg, p.nseg, blockIdx.x);
@@ -654,20 +728,21 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], GV_CWARPS);
     }
+    mbar_init(&recbar, 1);
     fence_barrier_init();
   }
   __syncthreads();
   if (tid == 0) pdl_trigger();
 
   if (warp == GV_CWARPS) {
-    // ---------------- producer ----------------
+    // ---------------- producer (weights only: no wait on the predecessor) ----
     if (lane != 0) return;
     const uint64_t pol = policy_evict_first();
     StageIter nx;
     nx.init(p.next.seg, p.next.nseg, blockIdx.x);
     // L2 prefetch cursors: own stages, then the next kernel's first stages
-    uint32_t pc = 0, pr = it.r0;                       // own (chunk, row)
-    const uint32_t nx_nch = nx.n_stages ? nx.nch : 0;   // next kernel (0: nothing to prefetch)
+    uint32_t pc = 0, pr = it.r0;
+    const uint32_t nx_nch = nx.n_stages ? nx.nch : 0;
     uint32_t nc = 0, nr = nx.r0;
     ChunkInfo nci = {};
     if (nx_nch) chunk_info(nx, 0, &nci);
@@ -720,128 +795,138 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
     return;
   }
 
-  // ---------------- consumers: activation prologue ----------------
-  // x (optionally RMS-normalised, src/tensor.rs:164-186) -> 16-element runs
-  // of three 8-bit limbs with a shared power-of-two scale.  A quad of lanes
-  // converts one run: each lane owns 4 elements (one dp4a word per limb).
-  pdl_wait();
-  const uint32_t ctid = tid;  // 0..255
-  const float4* x4 = reinterpret_cast<const float4*>(p.x);
-  const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
-  const uint32_t n4 = p.cols / 4;
-  float inv = 1.f;
-  if (p.prologue == PRO_RMSNORM) {
-    float ss = 0.f;
-    for (uint32_t i = ctid; i < n4; i += GV_CWARPS * 32) {
-      float4 v = x4[i];
-      ss = fmaf(v.x, v.x, ss);
-      ss = fmaf(v.y, v.y, ss);
-      ss = fmaf(v.z, v.z, ss);
-      ss = fmaf(v.w, v.w, ss);
+  // ---------------- consumers ----------------
+  const uint32_t ctid = tid;
+  for (uint32_t r = ctid; r < p.max_rows; r += GV_NT) acc[r] = 0.f;
+  pdl_wait();  // the predecessor's output (this GEMV's input) is complete
+  if (p.in_runs) {
+    // records written by the producing kernel: one bulk copy
+    if (ctid == 0) {
+      mbar_expect_tx(&recbar, NX * 64);
+      bulk_g2s(rec, p.in_runs, NX * 64, &recbar, 0ull);
+    }
+    if (!mbar_wait(&recbar, 0)) {
+      if (lane == 0) atomicExch(&p.state->error, 3u);
+      return;
+    }
+  } else {
+    // f32 input (RMS-normalised when norm_w is set) -> records; every load of
+    // this thread in flight at once (x in buf[0..7], weight in buf[8..15] when
+    // normalising, else x in buf[0..15]; the host bounds cols)
+    const float4* x4 = reinterpret_cast<const float4*>(p.x);
+    const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
+    const uint32_t n4 = p.cols / 4;
+    const bool norm = p.norm_w != nullptr;
+    float4 buf[16];
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      const bool isw = norm && j >= 8;
+      const uint32_t i4 = ctid + GV_NT * (isw ? j - 8 : j);
+      buf[j] = i4 < n4 ? (isw ? w4[i4] : x4[i4]) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float inv = 1.f;
+    if (norm) {
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        ss = fmaf(buf[j].x, buf[j].x, ss);
+        ss = fmaf(buf[j].y, buf[j].y, ss);
+        ss = fmaf(buf[j].z, buf[j].z, ss);
+        ss = fmaf(buf[j].w, buf[j].w, ss);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) red[warp] = ss;
+      named_sync(1, GV_NT);
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < GV_CWARPS; w++) tot += red[w];
+      inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)p.cols), p.eps)));
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) red[warp] = ss;
-    named_sync(1, GV_CWARPS * 32);
-    float tot = 0.f;
-#pragma unroll
-    for (int w = 0; w < GV_CWARPS; w++) tot += red[w];
-    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)p.cols), p.eps)));
-  }
-  for (uint32_t base = warp * 8; base < NX; base += GV_CWARPS * 8) {
-    uint32_t k = base + (lane >> 2), q = lane & 3, i4 = 4 * k + q;
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (k < NX && i4 < n4) {
-      float4 t = x4[i4];
-      v[0] = t.x;
-      v[1] = t.y;
-      v[2] = t.z;
-      v[3] = t.w;
-      if (p.prologue == PRO_RMSNORM) {
-        float4 wn = w4[i4];
+    for (int j = 0; j < 16; j++) {
+      if (norm && j >= 8) break;
+      if (GV_NT * j >= 4 * NX) break;  // block-uniform
+      const uint32_t i4 = ctid + GV_NT * j;
+      float v[4] = {buf[j].x, buf[j].y, buf[j].z, buf[j].w};
+      if (norm) {
+        const float4 wn = buf[j + 8];
         v[0] = __fmul_rn(__fmul_rn(v[0], inv), wn.x);
         v[1] = __fmul_rn(__fmul_rn(v[1], inv), wn.y);
         v[2] = __fmul_rn(__fmul_rn(v[2], inv), wn.z);
         v[3] = __fmul_rn(__fmul_rn(v[3], inv), wn.w);
       }
-    }
-    float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-    float sm = (v[0] + v[1]) + (v[2] + v[3]);
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    sm += __shfl_xor_sync(0xffffffffu, sm, 1);
-    sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-    if (k < NX) {
-      int e = 0;
-      if (m > 0.f) frexpf(m, &e);
-      uint32_t wa = 0, wb = 0, wc = 0;
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        int X = __float2int_rn(ldexpf(v[i], 22 - e));
-        int c = ((X + 128) & 255) - 128;
-        int X1 = (X - c) >> 8;
-        int b = ((X1 + 128) & 255) - 128;
-        int a = (X1 - b) >> 8;
-        wa |= (uint32_t)(a & 255) << (8 * i);
-        wb |= (uint32_t)(b & 255) << (8 * i);
-        wc |= (uint32_t)(c & 255) << (8 * i);
-      }
-      uint32_t* lp = reinterpret_cast<uint32_t*>(limbs + 48 * k);
-      lp[q] = wa;
-      lp[4 + q] = wb;
-      lp[8 + q] = wc;
-      if (q == 0) {
-        xsc[k] = ldexpf(1.0f, e - 22);
-        xsum[k] = sm;
-      }
+      quad_to_run(v, i4 & 3, (i4 >> 2) < NX ? rec : nullptr, i4 >> 2);
     }
   }
-  for (uint32_t r = ctid; r < p.max_rows; r += GV_CWARPS * 32) acc[r] = 0.f;
-  named_sync(1, GV_CWARPS * 32);
+  named_sync(1, GV_NT);
 
   bool ok = true;
   if (it.n_stages) {
     switch (it.dt) {
-      case FZ_Q4_K: ok = gv_consume<FZ_Q4_K>(p, it, chunks, ring, full, empty, limbs, xsc, xsum, acc); break;
-      case FZ_Q6_K: ok = gv_consume<FZ_Q6_K>(p, it, chunks, ring, full, empty, limbs, xsc, xsum, acc); break;
-      case FZ_Q8_0: ok = gv_consume<FZ_Q8_0>(p, it, chunks, ring, full, empty, limbs, xsc, xsum, acc); break;
-      case FZ_Q5_0: ok = gv_consume<FZ_Q5_0>(p, it, chunks, ring, full, empty, limbs, xsc, xsum, acc); break;
+      case FZ_Q4_K: ok = gv_consume<FZ_Q4_K>(p, it, chunks, ring, full, empty, rec, acc); break;
+      case FZ_Q6_K: ok = gv_consume<FZ_Q6_K>(p, it, chunks, ring, full, empty, rec, acc); break;
+      case FZ_Q8_0: ok = gv_consume<FZ_Q8_0>(p, it, chunks, ring, full, empty, rec, acc); break;
+      case FZ_Q5_0: ok = gv_consume<FZ_Q5_0>(p, it, chunks, ring, full, empty, rec, acc); break;
     }
   }
-  if (!ok && lane == 0) atomicExch(&p.state->error, 3u);
-  named_sync(1, GV_CWARPS * 32);
+  if (!ok) {
+    if (lane == 0) atomicExch(&p.state->error, 3u);
+    return;
+  }
+  named_sync(1, GV_NT);
 
   // ---------------- epilogue ----------------
   if (!it.n_stages) return;
   const GvSeg& s = *it.s;
-  uint32_t nrows = it.r1 - it.r0;
-  unsigned long long best = 0;
-  for (uint32_t i = ctid; i < nrows; i += GV_CWARPS * 32) {
-    uint32_t row = it.r0 + i;
-    float v = acc[i];
-    if (p.epilogue == EPI_STORE) {
-      s.out[row] = s.bias ? __fadd_rn(v, s.bias[row]) : v;
-    } else if (p.epilogue == EPI_RESID) {
-      s.out[row] = __fadd_rn(s.out[row], v);
-    } else if (p.epilogue == EPI_SWIGLU) {
-      if (!(i & 1)) {
-        float u = acc[i + 1];
-        s.out[row >> 1] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
+  const uint32_t nrows = it.r1 - it.r0;
+  if (p.epilogue == EPI_STORE) {
+    for (uint32_t i = ctid; i < nrows; i += GV_NT) {
+      uint32_t row = it.r0 + i;
+      s.out[row] = s.bias ? __fadd_rn(acc[i], s.bias[row]) : acc[i];
+    }
+  } else if (p.epilogue == EPI_RESID) {
+    // x += W v (src/model.rs:470, :477)
+    for (uint32_t i = ctid; i < nrows; i += GV_NT) {
+      uint32_t row = it.r0 + i;
+      s.out[row] = __fadd_rn(s.out[row], acc[i]);
+    }
+  } else if (p.epilogue == EPI_SWIGLU) {
+    // rows interleave gate/up: h = silu(gate) * up (src/tensor.rs:213-227)
+    float hv[4];
+    uint32_t np = nrows / 2;
+    for (uint32_t k = 0; k < 4; k++) {
+      uint32_t j = ctid + k * GV_NT;
+      hv[k] = 0.f;
+      if (j < np) {
+        float g = acc[2 * j], u = acc[2 * j + 1];
+        hv[k] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+        if (s.out) s.out[(it.r0 >> 1) + j] = hv[k];
       }
-    } else {
+    }
+    named_sync(1, GV_NT);
+    for (uint32_t k = 0; k < 4; k++) {
+      uint32_t j = ctid + k * GV_NT;
+      if (j < np) acc[j] = hv[k];
+    }
+    named_sync(1, GV_NT);
+    if (p.out_runs) values_to_runs(acc, np, nullptr, p.out_runs, it.r0 / 32, ctid, GV_NT);
+  } else {
+    unsigned long long best = 0;
+    for (uint32_t i = ctid; i < nrows; i += GV_NT) {
+      uint32_t row = it.r0 + i;
+      float v = acc[i];
       s.out[row] = v;
       unsigned long long k = argmax_key(v, row);
       best = k > best ? k : best;
     }
-  }
-  if (p.epilogue == EPI_LOGITS) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
       best = other > best ? other : best;
     }
     if (lane == 0) kred[warp] = best;
-    named_sync(1, GV_CWARPS * 32);
+    named_sync(1, GV_NT);
     if (ctid == 0) {
       unsigned long long m = 0;
       for (int w = 0; w < GV_CWARPS; w++) m = kred[w] > m ? kred[w] : m;
@@ -851,34 +936,44 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
 }
 
 // ---- host side ---------------------------------------------------------------
-constexpr uint32_t GV_SMEM_2 = 110 * 1024;   // two blocks per SM (current + next kernel)
-constexpr uint32_t GV_SMEM_1 = 220 * 1024;   // one block per SM
+constexpr uint32_t GV_SMEM = 200 * 1024;   // one block per SM
 constexpr uint32_t GV_PF_AHEAD = 96 * 1024;
 constexpr uint32_t GV_PF_NEXT = 64 * 1024;
 
 void kernels_init() {
-  CK(cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, GV_SMEM_1));
+  CK(cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, GV_SMEM));
   num_sms();
 }
 
-static void fill_segs(const GemvSeg* in, int nseg, GvSeg* out, uint32_t nctas) {
+static uint32_t epi_align(int epi) { return epi == EPI_SWIGLU ? 32 : 1; }
+
+// CTA ranges: one block per SM split in proportion to bytes, each segment's
+// rows divided into whole `align`-row units as evenly as the count allows.
+static void fill_segs(const GemvLaunch& g, GvSeg* out) {
+  const uint32_t sms = (uint32_t)num_sms();
+  const uint32_t align = epi_align(g.epilogue);
   uint64_t total = 0;
-  for (int i = 0; i < nseg; i++) total += (uint64_t)in[i].w.rows * in[i].w.stride;
+  for (int i = 0; i < g.nseg; i++) total += (uint64_t)g.seg[i].w.rows * dev_row_stride(g.seg[i].w.dtype, g.seg[i].w.cols);
   uint32_t begin = 0;
-  for (int i = 0; i < nseg; i++) {
-    const DevMat& w = in[i].w;
-    uint32_t want = (uint32_t)((double)nctas * (double)((uint64_t)w.rows * w.stride) / (double)total + 0.5);
-    uint32_t maxb = (w.rows + 1) / 2;
-    want = want < 1 ? 1 : want > maxb ? maxb : want;
-    out[i] = GvSeg{w.ptr, w.rows, w.dtype, w.cols, in[i].bias, in[i].out, begin, begin + want};
-    begin += want;
+  for (int i = 0; i < g.nseg; i++) {
+    const DevMat& w = g.seg[i].w;
+    if (w.rows % align) fail(FZ_EINVAL, "gemv: %u rows not a multiple of %u", w.rows, align);
+    uint32_t units = w.rows / align;
+    uint32_t share = g.nseg == 1 ? sms
+                                 : (uint32_t)((double)sms * (double)((uint64_t)w.rows * dev_row_stride(w.dtype, w.cols)) /
+                                                  (double)total + 0.5);
+    share = std::max<uint32_t>(1, std::min(share, units));
+    uint32_t per = (units + share - 1) / share;
+    uint32_t n = (units + per - 1) / per;
+    out[i] = GvSeg{w.ptr, w.rows, w.dtype, w.cols, g.seg[i].bias, g.seg[i].out, begin, begin + n, align};
+    begin += n;
   }
 }
 
-static uint32_t gemv_ctas(const GemvLaunch& g) {
-  uint32_t n = (uint32_t)num_sms();
-  if (g.nseg == 1) n = std::min<uint32_t>(n, (g.seg[0].w.rows + 1) / 2);
-  return n;
+uint32_t gemv_ctas(const GemvLaunch& g) {
+  GvSeg s[3];
+  fill_segs(g, s);
+  return s[g.nseg - 1].cta_end;
 }
 
 void launch_gemv(const GemvLaunch& g, cudaStream_t st) {
@@ -886,37 +981,38 @@ void launch_gemv(const GemvLaunch& g, cudaStream_t st) {
   uint32_t cols = g.seg[0].w.cols;
   for (int i = 0; i < g.nseg; i++)
     if (g.seg[i].w.cols != cols) fail(FZ_EINVAL, "gemv segments disagree on input width");
-  uint32_t nctas = gemv_ctas(g);
-  fill_segs(g.seg, g.nseg, p.seg, nctas);
+  if (!g.in_runs && !g.x) fail(FZ_EINVAL, "gemv: no input activation");
+  if (!g.in_runs && (cols / 4 > (g.norm_w ? 8u : 16u) * GV_NT || cols % 32))
+    fail(FZ_EINVAL, "gemv: input width %u unsupported for an f32 input", cols);
+  if (lay_nch(cols) > GV_MAX_CH) fail(FZ_EINVAL, "gemv: input width %u too large", cols);
+  fill_segs(g, p.seg);
   uint32_t grid = p.seg[g.nseg - 1].cta_end;
   p.nseg = g.nseg;
   p.cols = cols;
+  p.in_runs = reinterpret_cast<const XRun*>(g.in_runs);
   p.x = g.x;
   p.norm_w = g.norm_w;
   p.eps = g.eps;
-  p.prologue = g.prologue;
   p.epilogue = g.epilogue;
   p.state = g.state;
-  // shared memory: ring + activation limbs + per-run scale/sum + row sums
-  uint32_t U = (cols + 63) / 64, NX = 4 * U;
+  p.out_runs = reinterpret_cast<XRun*>(g.out_runs);
   uint32_t max_rows = 0, slot = 0;
   for (int i = 0; i < g.nseg; i++) {
     const GvSeg& s = p.seg[i];
-    uint32_t n = s.cta_end - s.cta_begin;
-    max_rows = std::max(max_rows, 2 * ((s.rows / 2 + n - 1) / n) + 2);
+    uint32_t n = s.cta_end - s.cta_begin, units = s.rows / s.align;
+    max_rows = std::max(max_rows, s.align * ((units + n - 1) / n) + s.align);
     slot = std::max(slot, GV_ROWS * lay_max_chunk_bytes(s.dtype, s.cols));
   }
   slot = (slot + 127) & ~127u;
-  uint32_t fixed = 48 * NX + 8 * NX + 4 * max_rows + 16 + 16 * GV_MAX_SLOTS + 128;
-  uint32_t budget = GV_SMEM_1;  // one block per SM (register file: 16 warps x up to 128 registers)
-  if (fixed + 2 * slot > budget) fail(FZ_EINVAL, "gemv: input width %u too large for shared memory", cols);
-  uint32_t slots = std::min<uint32_t>(GV_MAX_SLOTS, (budget - fixed) / slot);
+  uint32_t fixed = runs_for(cols) * 64 + 4 * max_rows + 128;
+  if (fixed + 2 * slot > GV_SMEM) fail(FZ_EINVAL, "gemv: %u rows per block exceed shared memory", max_rows);
+  uint32_t slots = std::min<uint32_t>(GV_MAX_SLOTS, (GV_SMEM - fixed) / slot);
   p.slots = slots;
   p.slot_bytes = slot;
   p.max_rows = max_rows;
   p.pf_ahead = GV_PF_AHEAD;
   if (g.next) {
-    fill_segs(g.next->seg, g.next->nseg, p.next.seg, gemv_ctas(*g.next));
+    fill_segs(*g.next, p.next.seg);
     p.next.nseg = g.next->nseg;
     p.next.budget = GV_PF_NEXT;
   }
@@ -924,42 +1020,70 @@ void launch_gemv(const GemvLaunch& g, cudaStream_t st) {
   launch_pdl(k_gemv, dim3(grid), dim3(GV_THREADS), smem, st, p);
 }
 
+// Embedding lookup of state->token (src/model.rs:482-506): one dequantized row.
+__global__ void k_embed(uint32_t dt, const uint8_t* __restrict__ base, uint32_t cols, uint32_t vocab,
+                        StepState* __restrict__ st, float* __restrict__ x) {
+  pdl_trigger();
+  pdl_wait();
+  const uint32_t tok = st->token, u = blockIdx.x * blockDim.x + threadIdx.x;
+  if (tok >= vocab) {
+    // the host validates ids before they reach the device; this is a guard
+    if (u == 0) st->error = 1;
+  }
+  if (u < (cols + 63) / 64) dequant_unit(dt, base, vocab, tok < vocab ? tok : 0, cols, u, x);
+}
+
+void launch_embed(const DevMat& emb, StepState* st, float* x, cudaStream_t s) {
+  uint32_t units = (emb.cols + 63) / 64;
+  launch_pdl(k_embed, dim3((units + 63) / 64), dim3(64), 0, s, emb.dtype, (const uint8_t*)emb.ptr, emb.cols, emb.rows,
+             st, x);
+}
+
 // ---------------------------------------------------------------------------
 // Attention (src/model.rs:371-438) with RoPE (src/model.rs:193-217) and the
-// KV append (src/model.rs:346-356) folded in.  Grid (splits, n_kv): a block
-// owns one KV head, the G = nh/nkv query heads that read it, and a slice of
-// positions [0, pos].  It rotates q (and, in the slice that holds pos, the
-// new k, which it also writes to the cache), bulk-copies its K and V rows
-// into shared memory, and writes the slice's (max, sum, weighted V)
-// partials; k_attn_combine merges the slices.  RoPE uses host-computed
-// cos/sin (glibc powf/sinf/cosf: the reference's own factors) and the
-// reference's uncontracted a*c - b*s / a*s + b*c.
+// KV append (src/model.rs:346-356) folded in: flash-decode.  Grid
+// (S, n_kv), S = ceil(#SM / n_kv): a block owns one KV head, the G = nh/nkv
+// query heads that read it, and an equal share of positions [0, pos] (sized
+// from pos at run time, so every block has work at every position).  K/V
+// rows stream through a 3-deep ring of 32-position tiles by bulk copy; warp
+// h keeps head h's online softmax (running max, sum and weighted V).  The
+// block that owns pos rotates the new k, appends k and v to the cache and
+// places them in its last tile.  k_attn_combine merges the S partials.
+// RoPE uses host-computed cos/sin (glibc powf/sinf/cosf: the reference's own
+// factors) and the reference's uncontracted a*c - b*s / a*s + b*c.
 // ---------------------------------------------------------------------------
 constexpr int AT_THREADS = 256;
 constexpr int AT_MAXG = 8;
+constexpr int AT_TP = 32;    // positions per tile
+constexpr int AT_NBUF = 3;   // tiles in flight
 
 template <int HD>
 __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ qkv, const float2* __restrict__ cs,
                                                       float* __restrict__ kc, float* __restrict__ vc,
                                                       float* __restrict__ partials, uint32_t nh, uint32_t nkv,
-                                                      uint32_t max_ctx, uint32_t per_split, StepState* st) {
+                                                      uint32_t max_ctx, StepState* st) {
+  constexpr int DPL = HD / 32;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(16) float qs[AT_MAXG][HD];
-  __shared__ __align__(8) uint64_t bar;
-  const uint32_t G = nh / nkv, kvh = blockIdx.y, split = blockIdx.x;
+  __shared__ __align__(8) uint64_t bar[AT_NBUF];
+  const uint32_t G = nh / nkv, kvh = blockIdx.y, split = blockIdx.x, S = gridDim.x;
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t half = HD / 2;
+  float* tiles = reinterpret_cast<float*>(smem);  // [NBUF][K|V][TP][HD]
+  const float* kvk = kc + (uint64_t)kvh * max_ctx * HD;
+  const float* kvv = vc + (uint64_t)kvh * max_ctx * HD;
   if (tid == 0) {
     pdl_trigger();
-    // The K/V rows of this slice below the (possibly not yet advanced)
-    // position are already final: start pulling them into L2 before waiting
-    // for the predecessor.
-    uint32_t p0 = *((volatile uint32_t*)&st->pos);
-    uint32_t a0 = split * per_split, a1 = min(min(p0, max_ctx), a0 + per_split);
+    // rows below the (possibly not yet advanced) position are final already:
+    // pull this block's share into L2 before waiting for the predecessor
+    uint32_t p0 = min(*((volatile uint32_t*)&st->pos), max_ctx - 1);
+    uint32_t per0 = (p0 + S) / S, a0 = min(split * per0, p0), a1 = min(p0, a0 + per0);
     if (a1 > a0) {
-      bulk_prefetch(kc + ((uint64_t)kvh * max_ctx + a0) * HD, (a1 - a0) * HD * 4);
-      bulk_prefetch(vc + ((uint64_t)kvh * max_ctx + a0) * HD, (a1 - a0) * HD * 4);
+      bulk_prefetch(kvk + (uint64_t)a0 * HD, (a1 - a0) * HD * 4);
+      bulk_prefetch(kvv + (uint64_t)a0 * HD, (a1 - a0) * HD * 4);
     }
+    for (int b = 0; b < AT_NBUF; b++) mbar_init(&bar[b], 1);
+    fence_barrier_init();
   }
   pdl_wait();
   const uint32_t pos = st->pos;
@@ -967,31 +1091,25 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
     if (tid == 0) st->error = 2;
     return;
   }
-  const uint32_t total = pos + 1;
-  const uint32_t t0 = split * per_split;
-  const uint32_t t1 = min(total, t0 + per_split);
-  const uint32_t n = t1 > t0 ? t1 - t0 : 0;
-  float* kt = reinterpret_cast<float*>(smem);     // [per_split][HD]
-  float* vt = kt + (size_t)per_split * HD;         // [per_split][HD]
-  float* sc = vt + (size_t)per_split * HD;         // [G][per_split]
-  const float* kvk = kc + (uint64_t)kvh * max_ctx * HD;
-  const float* kvv = vc + (uint64_t)kvh * max_ctx * HD;
-  // cached rows [t0, min(t1, pos)) arrive by bulk copy
-  const uint32_t ncached = t1 > pos ? (pos > t0 ? pos - t0 : 0) : n;
-  if (tid == 0) {
-    mbar_init(&bar, 1);
-    fence_barrier_init();
-  }
-  __syncthreads();
-  if (tid == 0 && ncached) {
-    uint32_t bytes = ncached * HD * 4;
-    mbar_expect_tx(&bar, 2 * bytes);
-    uint64_t pol = policy_evict_first();
-    bulk_g2s(kt, kvk + (uint64_t)t0 * HD, bytes, &bar, pol);
-    bulk_g2s(vt, kvv + (uint64_t)t0 * HD, bytes, &bar, pol);
-  }
-  // rotated queries (the 1/sqrt(hd) scale is applied to the dot, src/model.rs:237)
-  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+  const uint32_t total = pos + 1, per = (total + S - 1) / S;
+  const uint32_t t0 = min(split * per, total), t1 = min(total, t0 + per), n = t1 - t0;
+  const uint32_t ntiles = (n + AT_TP - 1) / AT_TP;
+  const uint64_t pol = policy_evict_first();
+  // tile j: positions [t0 + j*TP, ..); rows below pos come from the cache
+  auto issue = [&](uint32_t j) {
+    uint32_t b = j % AT_NBUF, a = t0 + j * AT_TP, e = min(min(t1, a + AT_TP), pos);
+    uint32_t rows = e > a ? e - a : 0;
+    float* kt = tiles + (size_t)b * 2 * AT_TP * HD;
+    mbar_expect_tx(&bar[b], 2 * rows * HD * 4);
+    if (rows) {
+      bulk_g2s(kt, kvk + (uint64_t)a * HD, rows * HD * 4, &bar[b], pol);
+      bulk_g2s(kt + AT_TP * HD, kvv + (uint64_t)a * HD, rows * HD * 4, &bar[b], pol);
+    }
+  };
+  __syncthreads();  // barrier init visible
+  if (tid == 0)
+    for (uint32_t j = 0; j < ntiles && j < (uint32_t)AT_NBUF; j++) issue(j);
+  // rotated queries
   const float2* csp = cs + (uint64_t)pos * half;
   for (uint32_t idx = tid; idx < G * half; idx += AT_THREADS) {
     uint32_t h = idx / half, i = idx % half;
@@ -1001,87 +1119,96 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
     qs[h][i] = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
     qs[h][i + half] = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
   }
-  if (t1 == total && n) {
-    // this slice holds pos: rotate the new k, append k and v
+  const bool owns_pos = n && t1 == total;
+  float kn[2] = {0.f, 0.f}, vn[2] = {0.f, 0.f};
+  if (owns_pos && tid < half) {
+    // rotate the new k, append k and v (KvCache::append)
     const float* kx = qkv + (uint64_t)(nh + kvh) * HD;
     const float* vx = qkv + (uint64_t)(nh + nkv + kvh) * HD;
+    float a = kx[tid], b = kx[tid + half];
+    float2 c = csp[tid];
+    kn[0] = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
+    kn[1] = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
+    vn[0] = vx[tid];
+    vn[1] = vx[tid + half];
     float* kdst = kc + ((uint64_t)kvh * max_ctx + pos) * HD;
     float* vdst = vc + ((uint64_t)kvh * max_ctx + pos) * HD;
-    for (uint32_t i = tid; i < half; i += AT_THREADS) {
-      float a = kx[i], b = kx[i + half];
-      float2 c = csp[i];
-      float ra = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
-      float rb = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
-      kdst[i] = ra;
-      kdst[i + half] = rb;
-      kt[(size_t)(pos - t0) * HD + i] = ra;
-      kt[(size_t)(pos - t0) * HD + i + half] = rb;
-    }
-    for (uint32_t i = tid; i < HD; i += AT_THREADS) {
-      float v = vx[i];
-      vdst[i] = v;
-      vt[(size_t)(pos - t0) * HD + i] = v;
-    }
-  }
-  if (ncached && !mbar_wait(&bar, 0)) {
-    if (tid == 0) st->error = 5;
-    return;
+    kdst[tid] = kn[0];
+    kdst[tid + half] = kn[1];
+    vdst[tid] = vn[0];
+    vdst[tid + half] = vn[1];
   }
   __syncthreads();
-  // scores: one (position, head) per thread-iteration; lanes start at
-  // different columns so a warp's 16-byte reads spread over the banks
-  for (uint32_t idx = tid; idx < n * G; idx += AT_THREADS) {
-    uint32_t t = idx % n, h = idx / n;
-    const float4* kr = reinterpret_cast<const float4*>(kt + (size_t)t * HD);
-    const float4* qr = reinterpret_cast<const float4*>(qs[h]);
-    float s = 0.f;
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+  float m = -INFINITY, l = 0.f, acc[DPL];
+#pragma unroll
+  for (int d = 0; d < DPL; d++) acc[d] = 0.f;
+  for (uint32_t j = 0; j < ntiles; j++) {
+    const uint32_t b = j % AT_NBUF, a = t0 + j * AT_TP, tn = min(t1, a + AT_TP) - a;
+    float* kt = tiles + (size_t)b * 2 * AT_TP * HD;
+    float* vt = kt + AT_TP * HD;
+    if (!mbar_wait(&bar[b], (j / AT_NBUF) & 1)) {
+      if (tid == 0) st->error = 5;
+      return;
+    }
+    if (owns_pos && pos >= a && pos < a + AT_TP) {  // block-uniform
+      if (tid < half) {
+        kt[(pos - a) * HD + tid] = kn[0];
+        kt[(pos - a) * HD + tid + half] = kn[1];
+        vt[(pos - a) * HD + tid] = vn[0];
+        vt[(pos - a) * HD + tid + half] = vn[1];
+      }
+      __syncthreads();
+    }
+    if (warp < G) {
+      const uint32_t t = lane;
+      float s = -INFINITY;
+      if (t < tn) {
+        const float4* kr = reinterpret_cast<const float4*>(kt + (size_t)t * HD);
+        const float4* qr = reinterpret_cast<const float4*>(qs[warp]);
+        float dsum = 0.f;
 #pragma unroll 8
-    for (uint32_t j = 0; j < HD / 4; j++) {
-      uint32_t jj = (j + t) & (HD / 4 - 1);
-      float4 k4 = kr[jj], q4 = qr[jj];
-      s = fmaf(q4.x, k4.x, s);
-      s = fmaf(q4.y, k4.y, s);
-      s = fmaf(q4.z, k4.z, s);
-      s = fmaf(q4.w, k4.w, s);
+        for (uint32_t c = 0; c < HD / 4; c++) {
+          uint32_t cc = (c + t) & (HD / 4 - 1);
+          float4 k4 = kr[cc], q4 = qr[cc];
+          dsum = fmaf(q4.x, k4.x, dsum);
+          dsum = fmaf(q4.y, k4.y, dsum);
+          dsum = fmaf(q4.z, k4.z, dsum);
+          dsum = fmaf(q4.w, k4.w, dsum);
+        }
+        s = __fmul_rn(dsum, scale);
+      }
+      float mt = s;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+      const float mn = fmaxf(m, mt);
+      const float alpha = expf(m - mn);
+      const float pr = t < tn ? expf(s - mn) : 0.f;
+      float ps = pr;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      l = fmaf(l, alpha, ps);
+      m = mn;
+#pragma unroll
+      for (int d = 0; d < DPL; d++) acc[d] *= alpha;
+      for (uint32_t t2 = 0; t2 < tn; t2++) {
+        const float pt = __shfl_sync(0xffffffffu, pr, t2);
+        const float* vr = vt + (size_t)t2 * HD + lane * DPL;
+#pragma unroll
+        for (int d = 0; d < DPL; d++) acc[d] = fmaf(pt, vr[d], acc[d]);
+      }
     }
-    sc[h * per_split + t] = __fmul_rn(s, scale);
+    __syncthreads();  // buffer b free
+    if (tid == 0 && j + AT_NBUF < ntiles) issue(j + AT_NBUF);
   }
-  __syncthreads();
-  // per-head max / exp / sum over this slice (warp h).  Partials:
-  // stats [nkv][G][S] of (max, sum), then acc [nkv][G][HD][Spad].
-  const uint32_t S = gridDim.x, Spad = (S + 3) & ~3u;
-  float2* stats = reinterpret_cast<float2*>(partials) + (uint64_t)kvh * G * S;
-  float* pacc = partials + 2 * (uint64_t)nkv * G * S + (uint64_t)kvh * G * HD * Spad;
+  // partials: stats [nkv][G][S] of (max, sum), then acc [nkv][G][HD][Spad]
+  const uint32_t Spad = (S + 3) & ~3u;
   if (warp < G) {
-    float m = -INFINITY;
-    for (uint32_t t = lane; t < n; t += 32) m = fmaxf(m, sc[warp * per_split + t]);
+    float2* stats = reinterpret_cast<float2*>(partials) + (uint64_t)kvh * G * S;
+    float* pacc = partials + ((2 * (uint64_t)nkv * G * S + 3) & ~3ull) + (uint64_t)kvh * G * HD * Spad;
+    if (lane == 0) stats[warp * S + split] = make_float2(m, l);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float l = 0.f;
-    for (uint32_t t = lane; t < n; t += 32) {
-      float e = expf(sc[warp * per_split + t] - m);
-      sc[warp * per_split + t] = e;
-      l += e;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) stats[warp * S + split] = make_float2(n ? m : -INFINITY, n ? l : 0.f);
-  }
-  __syncthreads();
-  // weighted V sum: thread per (head, dim)
-  for (uint32_t idx = tid; idx < G * HD; idx += AT_THREADS) {
-    uint32_t h = idx / HD, d = idx % HD;
-    const float* pr = sc + h * per_split;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    uint32_t t = 0;
-    for (; t + 4 <= n; t += 4) {
-      a0 = fmaf(pr[t], vt[(size_t)t * HD + d], a0);
-      a1 = fmaf(pr[t + 1], vt[(size_t)(t + 1) * HD + d], a1);
-      a2 = fmaf(pr[t + 2], vt[(size_t)(t + 2) * HD + d], a2);
-      a3 = fmaf(pr[t + 3], vt[(size_t)(t + 3) * HD + d], a3);
-    }
-    for (; t < n; t++) a0 = fmaf(pr[t], vt[(size_t)t * HD + d], a0);
-    pacc[((uint64_t)h * HD + d) * Spad + split] = (a0 + a1) + (a2 + a3);
+    for (int d = 0; d < DPL; d++) pacc[((uint64_t)warp * HD + lane * DPL + d) * Spad + split] = acc[d];
   }
 }
 
@@ -1089,8 +1216,8 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
 // w_s = exp(m_s - max_s m_s).  Grid nh, block hd.  Each thread reads its
 // split values as consecutive float4s, all issued before they are used.
 constexpr int AT_MAXS = 256;
-__global__ void k_attn_combine(const float* __restrict__ partials, float* __restrict__ ctx, uint32_t nh, uint32_t nkv,
-                               uint32_t hd, uint32_t S, StepState* st) {
+__global__ void k_attn_combine(const float* __restrict__ partials, float* __restrict__ ctx, XRun* __restrict__ ctx_runs,
+                               uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t S, StepState* st) {
   __shared__ float ws[AT_MAXS], ls[AT_MAXS];
   __shared__ float s_den;
   if (threadIdx.x == 0) pdl_trigger();
@@ -1100,7 +1227,7 @@ __global__ void k_attn_combine(const float* __restrict__ partials, float* __rest
   const uint32_t Spad = (S + 3) & ~3u;
   const float2* stats = reinterpret_cast<const float2*>(partials) + ((uint64_t)kvh * G + hg) * S;
   const float4* acc4 =
-      reinterpret_cast<const float4*>(partials + 2 * (uint64_t)nkv * G * S + (((uint64_t)h) * hd + d) * Spad);
+      reinterpret_cast<const float4*>(partials + ((2 * (uint64_t)nkv * G * S + 3) & ~3ull) + (((uint64_t)h) * hd + d) * Spad);
   // all of this thread's acc values in flight at once (S <= 64 in one pass)
   float4 av[16];
 #pragma unroll
@@ -1145,46 +1272,49 @@ __global__ void k_attn_combine(const float* __restrict__ partials, float* __rest
     num = fmaf(ws[4 * k + 2], a4.z, num);
     num = fmaf(ws[4 * k + 3], a4.w, num);
   }
-  ctx[(uint64_t)h * hd + d] = __fdiv_rn(num, s_den);
+  const float v = __fdiv_rn(num, s_den);
+  ctx[(uint64_t)h * hd + d] = v;
+  // run records of ctx (the o_proj input): 8 runs per 128-wide head
+  __shared__ float sv[128];
+  sv[d] = v;
+  __syncthreads();
+  values_to_runs(sv, hd, nullptr, ctx_runs, h * (hd / 16), d, hd);
 }
 
-static uint32_t attention_per_split(uint32_t hd) { return hd == 128 ? 64 : 128; }
-
-uint32_t attention_splits(uint32_t hd, uint32_t max_ctx) {
-  uint32_t per = attention_per_split(hd);
-  return (max_ctx + per - 1) / per;
+uint32_t attention_splits(uint32_t n_kv) {
+  uint32_t s = ((uint32_t)num_sms() + n_kv - 1) / n_kv;
+  return s < 1 ? 1 : s > AT_MAXS ? AT_MAXS : s;
 }
 
 uint64_t attention_partial_floats(uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t splits) {
   uint32_t G = nh / nkv, Spad = (splits + 3) & ~3u;
-  return 2ull * nkv * G * splits + (uint64_t)nkv * G * hd * Spad;
+  return ((2ull * nkv * G * splits + 3) & ~3ull) + (uint64_t)nkv * G * hd * Spad;
 }
 
+static size_t attention_smem(uint32_t hd) { return (size_t)AT_NBUF * 2 * AT_TP * hd * 4; }
+
 void attention_init() {
-  CK(cudaFuncSetAttribute(k_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
-  CK(cudaFuncSetAttribute(k_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+  CK(cudaFuncSetAttribute(k_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attention_smem(128)));
+  CK(cudaFuncSetAttribute(k_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attention_smem(64)));
 }
 
 void launch_attention(const AttnLaunch& a, cudaStream_t s) {
   uint32_t G = a.n_heads / a.n_kv;
   if (G > AT_MAXG) fail(FZ_EINVAL, "attention: GQA group %u > %d", G, AT_MAXG);
-  uint32_t per = attention_per_split(a.hd);
-  uint32_t splits = attention_splits(a.hd, a.max_ctx);
-  if (splits > a.splits) fail(FZ_EINVAL, "attention: partials sized for %u splits, need %u", a.splits, splits);
-  if (splits > AT_MAXS) fail(FZ_EINVAL, "attention: %u splits > %d (max_ctx too large)", splits, AT_MAXS);
-  size_t smem = (size_t)per * a.hd * 4 * 2 + (size_t)G * per * 4;
+  uint32_t splits = a.splits;
+  if (splits > AT_MAXS) fail(FZ_EINVAL, "attention: %u splits > %d", splits, AT_MAXS);
   dim3 grid(splits, a.n_kv);
   const float2* cs = reinterpret_cast<const float2*>(a.rope_cs);
   if (a.hd == 128)
-    launch_pdl(k_attn<128>, grid, dim3(AT_THREADS), smem, s, a.qkv, cs, a.kcache, a.vcache, a.partials, a.n_heads,
-               a.n_kv, a.max_ctx, per, a.state);
+    launch_pdl(k_attn<128>, grid, dim3(AT_THREADS), attention_smem(128), s, a.qkv, cs, a.kcache, a.vcache,
+               a.partials, a.n_heads, a.n_kv, a.max_ctx, a.state);
   else if (a.hd == 64)
-    launch_pdl(k_attn<64>, grid, dim3(AT_THREADS), smem, s, a.qkv, cs, a.kcache, a.vcache, a.partials, a.n_heads,
-               a.n_kv, a.max_ctx, per, a.state);
+    launch_pdl(k_attn<64>, grid, dim3(AT_THREADS), attention_smem(64), s, a.qkv, cs, a.kcache, a.vcache, a.partials,
+               a.n_heads, a.n_kv, a.max_ctx, a.state);
   else
     fail(FZ_EINVAL, "head_dim %u unsupported (64 or 128)", a.hd);
-  launch_pdl(k_attn_combine, dim3(a.n_heads), dim3(a.hd), 0, s, (const float*)a.partials, a.ctx, a.n_heads, a.n_kv,
-             a.hd, splits, a.state);
+  launch_pdl(k_attn_combine, dim3(a.n_heads), dim3(a.hd), 0, s, (const float*)a.partials, a.ctx,
+             reinterpret_cast<XRun*>(a.ctx_runs), a.n_heads, a.n_kv, a.hd, splits, a.state);
 }
 
 // ---------------------------------------------------------------------------

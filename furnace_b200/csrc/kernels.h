@@ -42,29 +42,35 @@ struct StepState {
   uint32_t pad[3];
 };
 
-enum GemvPrologue : int { PRO_COPY = 0, PRO_RMSNORM = 1 };
 enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_LOGITS = 3 };
+
+// Activation vectors travel between kernels as 64-byte run records (one per
+// 16 elements, see kernels.cu); runs_for(cols) records cover `cols`.
+uint32_t runs_for(uint32_t cols);
+void launch_to_runs(const float* x, uint32_t cols, void* runs, uint32_t nruns, cudaStream_t s);
 
 // Up to 3 weight segments sharing one input vector (q|k|v).
 struct GemvSeg {
   DevMat w;
   const float* bias;   // [rows] or null
-  float* out;          // destination base for this segment
+  float* out;          // destination base for this segment (RESID: the residual, updated in place)
 };
 
 struct GemvLaunch {
   GemvSeg seg[3];
   int nseg = 1;
-  const float* x = nullptr;         // input vector [cols]
-  const float* norm_w = nullptr;    // PRO_RMSNORM weight
+  const void* in_runs = nullptr;    // input as run records (written by the producing kernel), or
+  const float* x = nullptr;         // input as f32 [cols], converted in the GEMV prologue,
+  const float* norm_w = nullptr;    //   RMS-normalised with this weight when set
   float eps = 0.f;
-  int prologue = PRO_COPY;
   int epilogue = EPI_STORE;
   StepState* state = nullptr;       // EPI_LOGITS argmax key
+  void* out_runs = nullptr;         // SWIGLU: records of the next GEMV's input
   const GemvLaunch* next = nullptr; // the next GEMV of the step (L2 prefetch)
 };
 
 void launch_gemv(const GemvLaunch& g, cudaStream_t s);
+uint32_t gemv_ctas(const GemvLaunch& g);
 
 // Embedding row of state->token dequantized to f32.
 void launch_embed(const DevMat& emb, StepState* st, float* x, cudaStream_t s);
@@ -78,12 +84,13 @@ struct AttnLaunch {
   float* kcache;
   float* vcache;
   float* ctx;            // [nh*hd]
+  void* ctx_runs;        // run records of ctx (o_proj input)
   float* partials;       // attention_partial_floats(...) floats
   uint32_t n_heads, n_kv, hd, max_ctx, splits;
   StepState* state;
 };
 void launch_attention(const AttnLaunch& a, cudaStream_t s);
-uint32_t attention_splits(uint32_t hd, uint32_t max_ctx);
+uint32_t attention_splits(uint32_t n_kv);
 uint64_t attention_partial_floats(uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t splits);
 
 // Step bookkeeping after the logits (argmax -> ids_out, next token, pos++).

@@ -13,8 +13,11 @@
 //   bytes  of one chunk of nu units / nsb super-blocks:
 //     Q4_K  [nsb x 144 native super-blocks]
 //     Q6_K  [nsb x 208 bodies][nsb x f16 d, padded to 16]
-//           body = 4 x 48-byte groups (ql run a | ql run b | qh run) + the 16
-//           signed scales reordered per group as (g0, g2, g1, g3)
+//           body = [4 x 32 nibble bytes][4 x 16 high-bit bytes][4 x 4 scales]
+//           regrouped per unit of 64 consecutive elements: nibble byte i of
+//           unit k holds elements 64k+i (low) and 64k+32+i (high); high-bit
+//           byte i holds bits 4-5 of elements 64k+i, +16, +32, +48 (two bits
+//           each, low to high); scale byte s belongs to elements 64k+16s..+16
 //     Q8_0  [nu x 64 int8 quants][nu x 2 x f16 d, padded to 16]
 //     Q5_0  [nu x 32 nibble bytes][nu x 2 x u32 high bits, padded][nu x 2 x f16 d, padded]
 //   row stride = sum of chunk bytes (a multiple of 16).
@@ -99,15 +102,7 @@ FZ_HD uint32_t lay_chunk_of(uint32_t dt, uint32_t cols, uint32_t u) {
   return c;
 }
 
-// Index (in 16-element runs of x) of the j-th run (j < 4) unit u multiplies.
-FZ_HD uint32_t x_chunk_of(uint32_t dt, uint32_t u, uint32_t j) {
-  if (dt == FZ_Q6_K) {
-    // unit u = (super-block u/4, group uu = u%4): h = uu/2, is = uu%2;
-    // run j covers elements 256 sb + 128 h + 16 is + 32 j .. +16
-    uint32_t sb = u >> 2, uu = u & 3;
-    return 16 * sb + 8 * (uu >> 1) + (uu & 1) + 2 * j;
-  }
-  return 4 * u + j;  // 64 consecutive elements
-}
+// Unit u of every format covers elements 64u .. 64u+63, i.e. the 16-element
+// activation runs 4u .. 4u+3.
 
 }  // namespace fz

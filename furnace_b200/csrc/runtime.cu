@@ -74,8 +74,9 @@ struct fz_model {
   float* out_norm = nullptr;
   std::vector<Layer> layers;
   uint64_t resident = 0, streamed = 0;
-  // activations
+  // activations (f32) and the run records GEMVs read (see kernels.cu)
   DevBuf x, qkv, ctx, h, logits;
+  DevBuf runs_ctx, runs_h;  // attention output and ffn hidden as run records
 };
 
 struct fz_kv {
@@ -90,7 +91,7 @@ struct fz_kv {
 };
 
 struct fz_weight {
-  DevBuf buf;
+  DevBuf buf, runs;
   DevMat m;
 };
 
@@ -180,6 +181,8 @@ struct OpHook {
 };
 
 // One decode step: embed -> layers -> [norm + lm_head + argmax] -> finalize.
+// Every GEMV reads run records written by its predecessor's epilogue; RMSNorm
+// inputs are x (.) w with 1/rms from the predecessor's sum-of-squares partials.
 void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nullptr) {
   auto H = [&](int op, bool b) {
     if (hook) hook->at(op, b);
@@ -190,7 +193,6 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
   uint32_t hd = c.head_dim, qd = c.n_heads * hd, kd = c.n_kv_heads * hd;
   float* x = m->x.as<float>();
   float* qkv = m->qkv.as<float>();
-  // every GEMV of the step, in order, so each can prefetch the next one's weights
   std::vector<GemvLaunch> gl(4 * c.n_layers + 1);
   for (uint32_t li = 0; li < c.n_layers; li++) {
     Layer& L = m->layers[li];
@@ -202,24 +204,21 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
     g.x = x;
     g.norm_w = L.attn_norm;
     g.eps = c.rms_eps;
-    g.prologue = PRO_RMSNORM;
     g.epilogue = EPI_STORE;
     GemvLaunch& go = gl[4 * li + 1];
     go.seg[0] = GemvSeg{L.wo, nullptr, x};
-    go.x = m->ctx.as<float>();
-    go.prologue = PRO_COPY;
+    go.in_runs = m->runs_ctx.p;
     go.epilogue = EPI_RESID;
     GemvLaunch& gu = gl[4 * li + 2];
-    gu.seg[0] = GemvSeg{L.wgu, nullptr, m->h.as<float>()};
+    gu.seg[0] = GemvSeg{L.wgu, nullptr, nullptr};
     gu.x = x;
     gu.norm_w = L.ffn_norm;
     gu.eps = c.rms_eps;
-    gu.prologue = PRO_RMSNORM;
     gu.epilogue = EPI_SWIGLU;
+    gu.out_runs = m->runs_h.p;
     GemvLaunch& gd = gl[4 * li + 3];
     gd.seg[0] = GemvSeg{L.wd, nullptr, x};
-    gd.x = m->h.as<float>();
-    gd.prologue = PRO_COPY;
+    gd.in_runs = m->runs_h.p;
     gd.epilogue = EPI_RESID;
   }
   GemvLaunch& lm = gl[4 * c.n_layers];
@@ -227,7 +226,6 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
   lm.x = x;
   lm.norm_w = m->out_norm;
   lm.eps = c.rms_eps;
-  lm.prologue = PRO_RMSNORM;
   lm.epilogue = EPI_LOGITS;
   lm.state = st;
   size_t last = with_logits ? gl.size() - 1 : gl.size() - 2;
@@ -242,7 +240,7 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
     H(FZ_OP_QKV, false);
     float* kc = kv->k.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
     float* vc = kv->v.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
-    AttnLaunch a{qkv, kv->rope_cs.as<float>(), kc, vc, m->ctx.as<float>(), kv->partials.as<float>(),
+    AttnLaunch a{qkv, kv->rope_cs.as<float>(), kc, vc, m->ctx.as<float>(), m->runs_ctx.p, kv->partials.as<float>(),
                  c.n_heads, c.n_kv_heads, hd, kv->max_ctx, kv->splits, st};
     H(FZ_OP_ATTN, true);
     launch_attention(a, s);
@@ -549,6 +547,12 @@ int fz_model_load(const fz_file* f, int tp, const int* device_ids, fz_model** ou
     m->ctx.alloc(qd * 4);
     m->h.alloc(F * 4);
     m->logits.alloc((uint64_t)c.vocab * 4);
+    auto runs = [&](DevBuf& b, uint32_t n) {
+      b.alloc((uint64_t)runs_for(n) * 64);
+      CK(cudaMemset(b.p, 0, b.n));  // padding records past the vector must read as zero
+    };
+    runs(m->runs_ctx, qd);
+    runs(m->runs_h, F);
     // byte accounting
     m->resident = total + smalls.size() * 4;
     uint64_t per_tok = m->lm_head.gguf_bytes + m->embd.gguf_bytes / c.vocab + (uint64_t)H * 4;
@@ -624,10 +628,11 @@ int fz_kv_new(fz_model* m, uint32_t max_ctx, int kv_dtype, fz_kv** out) {
     }
     kv->rope_cs.alloc(cs.size() * 4);
     CK(cudaMemcpy(kv->rope_cs.p, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
-    kv->splits = attention_splits(c.head_dim, max_ctx);
-    uint32_t G = c.n_heads / c.n_kv_heads;
-    (void)G;
+    kv->splits = attention_splits(c.n_kv_heads);
     kv->partials.alloc(attention_partial_floats(c.n_heads, c.n_kv_heads, c.head_dim, kv->splits) * 4);
+    // the split-padding entries of the accumulator block are never written
+    // and must read as zero (they are weighted by 0 in the merge)
+    CK(cudaMemset(kv->partials.p, 0, kv->partials.n));
     kv->state.alloc(sizeof(StepState));
     CK(cudaMemset(kv->state.p, 0, sizeof(StepState)));
     kv->forced.alloc((uint64_t)max_ctx * 4 + 16);
@@ -821,6 +826,8 @@ int fz_weight_upload(uint32_t dtype, const void* raw, size_t nbytes, uint32_t d_
     w->buf.alloc((uint64_t)d_out * w->m.stride + 256);
     CK(cudaMemset(w->buf.p, 0, w->buf.n));
     w->m.ptr = w->buf.as<uint8_t>();
+    w->runs.alloc((uint64_t)runs_for(d_in) * 64);
+    CK(cudaMemset(w->runs.p, 0, w->runs.n));
     DevBuf staging(std::min<uint64_t>(nbytes + 16, 256ull << 20));
     upload_rows(dtype, (const uint8_t*)raw, d_out, d_in, w->m.ptr, staging, 0);
     *out = w.release();
@@ -833,11 +840,18 @@ int fz_matmul_quant_dev(const fz_weight* w, const float* a_dev, uint32_t seq, fl
   return guard([&] {
     need(w && a_dev && out_dev, "null argument");
     cudaStream_t s = (cudaStream_t)stream;
+    // widths up to 30720 convert the f32 input inside the GEMV; wider inputs
+    // are converted to run records by a separate pass
+    const bool direct = w->m.cols <= 30720;
     for (uint32_t i = 0; i < seq; i++) {
       GemvLaunch g;
       g.seg[0] = GemvSeg{w->m, nullptr, out_dev + (uint64_t)i * w->m.rows};
-      g.x = a_dev + (uint64_t)i * w->m.cols;
-      g.prologue = PRO_COPY;
+      if (direct) {
+        g.x = a_dev + (uint64_t)i * w->m.cols;
+      } else {
+        launch_to_runs(a_dev + (uint64_t)i * w->m.cols, w->m.cols, w->runs.p, runs_for(w->m.cols), s);
+        g.in_runs = w->runs.p;
+      }
       g.epilogue = EPI_STORE;
       launch_gemv(g, s);
     }
