@@ -300,6 +300,9 @@ void check_state(fz_kv* kv) {
   StepState st;
   CK(cudaMemcpyAsync(&st, kv->state.p, sizeof st, cudaMemcpyDeviceToHost, kv->m->stream));
   CK(cudaStreamSynchronize(kv->m->stream));
+  // codes 1-2: token >= vocab, position >= max_ctx; 3-5: a bounded device
+  // wait (input records, ring slot, KV tile) ran out
+  if (st.error >= 3) fail(FZ_ETIMEOUT, "a bounded device wait ran out (code %u)", st.error);
   if (st.error) fail(FZ_EINVAL, "device step rejected its input (code %u)", st.error);
 }
 
