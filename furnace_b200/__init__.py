@@ -41,6 +41,7 @@ EXPORTS = [
     "fz_model_load", "fz_model_free", "fz_model_config", "fz_model_bytes", "fz_kv_new", "fz_kv_free", "fz_kv_len",
     "fz_kv_set_len", "fz_kv_read", "fz_forward", "fz_decode_greedy", "fz_dequant", "fz_matmul_quant",
     "fz_weight_upload", "fz_weight_free", "fz_matmul_quant_dev", "fz_step_profile", "fz_model_stream",
+    "fz_dequant_dev_noalloc",
 ]
 
 OPS = ["embed", "qkv", "rope_append", "attention", "o_proj", "gate_up", "down", "lm_head", "finalize"]
@@ -114,6 +115,7 @@ def load_library(build_if_missing: bool = True):
         "fz_weight_upload": (I, [U32, P, S, U32, U32, pp]),
         "fz_weight_free": (None, [P]),
         "fz_matmul_quant_dev": (I, [P, P, U32, P, P]),
+        "fz_dequant_dev_noalloc": (I, [U32, P, S, S, P, P]),
         "fz_model_stream": (I, [P, pp, C.POINTER(I)]),
         "fz_step_profile": (I, [P, P, U32, U32, C.POINTER(C.c_double), C.POINTER(C.c_double), u32p]),
     }

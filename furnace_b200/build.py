@@ -16,7 +16,7 @@ OUT = os.path.join(HERE, "_build")
 LIB = os.path.join(OUT, "libfurnace_cuda.so")
 SYNTH = os.path.join(OUT, "libfzsynth.so")
 
-CUDA_SOURCES = ["kernels.cu", "runtime.cu"]
+CUDA_SOURCES = ["kernels.cu", "runtime.cu", "noalloc.cu"]
 CXX_SOURCES = ["gguf.cpp"]
 HEADERS = sorted(f for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))) + [os.path.join("..", "..", "include", "furnace.h")]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

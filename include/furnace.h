@@ -171,6 +171,20 @@ int fz_weight_upload(uint32_t dtype, const void* raw, size_t nbytes, uint32_t d_
 void fz_weight_free(fz_weight* w);
 int fz_matmul_quant_dev(const fz_weight* w, const float* a_dev, uint32_t seq, float* out_dev, void* stream);
 
+/* quant::dequantize on device buffers, allocating nothing.  No counterpart in
+ * the reference (its dequantize, src/quant.rs:261-281, returns a new Vec):
+ * fz_dequant allocates device buffers per call, which a caller whose device
+ * memory is fully committed, or that must not stall other streams with a
+ * device-wide cudaFree, cannot use.  raw_dev / out_dev are device pointers,
+ * `stream` a cudaStream_t as void*; the work is queued on that stream.  The
+ * repacked tensor lives in a fixed 8 MiB per-device scratch array: tensors
+ * whose device layout exceeds it return FZ_EINVAL (any tensor of at most
+ * 2 MiB of GGUF data fits).  Calls on one device whose work overlaps in time
+ * race on the scratch.  The first call on each device looks up the scratch
+ * address; make it before any stream capture begins. */
+int fz_dequant_dev_noalloc(uint32_t dtype, const void* raw_dev, size_t nbytes, size_t n, float* out_dev,
+                           void* stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif
