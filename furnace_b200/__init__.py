@@ -68,7 +68,7 @@ _lib = None
 
 
 def lib_path() -> str:
-    return _build.LIB
+    return os.environ.get("FURNACE_B200_LIB") or _build.LIB
 
 
 def load_library(build_if_missing: bool = True):
@@ -76,7 +76,7 @@ def load_library(build_if_missing: bool = True):
     global _lib
     if _lib is not None:
         return _lib
-    path = _build.LIB
+    path = os.environ.get("FURNACE_B200_LIB") or _build.LIB
     if not os.path.exists(path):
         if not build_if_missing:
             raise FurnaceError(FZ_ECUDA, f"CUDA library missing: {path}")

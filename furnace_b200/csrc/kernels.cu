@@ -25,7 +25,9 @@
 #include <cuda_fp16.h>
 
 #include <cstdio>
+#include <cstring>
 #include <utility>
+#include <vector>
 
 #include "fz_internal.h"
 #include "kernels.h"
@@ -61,6 +63,40 @@ __device__ __forceinline__ float h2f(uint32_t bits16) {
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
+// Optional per-CTA timeline of the step kernels (%globaltimer, ns), recorded
+// by thread 0 of every CTA while a trace buffer is installed (trace_enable):
+// t[0] start, t[1] after the wait on the predecessor, t[2] input ready,
+// t[3] main loop done, t[4] end.  Off (one global load per CTA) otherwise.
+// ---------------------------------------------------------------------------
+__device__ TraceRec* g_trace = nullptr;
+__device__ uint32_t g_trace_cap = 0;
+__device__ uint32_t g_trace_n = 0;
+
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+struct Tracer {
+  TraceRec* r = nullptr;
+  __device__ __forceinline__ void begin(uint32_t tag, uint32_t aux) {
+    TraceRec* base = g_trace;
+    if (!base) return;
+    const uint32_t i = atomicAdd(&g_trace_n, 1u);
+    if (i >= g_trace_cap) return;
+    r = base + i;
+    r->tag = tag;
+    r->cta = blockIdx.x | (blockIdx.y << 16);
+    r->aux = aux;
+    r->t[0] = gtimer();
+  }
+  __device__ __forceinline__ void mark(int k) {
+    if (r) r->t[k] = gtimer();
+  }
+};
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -671,20 +707,23 @@ __device__ bool gv_consume(const GvParams& p, const StageIter& it, const ChunkIn
   uint32_t slot = 0, phase = 0;
   for (uint32_t c = 0; c < it.nch; c++) {
     const uint32_t nu = chunks[c].nu, tb = chunks[c].tb;
+    // lanes past the chunk's units, and row slots past the CTA's rows, work
+    // on a clamped (valid) unit / row and drop the result: no divergence, so
+    // the rows of a warp interleave
+    const uint32_t lu = min(lane, nu - 1);
+    const float lane_on = lane < nu ? 1.f : 0.f;
     XRun xr[4];
-    if (lane < nu) {
-      const uint32_t u = chunks[c].cu0 + lane;
 #pragma unroll
-      for (uint32_t j = 0; j < 4; j++) xr[j] = load_run(rec, u, j);
-    }
+    for (uint32_t j = 0; j < 4; j++) xr[j] = load_run(rec, chunks[c].cu0 + lu, j);
     for (uint32_t ra = it.r0; ra < it.r1; ra += GV_ROWS) {
       if (!mbar_wait(&full[slot], phase)) return false;
       const uint8_t* tile = ring + (size_t)slot * p.slot_bytes;
+      const uint32_t last = it.r1 - 1 - ra;
       float v[GV_RPW];
 #pragma unroll
       for (int j = 0; j < GV_RPW; j++) {
-        uint32_t row = ra + warp + GV_CWARPS * j;
-        v[j] = (row < it.r1 && lane < nu) ? unit_dot<DT>(tile + (row - ra) * tb, lane, nu, xr) : 0.f;
+        const uint32_t rr = min(warp + GV_CWARPS * j, last);
+        v[j] = lane_on * unit_dot<DT>(tile + rr * tb, lu, nu, xr);
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1)
@@ -733,6 +772,8 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
   }
   __syncthreads();
   if (tid == 0) pdl_trigger();
+  Tracer tr;
+  if (tid == 0) tr.begin(TR_GEMV + p.epilogue, gridDim.x);
 
   if (warp == GV_CWARPS) {
     // ---------------- producer (weights only: no wait on the predecessor) ----
@@ -799,6 +840,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
   const uint32_t ctid = tid;
   for (uint32_t r = ctid; r < p.max_rows; r += GV_NT) acc[r] = 0.f;
   pdl_wait();  // the predecessor's output (this GEMV's input) is complete
+  if (ctid == 0) tr.mark(1);
   if (p.in_runs) {
     // records written by the producing kernel: one bulk copy
     if (ctid == 0) {
@@ -860,6 +902,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
     }
   }
   named_sync(1, GV_NT);
+  if (ctid == 0) tr.mark(2);
 
   bool ok = true;
   if (it.n_stages) {
@@ -875,6 +918,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
     return;
   }
   named_sync(1, GV_NT);
+  if (ctid == 0) tr.mark(3);
 
   // ---------------- epilogue ----------------
   if (!it.n_stages) return;
@@ -933,12 +977,31 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
       atomicMax(&p.state->argmax_key, m);
     }
   }
+  if (ctid == 0) tr.mark(4);
 }
 
 // ---- host side ---------------------------------------------------------------
 constexpr uint32_t GV_SMEM = 200 * 1024;   // one block per SM
 constexpr uint32_t GV_PF_AHEAD = 96 * 1024;
 constexpr uint32_t GV_PF_NEXT = 64 * 1024;
+
+// Install (cap > 0) or remove (cap == 0) the step-kernel trace buffer.
+void trace_install(TraceRec* buf, uint32_t cap) {
+  CK(cudaMemcpyToSymbol(g_trace, &buf, sizeof buf));
+  CK(cudaMemcpyToSymbol(g_trace_cap, &cap, sizeof cap));
+  trace_reset(0);
+}
+
+void trace_reset(cudaStream_t s) {
+  uint32_t z = 0;
+  CK(cudaMemcpyToSymbolAsync(g_trace_n, &z, sizeof z, 0, cudaMemcpyHostToDevice, s));
+}
+
+uint32_t trace_count() {
+  uint32_t n = 0;
+  CK(cudaMemcpyFromSymbol(&n, g_trace_n, sizeof n));
+  return n;
+}
 
 void kernels_init() {
   CK(cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, GV_SMEM));
@@ -1072,7 +1135,9 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
   float* tiles = reinterpret_cast<float*>(smem);  // [NBUF][K|V][TP][HD]
   const float* kvk = kc + (uint64_t)kvh * max_ctx * HD;
   const float* kvv = vc + (uint64_t)kvh * max_ctx * HD;
+  Tracer tr;
   if (tid == 0) {
+    tr.begin(TR_ATTN, gridDim.x * gridDim.y);
     pdl_trigger();
     // rows below the (possibly not yet advanced) position are final already:
     // pull this block's share into L2 before waiting for the predecessor
@@ -1086,6 +1151,7 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
     fence_barrier_init();
   }
   pdl_wait();
+  if (tid == 0) tr.mark(1);
   const uint32_t pos = st->pos;
   if (pos >= max_ctx) {
     if (tid == 0) st->error = 2;
@@ -1210,6 +1276,7 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
 #pragma unroll
     for (int d = 0; d < DPL; d++) pacc[((uint64_t)warp * HD + lane * DPL + d) * Spad + split] = acc[d];
   }
+  if (tid == 0) tr.mark(4);
 }
 
 // Merge the split partials: ctx[h][d] = sum_s w_s acc_s[d] / sum_s w_s l_s,
@@ -1220,8 +1287,13 @@ __global__ void k_attn_combine(const float* __restrict__ partials, float* __rest
                                uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t S, StepState* st) {
   __shared__ float ws[AT_MAXS], ls[AT_MAXS];
   __shared__ float s_den;
-  if (threadIdx.x == 0) pdl_trigger();
+  Tracer tr;
+  if (threadIdx.x == 0) {
+    tr.begin(TR_COMBINE, gridDim.x);
+    pdl_trigger();
+  }
   pdl_wait();
+  if (threadIdx.x == 0) tr.mark(1);
   (void)st;
   const uint32_t G = nh / nkv, h = blockIdx.x, kvh = h / G, hg = h % G, d = threadIdx.x;
   const uint32_t Spad = (S + 3) & ~3u;
@@ -1279,6 +1351,7 @@ __global__ void k_attn_combine(const float* __restrict__ partials, float* __rest
   sv[d] = v;
   __syncthreads();
   values_to_runs(sv, hd, nullptr, ctx_runs, h * (hd / 16), d, hd);
+  if (threadIdx.x == 0) tr.mark(4);
 }
 
 uint32_t attention_splits(uint32_t n_kv) {
@@ -1340,5 +1413,173 @@ __global__ void k_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_
 void launch_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, bool has_logits, cudaStream_t s) {
   launch_pdl(k_finalize, dim3(1), dim3(1), 0, s, st, forced, ids_out, has_logits ? 1 : 0);
 }
+
+// ---------------------------------------------------------------------------
+// Persistent decode step
+// ---------------------------------------------------------------------------
+#include "step_kernel.cuh"
+
+uint32_t step_attention_splits(uint32_t n_kv) { return std::max<uint32_t>(1, (uint32_t)num_sms() / n_kv); }
+
+static uint32_t step_u_bytes(const StepLaunch& L) {
+  uint32_t u = 0;
+  for (uint32_t i = 0; i < L.nph; i++) {
+    const StepPhase& ph = L.phases[i];
+    if (ph.kind == SP_ATTN) u = std::max<uint32_t>(u, (uint32_t)SK_NBUF * 2 * SK_TP * ph.a.hd * 4);
+    if (ph.kind == SP_GEMV && ph.g.x) u = std::max<uint32_t>(u, runs_for(ph.g.seg[0].w.cols) * 64);
+  }
+  return (u + 127) & ~127u;
+}
+
+// Host copy of cta_rows (the device's row split of one segment).
+static void host_cta_rows(const GvSeg& s, uint32_t b, uint32_t* r0, uint32_t* r1) {
+  uint32_t n = s.cta_end - s.cta_begin, lb = b - s.cta_begin, units = s.rows / s.align;
+  *r0 = s.align * (uint32_t)((uint64_t)units * lb / n);
+  *r1 = lb + 1 == n ? s.rows : s.align * (uint32_t)((uint64_t)units * (lb + 1) / n);
+}
+
+StepPlan step_plan_build(const StepLaunch& L) {
+  const uint32_t grid = (uint32_t)num_sms();
+  StepPlan plan;
+  plan.nph = L.nph;
+  plan.u_bytes = step_u_bytes(L);
+  plan.ring_bytes = SK_SMEM - plan.u_bytes - 2 * SK_CREC - SK_ACC;
+  std::vector<PhaseRec> rec((size_t)L.nph * grid);
+  memset(rec.data(), 0, rec.size() * sizeof(PhaseRec));
+  std::vector<std::vector<StageRec>> st(grid);
+  for (uint32_t i = 0; i < L.nph; i++) {
+    const StepPhase& sp = L.phases[i];
+    if (sp.kind == SP_EMBED) {
+      for (uint32_t b = 0; b < grid; b++) rec[(size_t)i * grid + b].kind = PH_EMBED;
+    } else if (sp.kind == SP_ATTN) {
+      const AttnLaunch& a = sp.a;
+      if (a.hd != 64 && a.hd != 128) fail(FZ_EINVAL, "head_dim %u unsupported (64 or 128)", a.hd);
+      const uint32_t G = a.n_heads / a.n_kv;
+      if (G > AT_MAXG || a.n_heads % a.n_kv) fail(FZ_EINVAL, "attention: GQA group %u unsupported", G);
+      if (a.splits * a.n_kv > grid || a.splits < 1) fail(FZ_EINVAL, "attention: %u splits x %u KV heads", a.splits, a.n_kv);
+      for (uint32_t b = 0; b < grid; b++) {
+        PhaseRec& d = rec[(size_t)i * grid + b];
+        d.kind = PH_ATTN;
+        d.qkv = a.qkv;
+        d.kc = a.kcache;
+        d.vc = a.vcache;
+        d.ctx = a.ctx;
+        d.ctx_runs = reinterpret_cast<XRun*>(a.ctx_runs);
+        d.nh = a.n_heads;
+        d.nkv = a.n_kv;
+        d.hd = a.hd;
+        d.S = a.splits;
+        d.active = b < a.splits * a.n_kv;
+        d.kvh = d.active ? b / a.splits : 0;
+        d.split = d.active ? b % a.splits : 0;
+      }
+    } else {
+      const GemvLaunch& g = sp.g;
+      const uint32_t cols = g.seg[0].w.cols;
+      for (int k = 0; k < g.nseg; k++)
+        if (g.seg[k].w.cols != cols) fail(FZ_EINVAL, "gemv segments disagree on input width");
+      if (!g.in_runs && !g.x) fail(FZ_EINVAL, "gemv: no input activation");
+      if (g.x && (cols / 4 > (g.norm_w ? 8u : 16u) * GV_NT || cols % 32))
+        fail(FZ_EINVAL, "gemv: input width %u unsupported for an f32 input", cols);
+      if (lay_nch(cols) > GV_MAX_CH) fail(FZ_EINVAL, "gemv: input width %u too large", cols);
+      if (g.epilogue == EPI_SWIGLU && !g.out_runs) fail(FZ_EINVAL, "step: SwiGLU phase without output records");
+      GvSeg segs[3];
+      fill_segs(g, segs);
+      for (uint32_t b = 0; b < grid; b++) {
+        PhaseRec& d = rec[(size_t)i * grid + b];
+        d.kind = PH_GEMV;
+        d.epi = g.epilogue;
+        d.cols = cols;
+        d.x = g.x;
+        d.norm_w = g.norm_w;
+        d.eps = g.eps;
+        d.in_runs = reinterpret_cast<const XRun*>(g.in_runs);
+        d.out_runs = reinterpret_cast<XRun*>(g.out_runs);
+        int si = 0;
+        while (si + 1 < g.nseg && b >= segs[si].cta_end) si++;
+        const GvSeg& sg = segs[si];
+        if (b < sg.cta_begin || b >= sg.cta_end) continue;
+        uint32_t r0, r1;
+        host_cta_rows(sg, b, &r0, &r1);
+        if (r1 <= r0) continue;
+        if ((r1 - r0) * 4 > SK_ACC) fail(FZ_EINVAL, "step: %u rows per block exceed the accumulators", r1 - r0);
+        d.active = 1;
+        d.dt = sg.dtype;
+        d.r0 = r0;
+        d.r1 = r1;
+        d.nch = lay_nch(cols);
+        d.out = sg.out;
+        d.bias = sg.bias;
+        for (uint32_t c = 0; c < d.nch; c++) {
+          const uint32_t nu = lay_cu0(sg.dtype, cols, c + 1) - lay_cu0(sg.dtype, cols, c);
+          const uint32_t tb = lay_chunk_bytes(sg.dtype, nu);
+          if (GV_ROWS * tb > plan.ring_bytes) fail(FZ_EINVAL, "step: a weight stage exceeds the %u-byte ring", plan.ring_bytes);
+          const uint8_t* plane = sg.w + (uint64_t)sg.rows * lay_chunk_off(sg.dtype, cols, c);
+          for (uint32_t ra = r0; ra < r1; ra += GV_ROWS)
+            st[b].push_back(StageRec{plane + (uint64_t)ra * tb, (std::min(ra + GV_ROWS, r1) - ra) * tb, 0});
+        }
+      }
+    }
+  }
+  // blob: [PhaseRec nph x grid][stage_first[grid]][stage lists, each ended by
+  // a zero record and padded to whole blocks][SL_NB zero blocks]
+  std::vector<uint32_t> first(grid);
+  std::vector<StageRec> all;
+  for (uint32_t b = 0; b < grid; b++) {
+    first[b] = (uint32_t)all.size();
+    all.insert(all.end(), st[b].begin(), st[b].end());
+    all.push_back(StageRec{nullptr, 0, 0});
+    while (all.size() % SL_BLK) all.push_back(StageRec{nullptr, 0, 0});
+  }
+  all.resize(all.size() + SL_NB * SL_BLK, StageRec{nullptr, 0, 0});
+  const size_t rec_bytes = rec.size() * sizeof(PhaseRec);
+  plan.off_stage_first = rec_bytes;
+  plan.off_stages = (rec_bytes + grid * 4 + 255) & ~(size_t)255;
+  plan.blob.assign(plan.off_stages + all.size() * sizeof(StageRec), 0);
+  memcpy(plan.blob.data(), rec.data(), rec_bytes);
+  memcpy(plan.blob.data() + plan.off_stage_first, first.data(), grid * 4);
+  memcpy(plan.blob.data() + plan.off_stages, all.data(), all.size() * sizeof(StageRec));
+  return plan;
+}
+
+void launch_step(const StepLaunch& L, const StepPlan& plan, const void* plan_dev, cudaStream_t s) {
+  SkParams P{};
+  const uint8_t* base = reinterpret_cast<const uint8_t*>(plan_dev);
+  P.rec = reinterpret_cast<const PhaseRec*>(base);
+  P.stage_first = reinterpret_cast<const uint32_t*>(base + plan.off_stage_first);
+  P.stages = reinterpret_cast<const StageRec*>(base + plan.off_stages);
+  P.nph = plan.nph;
+  P.u_bytes = plan.u_bytes;
+  P.ring_bytes = plan.ring_bytes;
+  P.pf_ahead = SK_PF_AHEAD;
+  P.st = L.state;
+  P.bar = L.bar;
+  P.attn_cnt = L.attn_cnt;
+  P.partials = L.partials;
+  P.rope_cs = reinterpret_cast<const float2*>(L.rope_cs);
+  P.max_ctx = L.max_ctx;
+  P.emb = L.emb.ptr;
+  P.emb_dt = L.emb.dtype;
+  P.emb_rows = L.emb.rows;
+  P.emb_cols = L.emb.cols;
+  P.x = L.x;
+  P.forced = L.forced;
+  P.ids_out = L.ids_out;
+  P.has_logits = L.has_logits ? 1 : 0;
+  CK(cudaMemsetAsync(L.bar, 0, sizeof(uint32_t), s));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((uint32_t)num_sms());
+  cfg.blockDim = dim3(GV_THREADS);
+  cfg.dynamicSmemBytes = SK_SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CK(cudaLaunchKernelEx(&cfg, k_step, P));
+}
+
+void step_init() { CK(cudaFuncSetAttribute(k_step, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM)); }
 
 }  // namespace fz

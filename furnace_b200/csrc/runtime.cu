@@ -7,6 +7,9 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
 #include <vector>
 
 #include "fz_internal.h"
@@ -77,12 +80,16 @@ struct fz_model {
   // activations (f32) and the run records GEMVs read (see kernels.cu)
   DevBuf x, qkv, ctx, h, logits;
   DevBuf runs_ctx, runs_h;  // attention output and ffn hidden as run records
+  DevBuf trace;             // step-kernel timeline (FURNACE_B200_TRACE=<file>)
+  std::string trace_path;
 };
 
 struct fz_kv {
   fz_model* m = nullptr;
   uint32_t max_ctx = 0, len = 0, splits = 0;
   DevBuf k, v, rope_cs, partials, state, forced, ids;
+  DevBuf plan_full, plan_layers, bar, attn_cnt;  // persistent step kernel
+  StepPlan sp_full, sp_layers;
   cudaGraphExec_t g_full = nullptr, g_layers = nullptr;
   ~fz_kv() {
     if (g_full) cudaGraphExecDestroy(g_full);
@@ -183,10 +190,9 @@ struct OpHook {
 // One decode step: embed -> layers -> [norm + lm_head + argmax] -> finalize.
 // Every GEMV reads run records written by its predecessor's epilogue; RMSNorm
 // inputs are x (.) w with 1/rms from the predecessor's sum-of-squares partials.
-void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nullptr) {
-  auto H = [&](int op, bool b) {
-    if (hook) hook->at(op, b);
-  };
+// The GEMV launches of one step in execution order: qkv, o_proj, gate_up,
+// down per layer (src/model.rs:444-478), then lm_head (src/model.rs:594-600).
+std::vector<GemvLaunch> step_gemvs(fz_kv* kv) {
   fz_model* m = kv->m;
   const fz_config& c = m->cfg;
   StepState* st = kv->state.as<StepState>();
@@ -228,6 +234,32 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
   lm.eps = c.rms_eps;
   lm.epilogue = EPI_LOGITS;
   lm.state = st;
+  return gl;
+}
+
+AttnLaunch layer_attention(fz_kv* kv, uint32_t li, uint32_t splits) {
+  fz_model* m = kv->m;
+  const fz_config& c = m->cfg;
+  const uint32_t hd = c.head_dim;
+  float* kc = kv->k.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
+  float* vc = kv->v.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
+  return AttnLaunch{m->qkv.as<float>(), kv->rope_cs.as<float>(), kc, vc, m->ctx.as<float>(), m->runs_ctx.p,
+                    kv->partials.as<float>(), c.n_heads, c.n_kv_heads, hd, kv->max_ctx, splits,
+                    kv->state.as<StepState>()};
+}
+
+// One step as separate kernels (programmatic dependent launches): the path
+// of fz_step_profile, whose per-kernel events time each op.
+void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nullptr) {
+  auto H = [&](int op, bool b) {
+    if (hook) hook->at(op, b);
+  };
+  fz_model* m = kv->m;
+  const fz_config& c = m->cfg;
+  StepState* st = kv->state.as<StepState>();
+  float* x = m->x.as<float>();
+  std::vector<GemvLaunch> gl = step_gemvs(kv);
+  GemvLaunch& lm = gl[4 * c.n_layers];
   size_t last = with_logits ? gl.size() - 1 : gl.size() - 2;
   for (size_t i = 0; i <= last; i++) gl[i].next = i < last ? &gl[i + 1] : &gl[0];
 
@@ -238,10 +270,7 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
     H(FZ_OP_QKV, true);
     launch_gemv(gl[4 * li], s);
     H(FZ_OP_QKV, false);
-    float* kc = kv->k.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
-    float* vc = kv->v.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
-    AttnLaunch a{qkv, kv->rope_cs.as<float>(), kc, vc, m->ctx.as<float>(), m->runs_ctx.p, kv->partials.as<float>(),
-                 c.n_heads, c.n_kv_heads, hd, kv->max_ctx, kv->splits, st};
+    AttnLaunch a = layer_attention(kv, li, kv->splits);
     H(FZ_OP_ATTN, true);
     launch_attention(a, s);
     H(FZ_OP_ATTN, false);
@@ -265,14 +294,100 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
   H(FZ_OP_FINALIZE, false);
 }
 
+// The step's phases for the persistent step kernel: embed, then per layer
+// qkv, attention, o_proj, gate_up, down, then lm_head when with_logits.
+std::vector<StepPhase> step_phases(fz_kv* kv, bool with_logits) {
+  const fz_config& c = kv->m->cfg;
+  std::vector<GemvLaunch> gl = step_gemvs(kv);
+  const uint32_t splits = step_attention_splits(c.n_kv_heads);
+  std::vector<StepPhase> ph;
+  StepPhase e;
+  e.kind = SP_EMBED;
+  ph.push_back(e);
+  for (uint32_t li = 0; li < c.n_layers; li++) {
+    for (int k = 0; k < 4; k++) {
+      StepPhase g;
+      g.kind = SP_GEMV;
+      g.g = gl[4 * li + k];
+      g.g.next = nullptr;
+      ph.push_back(g);
+      if (k == 0) {
+        StepPhase a;
+        a.kind = SP_ATTN;
+        a.a = layer_attention(kv, li, splits);
+        ph.push_back(a);
+      }
+    }
+  }
+  if (with_logits) {
+    StepPhase g;
+    g.kind = SP_GEMV;
+    g.g = gl[4 * c.n_layers];
+    g.g.next = nullptr;
+    ph.push_back(g);
+  }
+  return ph;
+}
+
+StepLaunch step_launch(fz_kv* kv, const std::vector<StepPhase>& ph, bool with_logits) {
+  fz_model* m = kv->m;
+  StepLaunch L;
+  L.phases = ph.data();
+  L.nph = (uint32_t)ph.size();
+  L.state = kv->state.as<StepState>();
+  L.bar = kv->bar.as<uint32_t>();
+  L.attn_cnt = kv->attn_cnt.as<uint32_t>();
+  L.partials = kv->partials.as<float>();
+  L.rope_cs = kv->rope_cs.as<float>();
+  L.max_ctx = kv->max_ctx;
+  L.emb = m->embd;
+  L.x = m->x.as<float>();
+  L.forced = kv->forced.as<uint32_t>();
+  L.ids_out = kv->ids.as<uint32_t>();
+  L.has_logits = with_logits;
+  return L;
+}
+
+// The step is captured as separate kernels (programmatic dependent launches)
+// unless FURNACE_B200_STEP=fused selects the persistent step kernel, which is
+// parity-tested but slower on B200 today: its grid barriers (~2.6 us each,
+// five per layer) and latency-bound attention phase cost more than the kernel
+// boundaries they replace.
+bool fused_step() {
+  const char* e = getenv("FURNACE_B200_STEP");
+  return e && strcmp(e, "fused") == 0;
+}
+
 void build_graphs(fz_kv* kv) {
   if (kv->g_full) return;
   cudaStream_t s = kv->m->stream;
+  const bool fused = fused_step();
+  std::vector<StepPhase> ph[2];
+  if (fused) {
+    step_init();
+    kv->bar.alloc(16);
+    kv->attn_cnt.alloc(4 * kv->m->cfg.n_kv_heads + 16);
+    CK(cudaMemset(kv->attn_cnt.p, 0, kv->attn_cnt.n));
+    for (int variant = 0; variant < 2; variant++) {
+      ph[variant] = step_phases(kv, variant == 0);
+      DevBuf& plan = variant == 0 ? kv->plan_full : kv->plan_layers;
+      StepPlan& sp = variant == 0 ? kv->sp_full : kv->sp_layers;
+      sp = step_plan_build(step_launch(kv, ph[variant], variant == 0));
+      plan.alloc(sp.blob.size());
+      CK(cudaMemcpy(plan.p, sp.blob.data(), sp.blob.size(), cudaMemcpyHostToDevice));
+      sp.blob.clear();
+      sp.blob.shrink_to_fit();
+    }
+  }
   for (int variant = 0; variant < 2; variant++) {
     cudaGraph_t g;
     CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
     try {
-      record_step(kv, variant == 0, s);
+      if (fused)
+        launch_step(step_launch(kv, ph[variant], variant == 0), variant == 0 ? kv->sp_full : kv->sp_layers,
+                    (variant == 0 ? kv->plan_full : kv->plan_layers).p, s);
+      else
+        record_step(kv, variant == 0, s);
     } catch (...) {
       cudaStreamEndCapture(s, &g);
       if (g) cudaGraphDestroy(g);
@@ -563,6 +678,14 @@ int fz_model_load(const fz_file* f, int tp, const int* device_ids, fz_model** ou
       per_tok += L.wq.gguf_bytes + L.wk.gguf_bytes + L.wv.gguf_bytes + L.wo.gguf_bytes + L.wgu.gguf_bytes +
                  L.wd.gguf_bytes + (uint64_t)(2 * H + qd + 2 * kd) * 4;
     m->streamed = per_tok;
+    // optional timeline of every step kernel's CTAs, written to the named
+    // file by fz_model_free (the records of the last fz_decode_greedy call)
+    if (const char* tp = getenv("FURNACE_B200_TRACE")) {
+      const uint32_t cap = 1u << 20;
+      m->trace.alloc((uint64_t)cap * sizeof(TraceRec));
+      m->trace_path = tp;
+      trace_install(m->trace.as<TraceRec>(), cap);
+    }
     CK(cudaStreamSynchronize(m->stream));
     *out = m.release();
   });
@@ -574,6 +697,19 @@ void fz_model_free(fz_model* m) {
   if (m->stream) {
     cudaStreamSynchronize(m->stream);
     cudaStreamDestroy(m->stream);
+  }
+  if (m->trace.p) {
+    try {
+      uint32_t n = std::min<uint32_t>(trace_count(), (uint32_t)(m->trace.n / sizeof(TraceRec)));
+      std::vector<TraceRec> recs(n);
+      if (n) CK(cudaMemcpy(recs.data(), m->trace.p, n * sizeof(TraceRec), cudaMemcpyDeviceToHost));
+      if (FILE* f = fopen(m->trace_path.c_str(), "wb")) {
+        if (n) fwrite(recs.data(), sizeof(TraceRec), n, f);
+        fclose(f);
+      }
+      trace_install(nullptr, 0);
+    } catch (...) {
+    }
   }
   delete m;
 }
@@ -717,6 +853,7 @@ int fz_decode_greedy(fz_model* m, fz_kv* kv, uint32_t first, uint32_t n_steps, c
       if (stop_ids[i] == first) return;  // src/generate.rs:125-127
     ids_out[0] = first;
     uint32_t written = 1;
+    if (m->trace.p) trace_reset(m->stream);
     if (fwd) {
       use_device(m);
       build_graphs(kv);
