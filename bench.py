@@ -17,9 +17,11 @@ e2e   : the same metric through the public C-ABI call (fz_decode_greedy)
         restatement in oracle/, the reference itself cannot be built here)
         timed on the host cores, one decode token per step.
 
-With --gpus N > 1 (torchrun, one process per GPU) every rank decodes its own
-replica of the model (tensor parallelism is not in this build yet), so the
-scaling is weak: value = total tokens/s of all ranks.
+With --gpus N > 1 (torchrun, one process per GPU) the model is split
+tensor-parallel over TP = the largest of N, N/2, ... that divides the head and
+KV-head counts (C3: 4), one NCCL communicator per TP group, and N / TP groups
+decode independent streams: value = total tokens/s of all groups; scaling
+"strong" when one group spans all N GPUs.
 """
 
 from __future__ import annotations
@@ -35,6 +37,8 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+# rank 0 prints exactly one JSON line: keep NCCL's version banner off stdout
+os.environ["NCCL_DEBUG"] = "WARN"
 
 STEP_TOKENS = 16
 CONFIG = "c3"
@@ -81,6 +85,14 @@ class Dist:
         t = torch.tensor([v], dtype=torch.float64)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
+
+    def bcast(self, obj):
+        """rank 0's obj on every rank."""
+        if not self.pg:
+            return obj
+        box = [obj]
+        self.pg.broadcast_object_list(box, src=0)
+        return box[0]
 
     def close(self):
         if self.pg:
@@ -270,7 +282,16 @@ def run_ours(args, dist):
     cud = Cudart()
     cud.set_device(dev)
     f = fz.GgufFile.open(path)
-    model = fz.Model.load(f, devices=[dev])
+    # tensor-parallel groups of `tp` consecutive ranks (see the module docstring)
+    tp = dist.world
+    while tp > 1 and (spec.n_heads % tp or spec.n_kv_heads % tp or dist.world % tp):
+        tp //= 2
+    groups = dist.world // tp
+    if tp > 1:
+        ids = dist.bcast([fz.tp_unique_id() for _ in range(groups)] if dist.rank == 0 else None)
+        model = fz.Model.load_tp(f, dist.rank % tp, tp, ids[dist.rank // tp], dev)
+    else:
+        model = fz.Model.load(f, devices=[dev])
     cfg = model.config
     resident, per_tok = model.param_bytes()
     stream, _ = model.stream()
@@ -278,7 +299,7 @@ def run_ours(args, dist):
     total_tokens = args.steps * T
     max_ctx = args.prefill + max(args.warmup * T, 2 * T) + total_tokens + 8
     kv = fz.KvCache(model, max_ctx)
-    prompt = synth.prompt_ids(cfg.vocab, args.prefill, seed=dist.rank)
+    prompt = synth.prompt_ids(cfg.vocab, args.prefill, seed=dist.rank // tp)  # one prompt per TP group
     t0 = time.perf_counter()
     _, first = model.forward(prompt, kv, want_logits=False)
     prefill_s = time.perf_counter() - t0
@@ -302,7 +323,7 @@ def run_ours(args, dist):
     dist.barrier()
     clocks = sampler.stop()
     ms = dist.max(ms)
-    tok_s = total_tokens * dist.world / (ms / 1000.0)
+    tok_s = total_tokens * groups / (ms / 1000.0)
     # ---- e2e: public API, one call per step, host buffers ---------------
     kv.len = base
     dist.barrier()
@@ -312,7 +333,7 @@ def run_ours(args, dist):
         ids2, _ = model.decode_greedy(tok, T + 1, kv)
         tok = int(ids2[-1])
     e2e_s = dist.max(time.perf_counter() - t0)
-    e2e = {"value": total_tokens * dist.world / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 + 32,
+    e2e = {"value": total_tokens * groups / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 + 32,
            "d2h_bytes_per_step": 4 * (T + 1) + 32,
            "note": "fz_decode_greedy per step; h2d = seed token + step state, d2h = ids + status"}
     # ---- per-op timing of one step's kernels (roofline of the GEMV) -----
@@ -333,15 +354,17 @@ def run_ours(args, dist):
     step_ms_sum = sum(v[0] for v in prof.values())
     ops = {o: {"ms_per_token": prof[o][0] / T, "share": prof[o][0] / step_ms_sum,
                "gbs": (prof[o][1] / (prof[o][0] / 1000.0) / 1e9) if prof[o][0] else None} for o in prof}
-    hbm = per_tok * tok_s / dist.world / 1e9
+    hbm = per_tok * tok_s / groups / 1e9  # this rank's weight bytes per token x the group's token rate
     launches_per_token = 6 * cfg.n_layers + 3
     out = {
         "metric": "decode_tok_per_s", "value": tok_s, "unit": "tok/s", "n_gpus": dist.world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "strong" if groups == 1 else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{spec.name}: {args.prefill}-token prefill then {total_tokens} greedy decode tokens "
-                               f"(batch 1), {T} tokens per step", "model": spec.name, "global_batch": dist.world,
-                   "seq_len": args.prefill + total_tokens, "parallelism": f"replicas{dist.world}",
+                               f"(batch 1), {T} tokens per step", "model": spec.name, "global_batch": groups,
+                   "seq_len": args.prefill + total_tokens,
+                   "parallelism": f"tp{tp}" + (f"x{groups}" if groups > 1 else ""),
                    "l2": "inputs larger than L2: %.2f GB of weights streamed per token" % (per_tok / 1e9),
                    "kv": "f32"},
         "hbm_gbs_per_gpu": hbm, "hbm_frac_of_8tbs": hbm / 8000.0, "hbm_frac_of_measured": hbm / peak,

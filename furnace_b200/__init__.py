@@ -41,7 +41,7 @@ EXPORTS = [
     "fz_model_load", "fz_model_free", "fz_model_config", "fz_model_bytes", "fz_kv_new", "fz_kv_free", "fz_kv_len",
     "fz_kv_set_len", "fz_kv_read", "fz_forward", "fz_decode_greedy", "fz_dequant", "fz_matmul_quant",
     "fz_weight_upload", "fz_weight_free", "fz_matmul_quant_dev", "fz_step_profile", "fz_model_stream",
-    "fz_dequant_dev_noalloc",
+    "fz_dequant_dev_noalloc", "fz_tp_slice_of", "fz_tp_unique_id", "fz_model_load_tp",
 ]
 
 OPS = ["embed", "qkv", "rope_append", "attention", "o_proj", "gate_up", "down", "lm_head", "finalize"]
@@ -57,6 +57,11 @@ class _Config(C.Structure):
     _fields_ = [("n_layers", C.c_uint32), ("n_heads", C.c_uint32), ("n_kv_heads", C.c_uint32),
                 ("hidden", C.c_uint32), ("ffn", C.c_uint32), ("head_dim", C.c_uint32), ("rope_theta", C.c_float),
                 ("rms_eps", C.c_float), ("vocab", C.c_uint32), ("context_length", C.c_uint32)]
+
+
+class _TpSlice(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("q_head0", "q_heads", "kv_head0", "kv_heads", "o_col0", "o_cols", "ffn0",
+                                          "ffn_n", "vocab0", "vocab_n", "vocab_pad")]
 
 
 class _TensorInfo(C.Structure):
@@ -116,6 +121,9 @@ def load_library(build_if_missing: bool = True):
         "fz_weight_free": (None, [P]),
         "fz_matmul_quant_dev": (I, [P, P, U32, P, P]),
         "fz_dequant_dev_noalloc": (I, [U32, P, S, S, P, P]),
+        "fz_tp_slice_of": (I, [P, I, I, P]),
+        "fz_tp_unique_id": (I, [P, S]),
+        "fz_model_load_tp": (I, [P, I, I, P, S, I, pp]),
         "fz_model_stream": (I, [P, pp, C.POINTER(I)]),
         "fz_step_profile": (I, [P, P, U32, U32, C.POINTER(C.c_double), C.POINTER(C.c_double), u32p]),
     }
@@ -247,6 +255,10 @@ class Config:
         return cls(c.n_layers, c.n_heads, c.n_kv_heads, c.hidden, c.ffn, c.head_dim, c.rope_theta, c.rms_eps, c.vocab,
                    c.context_length)
 
+    def _to_c(self) -> _Config:
+        return _Config(self.n_layers, self.n_heads, self.n_kv_heads, self.hidden, self.ffn, self.head_dim,
+                       self.rope_theta, self.rms_eps, self.vocab, self.context_length)
+
     @classmethod
     def from_gguf(cls, f: GgufFile) -> "Config":
         c = _Config()
@@ -270,6 +282,15 @@ class Model:
         h = C.c_void_p()
         dev = (C.c_int * len(devices))(*devices) if devices else None
         _check(load_library().fz_model_load(f._h, tp, dev, C.byref(h)))
+        return cls(h)
+
+    @classmethod
+    def load_tp(cls, f: GgufFile, rank: int, world: int, nccl_id: bytes, device: int) -> "Model":
+        """Rank `rank`'s share of Model::load under tensor parallelism (one
+        process per GPU); every rank calls it with the same nccl_id."""
+        h = C.c_void_p()
+        buf = C.create_string_buffer(bytes(nccl_id), max(len(nccl_id), 1)) if nccl_id else None
+        _check(load_library().fz_model_load_tp(f._h, rank, world, buf, len(nccl_id or b""), device, C.byref(h)))
         return cls(h)
 
     def close(self):
@@ -412,3 +433,19 @@ def generate(model: Model, prompt_ids, max_new: int, stop_ids=(), max_ctx: int |
     if keep_logits:
         lg = np.concatenate([logits[None], lg], axis=0)[: len(ids)]
     return ids, lg
+
+
+def tp_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for fz_model_load_tp; made on one
+    rank and handed to all (torch.distributed broadcast, a file, ...)."""
+    buf = C.create_string_buffer(128)
+    _check(load_library().fz_tp_unique_id(buf, 128))
+    return buf.raw
+
+
+def tp_slice(config: "Config", rank: int, world: int) -> dict:
+    """This rank's share under tensor parallelism (fz_tp_slice_of)."""
+    c, out = config._to_c(), _TpSlice()
+    _check(load_library().fz_tp_slice_of(C.byref(c), rank, world, C.byref(out)))
+    return {n: getattr(out, n) for n, _ in _TpSlice._fields_}
+

@@ -17,7 +17,7 @@ LIB = os.path.join(OUT, "libfurnace_cuda.so")
 SYNTH = os.path.join(OUT, "libfzsynth.so")
 
 CUDA_SOURCES = ["kernels.cu", "runtime.cu", "noalloc.cu"]
-CXX_SOURCES = ["gguf.cpp"]
+CXX_SOURCES = ["gguf.cpp", "nccl_dyn.cpp"]
 HEADERS = sorted(f for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))) + [os.path.join("..", "..", "include", "furnace.h")]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -56,7 +56,7 @@ def build_cuda(force: bool = False, verbose: bool = False) -> str:
                 print(r.stderr)
         objs.append(o)
     tmp = LIB + ".tmp"
-    _run([NVCC] + ARCH + ["-shared", "-o", tmp] + objs + ["-lcudart"])
+    _run([NVCC] + ARCH + ["-shared", "-o", tmp] + objs + ["-lcudart", "-ldl"])
     os.replace(tmp, LIB)
     return LIB
 

@@ -486,6 +486,7 @@ struct GvParams {
   XRun* out_runs;        // SWIGLU: records of the next GEMV's input
   uint32_t slots, slot_bytes, max_rows, pf_ahead;
   GvNext next;
+  uint32_t idx_base;     // EPI_LOGITS: global index of row 0
 };
 
 // This CTA's row range within its segment: whole multiples of seg.align rows
@@ -961,7 +962,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
       uint32_t row = it.r0 + i;
       float v = acc[i];
       s.out[row] = v;
-      unsigned long long k = argmax_key(v, row);
+      unsigned long long k = argmax_key(v, row + p.idx_base);
       best = k > best ? k : best;
     }
 #pragma unroll
@@ -1059,6 +1060,7 @@ void launch_gemv(const GemvLaunch& g, cudaStream_t st) {
   p.epilogue = g.epilogue;
   p.state = g.state;
   p.out_runs = reinterpret_cast<XRun*>(g.out_runs);
+  p.idx_base = g.idx_base;
   uint32_t max_rows = 0, slot = 0;
   for (int i = 0; i < g.nseg; i++) {
     const GvSeg& s = p.seg[i];
@@ -1284,7 +1286,7 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
 // split values as consecutive float4s, all issued before they are used.
 constexpr int AT_MAXS = 256;
 __global__ void k_attn_combine(const float* __restrict__ partials, float* __restrict__ ctx, XRun* __restrict__ ctx_runs,
-                               uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t S, StepState* st) {
+                               uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t S, StepState* st, uint32_t run0) {
   __shared__ float ws[AT_MAXS], ls[AT_MAXS];
   __shared__ float s_den;
   Tracer tr;
@@ -1350,7 +1352,7 @@ __global__ void k_attn_combine(const float* __restrict__ partials, float* __rest
   __shared__ float sv[128];
   sv[d] = v;
   __syncthreads();
-  values_to_runs(sv, hd, nullptr, ctx_runs, h * (hd / 16), d, hd);
+  values_to_runs(sv, hd, nullptr, ctx_runs, run0 + h * (hd / 16), d, hd);
   if (threadIdx.x == 0) tr.mark(4);
 }
 
@@ -1387,7 +1389,7 @@ void launch_attention(const AttnLaunch& a, cudaStream_t s) {
   else
     fail(FZ_EINVAL, "head_dim %u unsupported (64 or 128)", a.hd);
   launch_pdl(k_attn_combine, dim3(a.n_heads), dim3(a.hd), 0, s, (const float*)a.partials, a.ctx,
-             reinterpret_cast<XRun*>(a.ctx_runs), a.n_heads, a.n_kv, a.hd, splits, a.state);
+             reinterpret_cast<XRun*>(a.ctx_runs), a.n_heads, a.n_kv, a.hd, splits, a.state, a.ctx_run0);
 }
 
 // ---------------------------------------------------------------------------

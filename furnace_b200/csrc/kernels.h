@@ -78,6 +78,7 @@ struct GemvLaunch {
   StepState* state = nullptr;       // EPI_LOGITS argmax key
   void* out_runs = nullptr;         // SWIGLU: records of the next GEMV's input
   const GemvLaunch* next = nullptr; // the next GEMV of the step (L2 prefetch)
+  uint32_t idx_base = 0;            // EPI_LOGITS: global index of row 0 (vocab slice)
 };
 
 void launch_gemv(const GemvLaunch& g, cudaStream_t s);
@@ -99,6 +100,7 @@ struct AttnLaunch {
   float* partials;       // attention_partial_floats(...) floats
   uint32_t n_heads, n_kv, hd, max_ctx, splits;
   StepState* state;
+  uint32_t ctx_run0 = 0;  // run record index of ctx[0] in ctx_runs
 };
 void launch_attention(const AttnLaunch& a, cudaStream_t s);
 uint32_t attention_splits(uint32_t n_kv);

@@ -1,0 +1,38 @@
+#include "nccl_dyn.h"
+
+#include <dlfcn.h>
+
+#include <mutex>
+
+#include "fz_internal.h"
+
+namespace fz {
+
+const NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  static const char* err = nullptr;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      err = "libnccl.so.2 not found";
+      return;
+    }
+    auto sym = [&](const char* name) -> void* {
+      void* p = dlsym(h, name);
+      if (!p) err = "libnccl.so.2 lacks a required symbol";
+      return p;
+    };
+    api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(sym("ncclGetUniqueId"));
+    api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(sym("ncclCommInitRank"));
+    api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(sym("ncclCommDestroy"));
+    api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(sym("ncclAllReduce"));
+    api.AllGather = reinterpret_cast<decltype(api.AllGather)>(sym("ncclAllGather"));
+    api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(sym("ncclGetErrorString"));
+  });
+  if (err) fail(FZ_ECUDA, "%s", err);
+  return api;
+}
+
+}  // namespace fz

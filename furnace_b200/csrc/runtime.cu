@@ -9,11 +9,13 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <string>
 #include <vector>
 
 #include "fz_internal.h"
 #include "kernels.h"
+#include "nccl_dyn.h"
 
 namespace fz {
 const std::string& last_error();
@@ -82,6 +84,13 @@ struct fz_model {
   DevBuf runs_ctx, runs_h;  // attention output and ffn hidden as run records
   DevBuf trace;             // step-kernel timeline (FURNACE_B200_TRACE=<file>)
   std::string trace_path;
+  // tensor parallelism: this rank's share (world == 1: everything)
+  int rank = 0, world = 1;
+  ncclComm_t comm = nullptr;
+  fz_tp_slice sl{};
+  uint32_t nh_l = 0, nkv_l = 0, qd_l = 0, kd_l = 0;
+  std::vector<uint32_t> o_off;  // per layer: ctx[0]'s column within o_proj's block-aligned input
+  uint32_t o_w = 0;             // widest o_proj input (run records of ctx cover it)
 };
 
 struct fz_kv {
@@ -152,6 +161,54 @@ void upload_rows(uint32_t dtype, const uint8_t* raw, uint64_t rows, uint32_t col
   }
 }
 
+// This rank's share of the model (see fz_tp_slice in include/furnace.h).
+fz_tp_slice tp_slice(const fz_config& c, int r, int T) {
+  need(T >= 1 && r >= 0 && r < T, "rank %d of %d", r, T);
+  need(c.n_heads % T == 0 && c.n_kv_heads % T == 0, "%u heads / %u KV heads do not split over %d ranks", c.n_heads,
+       c.n_kv_heads, T);
+  fz_tp_slice s{};
+  s.q_heads = c.n_heads / T;
+  s.q_head0 = r * s.q_heads;
+  s.kv_heads = c.n_kv_heads / T;
+  s.kv_head0 = r * s.kv_heads;
+  s.o_col0 = s.q_head0 * c.head_dim;
+  s.o_cols = s.q_heads * c.head_dim;
+  const uint32_t U = (c.ffn + 255) / 256;  // FFN slices on 256-element boundaries
+  s.ffn0 = std::min(c.ffn, (uint32_t)((uint64_t)r * U / T) * 256);
+  const uint32_t f1 = r + 1 == T ? c.ffn : std::min(c.ffn, (uint32_t)((uint64_t)(r + 1) * U / T) * 256);
+  need(f1 > s.ffn0, "FFN %u too small for %d ranks", c.ffn, T);
+  s.ffn_n = f1 - s.ffn0;
+  const uint32_t vs = (c.vocab + T - 1) / T;
+  s.vocab_pad = vs * T;
+  s.vocab0 = r * vs;
+  s.vocab_n = std::min(vs, c.vocab - std::min(c.vocab, s.vocab0));
+  return s;
+}
+
+void nccl_check(ncclResult_t r, const char* what) {
+  if (r != ncclSuccess) fail(FZ_ECUDA, "%s failed: %s", what, nccl().GetErrorString(r));
+}
+
+// Upload rows [0, rows) restricted to input columns [col0, col0 + ncols)
+// (block-aligned) of a [rows, cols] GGUF weight: rows are gathered on the host.
+void upload_cols(uint32_t dtype, const uint8_t* raw, uint64_t rows, uint32_t cols, uint32_t col0, uint32_t ncols,
+                 uint8_t* dst, DevBuf& staging, cudaStream_t s) {
+  uint32_t be, bb;
+  block_geom(dtype, &be, &bb);
+  need(col0 % be == 0 && ncols % be == 0 && col0 + ncols <= cols, "column slice not block-aligned");
+  const uint64_t row_raw = gguf_bytes(dtype, 1, cols), sl_raw = gguf_bytes(dtype, 1, ncols);
+  const uint64_t off = (uint64_t)(col0 / be) * bb;
+  const uint64_t chunk_rows = std::max<uint64_t>(1, staging.n / sl_raw);
+  std::vector<uint8_t> host(std::min(chunk_rows, rows) * sl_raw);
+  for (uint64_t r0 = 0; r0 < rows; r0 += chunk_rows) {
+    const uint64_t nr = std::min(chunk_rows, rows - r0);
+    for (uint64_t r = 0; r < nr; r++) memcpy(&host[r * sl_raw], raw + (r0 + r) * row_raw + off, sl_raw);
+    CK(cudaMemcpyAsync(staging.p, host.data(), nr * sl_raw, cudaMemcpyHostToDevice, s));
+    launch_repack(dtype, staging.as<uint8_t>(), dst, (uint32_t)r0, (uint32_t)nr, (uint32_t)rows, ncols, s);
+    CK(cudaStreamSynchronize(s));
+  }
+}
+
 const TensorEntry& tensor2d(const GgufFile& f, const std::string& name, uint64_t out, uint64_t in) {
   const TensorEntry* t = f.find(name);
   if (!t) fail(FZ_EFORMAT, "no tensor named '%s'", name.c_str());
@@ -196,7 +253,10 @@ std::vector<GemvLaunch> step_gemvs(fz_kv* kv) {
   fz_model* m = kv->m;
   const fz_config& c = m->cfg;
   StepState* st = kv->state.as<StepState>();
-  uint32_t hd = c.head_dim, qd = c.n_heads * hd, kd = c.n_kv_heads * hd;
+  const uint32_t qd = m->qd_l, kd = m->kd_l;  // this rank's q / k widths
+  // tensor parallelism: o_proj and down partial sums of ranks > 0 overwrite
+  // x, rank 0 adds its partial to x, and the all-reduce that follows sums them
+  const int resid = m->rank == 0 ? EPI_RESID : EPI_STORE;
   float* x = m->x.as<float>();
   float* qkv = m->qkv.as<float>();
   std::vector<GemvLaunch> gl(4 * c.n_layers + 1);
@@ -214,7 +274,7 @@ std::vector<GemvLaunch> step_gemvs(fz_kv* kv) {
     GemvLaunch& go = gl[4 * li + 1];
     go.seg[0] = GemvSeg{L.wo, nullptr, x};
     go.in_runs = m->runs_ctx.p;
-    go.epilogue = EPI_RESID;
+    go.epilogue = resid;
     GemvLaunch& gu = gl[4 * li + 2];
     gu.seg[0] = GemvSeg{L.wgu, nullptr, nullptr};
     gu.x = x;
@@ -225,10 +285,11 @@ std::vector<GemvLaunch> step_gemvs(fz_kv* kv) {
     GemvLaunch& gd = gl[4 * li + 3];
     gd.seg[0] = GemvSeg{L.wd, nullptr, x};
     gd.in_runs = m->runs_h.p;
-    gd.epilogue = EPI_RESID;
+    gd.epilogue = resid;
   }
   GemvLaunch& lm = gl[4 * c.n_layers];
-  lm.seg[0] = GemvSeg{m->lm_head, nullptr, m->logits.as<float>()};
+  lm.seg[0] = GemvSeg{m->lm_head, nullptr, m->logits.as<float>() + m->sl.vocab0};
+  lm.idx_base = m->sl.vocab0;
   lm.x = x;
   lm.norm_w = m->out_norm;
   lm.eps = c.rms_eps;
@@ -241,11 +302,19 @@ AttnLaunch layer_attention(fz_kv* kv, uint32_t li, uint32_t splits) {
   fz_model* m = kv->m;
   const fz_config& c = m->cfg;
   const uint32_t hd = c.head_dim;
-  float* kc = kv->k.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
-  float* vc = kv->v.as<float>() + (uint64_t)li * c.n_kv_heads * kv->max_ctx * hd;
-  return AttnLaunch{m->qkv.as<float>(), kv->rope_cs.as<float>(), kc, vc, m->ctx.as<float>(), m->runs_ctx.p,
-                    kv->partials.as<float>(), c.n_heads, c.n_kv_heads, hd, kv->max_ctx, splits,
-                    kv->state.as<StepState>()};
+  float* kc = kv->k.as<float>() + (uint64_t)li * m->nkv_l * kv->max_ctx * hd;
+  float* vc = kv->v.as<float>() + (uint64_t)li * m->nkv_l * kv->max_ctx * hd;
+  AttnLaunch a{m->qkv.as<float>(), kv->rope_cs.as<float>(), kc, vc, m->ctx.as<float>(), m->runs_ctx.p,
+               kv->partials.as<float>(), m->nh_l, m->nkv_l, hd, kv->max_ctx, splits,
+               kv->state.as<StepState>()};
+  a.ctx_run0 = m->o_off[li] / 16;
+  return a;
+}
+
+// Sum of the ranks' residual-stream partials (tensor parallelism).
+void tp_allreduce_x(fz_model* m, cudaStream_t s) {
+  if (m->world == 1) return;
+  nccl_check(nccl().AllReduce(m->x.p, m->x.p, m->cfg.hidden, ncclFloat32, ncclSum, m->comm, s), "ncclAllReduce");
 }
 
 // One step as separate kernels (programmatic dependent launches): the path
@@ -276,17 +345,24 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
     H(FZ_OP_ATTN, false);
     H(FZ_OP_OPROJ, true);
     launch_gemv(gl[4 * li + 1], s);
+    tp_allreduce_x(m, s);
     H(FZ_OP_OPROJ, false);
     H(FZ_OP_GATEUP, true);
     launch_gemv(gl[4 * li + 2], s);
     H(FZ_OP_GATEUP, false);
     H(FZ_OP_DOWN, true);
     launch_gemv(gl[4 * li + 3], s);
+    tp_allreduce_x(m, s);
     H(FZ_OP_DOWN, false);
   }
   if (with_logits) {
     H(FZ_OP_LMHEAD, true);
     launch_gemv(lm, s);
+    // greedy pick over all ranks' vocabulary slices: max of the packed
+    // (logit, index) keys, which prefers the first index on ties
+    if (m->world > 1)
+      nccl_check(nccl().AllReduce(&st->argmax_key, &st->argmax_key, 1, ncclUint64, ncclMax, m->comm, s),
+                 "ncclAllReduce");
     H(FZ_OP_LMHEAD, false);
   }
   H(FZ_OP_FINALIZE, true);
@@ -299,7 +375,7 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
 std::vector<StepPhase> step_phases(fz_kv* kv, bool with_logits) {
   const fz_config& c = kv->m->cfg;
   std::vector<GemvLaunch> gl = step_gemvs(kv);
-  const uint32_t splits = step_attention_splits(c.n_kv_heads);
+  const uint32_t splits = step_attention_splits(kv->m->nkv_l);
   std::vector<StepPhase> ph;
   StepPhase e;
   e.kind = SP_EMBED;
@@ -361,12 +437,12 @@ bool fused_step() {
 void build_graphs(fz_kv* kv) {
   if (kv->g_full) return;
   cudaStream_t s = kv->m->stream;
-  const bool fused = fused_step();
+  const bool fused = fused_step() && kv->m->world == 1;
   std::vector<StepPhase> ph[2];
   if (fused) {
     step_init();
     kv->bar.alloc(16);
-    kv->attn_cnt.alloc(4 * kv->m->cfg.n_kv_heads + 16);
+    kv->attn_cnt.alloc(4 * kv->m->nkv_l + 16);
     CK(cudaMemset(kv->attn_cnt.p, 0, kv->attn_cnt.n));
     for (int variant = 0; variant < 2; variant++) {
       ph[variant] = step_phases(kv, variant == 0);
@@ -399,6 +475,15 @@ void build_graphs(fz_kv* kv) {
     cudaGraphDestroy(g);
     (variant == 0 ? kv->g_full : kv->g_layers) = ge;
   }
+}
+
+// Every rank's vocabulary slice of the last logits, in place (tensor
+// parallelism; slices are vocab_pad / world long and in rank order).
+void tp_gather_logits(fz_model* m, cudaStream_t s) {
+  if (m->world == 1) return;
+  const size_t per = m->sl.vocab_pad / m->world;
+  float* all = m->logits.as<float>();
+  nccl_check(nccl().AllGather(all + (size_t)m->rank * per, all, per, ncclFloat32, m->comm, s), "ncclAllGather");
 }
 
 void set_state(fz_kv* kv, uint32_t pos, uint32_t token, uint32_t n_forced) {
@@ -524,170 +609,245 @@ int fz_config_from_gguf(const fz_file* f, fz_config* out) {
   });
 }
 
+}  // extern "C"
+
+namespace {
+
+// Model::load (src/model.rs:520-552) for rank `rank` of `world`: the rank's
+// slice of every matrix, uploaded raw and repacked into the device layout.
+std::unique_ptr<fz_model> load_model(const fz_file* f, int rank, int world, const ncclUniqueId* id, int device) {
+  need(f != nullptr, "null argument");
+  const GgufFile& g = *f->g;
+  auto m = std::make_unique<fz_model>();
+  m->cfg = config_from_gguf(g);
+  const fz_config& c = m->cfg;
+  m->device = device;
+  m->rank = rank;
+  m->world = world;
+  CK(cudaSetDevice(m->device));
+  need(c.head_dim == 64 || c.head_dim == 128, "head_dim %u unsupported (64 or 128)", c.head_dim);
+  need(c.n_kv_heads && c.n_heads % c.n_kv_heads == 0, "%u heads not divisible by %u kv heads", c.n_heads, c.n_kv_heads);
+  need(c.n_heads / c.n_kv_heads <= 8, "GQA group %u > 8 unsupported", c.n_heads / c.n_kv_heads);
+  need(c.hidden % 32 == 0 && c.ffn % 32 == 0, "hidden/ffn must be multiples of 32");
+  const fz_tp_slice sl = tp_slice(c, rank, world);
+  m->sl = sl;
+  m->nh_l = sl.q_heads;
+  m->nkv_l = sl.kv_heads;
+  const uint32_t hd = c.head_dim, H = c.hidden, F = c.ffn;
+  const uint32_t qd = c.n_heads * hd, kd = c.n_kv_heads * hd;
+  const uint32_t qd_l = sl.q_heads * hd, kd_l = sl.kv_heads * hd, F_l = sl.ffn_n;
+  m->qd_l = qd_l;
+  m->kd_l = kd_l;
+  CK(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+  kernels_init();
+  attention_init();
+
+  // the matrices of this rank: rows [row0, row0 + rows) and block-aligned
+  // input columns [col0, col0 + cols) of each GGUF weight
+  struct Up {
+    const TensorEntry* t;
+    uint64_t row0;
+    uint32_t col0, in_d;
+    DevMat* dst;
+  };
+  m->layers.resize(c.n_layers);
+  m->o_off.assign(c.n_layers, 0);
+  std::vector<Up> ups;
+  auto add = [&](const std::string& name, uint64_t out_d, uint64_t in_d, uint64_t row0, uint32_t rows, uint32_t col0,
+                 uint32_t cols, DevMat* dst) {
+    const TensorEntry& t = tensor2d(g, name, out_d, in_d);
+    dst->dtype = t.dtype;
+    dst->rows = rows;
+    dst->cols = cols;
+    dst->stride = dev_row_stride(t.dtype, cols);
+    dst->gguf_bytes = gguf_bytes(t.dtype, rows, cols);
+    ups.push_back({&t, row0, col0, (uint32_t)in_d, dst});
+  };
+  add("token_embd.weight", c.vocab, H, 0, c.vocab, 0, H, &m->embd);
+  // lm_head: this rank's vocabulary rows (a tied model on one device reads
+  // token_embd itself, src/model.rs:539-545)
+  const bool tied = g.find("output.weight") == nullptr, share_embd = tied && world == 1;
+  if (!share_embd)
+    add(tied ? "token_embd.weight" : "output.weight", c.vocab, H, sl.vocab0, sl.vocab_n, 0, H, &m->lm_head);
+  std::vector<const TensorEntry*> gates(c.n_layers), upsw(c.n_layers);
+  for (uint32_t i = 0; i < c.n_layers; i++) {
+    std::string p = "blk." + std::to_string(i) + ".";
+    Layer& L = m->layers[i];
+    add(p + "attn_q.weight", qd, H, (uint64_t)sl.q_head0 * hd, qd_l, 0, H, &L.wq);
+    add(p + "attn_k.weight", kd, H, (uint64_t)sl.kv_head0 * hd, kd_l, 0, H, &L.wk);
+    add(p + "attn_v.weight", kd, H, (uint64_t)sl.kv_head0 * hd, kd_l, 0, H, &L.wv);
+    // o_proj: this rank's ctx columns, widened to whole blocks; the part of
+    // a shared boundary block that belongs to the neighbour multiplies zeros
+    const TensorEntry* to = g.find(p + "attn_output.weight");
+    need(to != nullptr, "no tensor named '%s'", (p + "attn_output.weight").c_str());
+    uint32_t be, bb;
+    block_geom(to->dtype, &be, &bb);
+    const uint32_t a0 = sl.o_col0 / be * be, a1 = (sl.o_col0 + sl.o_cols + be - 1) / be * be;
+    m->o_off[i] = sl.o_col0 - a0;
+    m->o_w = std::max(m->o_w, a1 - a0);
+    add(p + "attn_output.weight", H, qd, 0, H, a0, a1 - a0, &L.wo);
+    add(p + "ffn_down.weight", H, F, 0, H, sl.ffn0, F_l, &L.wd);
+    gates[i] = &tensor2d(g, p + "ffn_gate.weight", F, H);
+    upsw[i] = &tensor2d(g, p + "ffn_up.weight", F, H);
+    need(gates[i]->dtype == upsw[i]->dtype, "blk.%u ffn_gate/ffn_up dtypes differ (%u vs %u)", i, gates[i]->dtype,
+         upsw[i]->dtype);
+    L.wgu.dtype = gates[i]->dtype;
+    L.wgu.rows = 2 * F_l;
+    L.wgu.cols = H;
+    L.wgu.stride = dev_row_stride(L.wgu.dtype, H);
+    L.wgu.gguf_bytes = 2 * gguf_bytes(L.wgu.dtype, F_l, H);
+  }
+  need(m->o_w % 16 == 0, "o_proj input width %u", m->o_w);
+  // one pool for every matrix, 256-byte aligned, in the order a decode step
+  // streams them (L2 prefetch runs from one matrix into the next)
+  uint64_t total = 0;
+  auto reserve = [&](DevMat& d) {
+    uint64_t off = total;
+    total = (total + (uint64_t)d.rows * d.stride + 255) & ~uint64_t(255);
+    return off;
+  };
+  std::vector<std::pair<DevMat*, uint64_t>> order;
+  order.push_back({&m->embd, reserve(m->embd)});
+  for (uint32_t i = 0; i < c.n_layers; i++) {
+    Layer& L = m->layers[i];
+    for (DevMat* d : {&L.wq, &L.wk, &L.wv, &L.wo, &L.wgu, &L.wd}) order.push_back({d, reserve(*d)});
+  }
+  if (!share_embd) order.push_back({&m->lm_head, reserve(m->lm_head)});
+  m->weights.alloc(total);
+  CK(cudaMemset(m->weights.p, 0, total));
+  uint8_t* base = m->weights.as<uint8_t>();
+  for (auto& o : order) o.first->ptr = base + o.second;
+  uint64_t max_raw = 0;
+  for (auto& u : ups) max_raw = std::max<uint64_t>(max_raw, u.dst->gguf_bytes);
+  DevBuf staging(std::min<uint64_t>(max_raw + 16, 256ull << 20));
+  for (auto& u : ups) {
+    DevMat& d = *u.dst;
+    uint64_t nb;
+    const uint8_t* raw = g.tensor_data(*u.t, &nb);
+    if (u.col0 == 0 && d.cols == u.in_d)
+      upload_rows(d.dtype, raw + u.row0 * gguf_bytes(d.dtype, 1, u.in_d), d.rows, d.cols, d.ptr, staging, m->stream);
+    else
+      upload_cols(d.dtype, raw, d.rows, u.in_d, u.col0, d.cols, d.ptr, staging, m->stream);
+  }
+  if (share_embd) m->lm_head = m->embd;
+  // gate/up interleaved by row: row 2i = gate_(ffn0+i), row 2i+1 = up_(ffn0+i)
+  {
+    DevBuf tmp(2 * gguf_bytes(gates[0]->dtype, 1, H) * 512 + 16);
+    for (uint32_t i = 0; i < c.n_layers; i++) {
+      DevMat& d = m->layers[i].wgu;
+      uint64_t nb;
+      const uint8_t* graw = g.tensor_data(*gates[i], &nb);
+      const uint8_t* uraw = g.tensor_data(*upsw[i], &nb);
+      uint64_t rb = gguf_bytes(d.dtype, 1, H);
+      std::vector<uint8_t> hbuf(rb * 2 * 512);
+      for (uint32_t r0 = 0; r0 < F_l; r0 += 512) {
+        uint32_t nr = std::min<uint32_t>(512, F_l - r0);
+        for (uint32_t r = 0; r < nr; r++) {
+          memcpy(&hbuf[(2 * r) * rb], graw + (uint64_t)(sl.ffn0 + r0 + r) * rb, rb);
+          memcpy(&hbuf[(2 * r + 1) * rb], uraw + (uint64_t)(sl.ffn0 + r0 + r) * rb, rb);
+        }
+        CK(cudaMemcpyAsync(tmp.p, hbuf.data(), 2 * nr * rb, cudaMemcpyHostToDevice, m->stream));
+        launch_repack(d.dtype, tmp.as<uint8_t>(), d.ptr, 2 * r0, 2 * nr, d.rows, H, m->stream);
+        CK(cudaStreamSynchronize(m->stream));
+      }
+    }
+  }
+  // norms (replicated) and this rank's q/k/v bias slices
+  std::vector<float> smalls;
+  std::vector<std::pair<size_t, float**>> fix;
+  auto push = [&](const std::vector<float>& v, float** where) {
+    fix.push_back({smalls.size(), where});
+    smalls.insert(smalls.end(), v.begin(), v.end());
+    while (smalls.size() % 64) smalls.push_back(0.f);
+  };
+  for (uint32_t i = 0; i < c.n_layers; i++) {
+    std::string p = "blk." + std::to_string(i) + ".";
+    Layer& L = m->layers[i];
+    push(vec_f32(g, p + "attn_norm.weight", H), &L.attn_norm);
+    push(vec_f32(g, p + "ffn_norm.weight", H), &L.ffn_norm);
+    std::vector<float> bq = vec_f32(g, p + "attn_q.bias", qd);
+    std::vector<float> bk = vec_f32(g, p + "attn_k.bias", kd), bv = vec_f32(g, p + "attn_v.bias", kd);
+    std::vector<float> b(bq.begin() + (size_t)sl.q_head0 * hd, bq.begin() + (size_t)sl.q_head0 * hd + qd_l);
+    b.insert(b.end(), bk.begin() + (size_t)sl.kv_head0 * hd, bk.begin() + (size_t)sl.kv_head0 * hd + kd_l);
+    b.insert(b.end(), bv.begin() + (size_t)sl.kv_head0 * hd, bv.begin() + (size_t)sl.kv_head0 * hd + kd_l);
+    push(b, &L.bqkv);
+  }
+  push(vec_f32(g, "output_norm.weight", H), &m->out_norm);
+  m->smalls.alloc(smalls.size() * 4);
+  CK(cudaMemcpy(m->smalls.p, smalls.data(), smalls.size() * 4, cudaMemcpyHostToDevice));
+  for (auto& fx : fix) *fx.second = m->smalls.as<float>() + fx.first;
+  // activations
+  m->x.alloc(H * 4);
+  m->qkv.alloc((qd_l + 2 * kd_l) * 4);
+  m->ctx.alloc(qd_l * 4);
+  m->h.alloc(F_l * 4);
+  m->logits.alloc((uint64_t)sl.vocab_pad * 4);
+  CK(cudaMemset(m->logits.p, 0, m->logits.n));
+  auto runs = [&](DevBuf& b, uint32_t n) {
+    b.alloc((uint64_t)runs_for(n) * 64);
+    CK(cudaMemset(b.p, 0, b.n));  // padding records past the vector must read as zero
+  };
+  runs(m->runs_ctx, m->o_w);
+  runs(m->runs_h, F_l);
+  // byte accounting (this rank)
+  m->resident = total + smalls.size() * 4;
+  uint64_t per_tok = m->lm_head.gguf_bytes + m->embd.gguf_bytes / c.vocab + (uint64_t)H * 4;
+  for (auto& L : m->layers)
+    per_tok += L.wq.gguf_bytes + L.wk.gguf_bytes + L.wv.gguf_bytes + L.wo.gguf_bytes + L.wgu.gguf_bytes +
+               L.wd.gguf_bytes + (uint64_t)(2 * H + qd_l + 2 * kd_l) * 4;
+  m->streamed = per_tok;
+  if (world > 1) {
+    need(id != nullptr, "tensor parallelism needs an NCCL id");
+    nccl_check(nccl().CommInitRank(&m->comm, world, *id, rank), "ncclCommInitRank");
+  }
+  // optional timeline of every step kernel's CTAs, written to the named
+  // file by fz_model_free (the records of the last fz_decode_greedy call)
+  if (const char* tp = getenv("FURNACE_B200_TRACE")) {
+    const uint32_t cap = 1u << 20;
+    m->trace.alloc((uint64_t)cap * sizeof(TraceRec));
+    m->trace_path = tp;
+    trace_install(m->trace.as<TraceRec>(), cap);
+  }
+  CK(cudaStreamSynchronize(m->stream));
+  return m;
+}
+
+}  // namespace
+
+extern "C" {
+
 int fz_model_load(const fz_file* f, int tp, const int* device_ids, fz_model** out) {
   return guard([&] {
     need(f && out, "null argument");
-    need(tp == 1, "tensor parallel degree %d not supported by this build (1 only)", tp);
-    const GgufFile& g = *f->g;
-    auto m = std::make_unique<fz_model>();
-    m->cfg = config_from_gguf(g);
-    const fz_config& c = m->cfg;
-    m->device = device_ids ? device_ids[0] : 0;
-    CK(cudaSetDevice(m->device));
-    need(c.head_dim == 64 || c.head_dim == 128, "head_dim %u unsupported (64 or 128)", c.head_dim);
-    need(c.n_kv_heads && c.n_heads % c.n_kv_heads == 0, "%u heads not divisible by %u kv heads", c.n_heads, c.n_kv_heads);
-    need(c.n_heads / c.n_kv_heads <= 8, "GQA group %u > 8 unsupported", c.n_heads / c.n_kv_heads);
-    need(c.hidden % 32 == 0 && c.ffn % 32 == 0, "hidden/ffn must be multiples of 32");
-    CK(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
-    kernels_init();
-    attention_init();
-    uint32_t H = c.hidden, F = c.ffn, qd = c.n_heads * c.head_dim, kd = c.n_kv_heads * c.head_dim;
+    need(tp == 1, "fz_model_load loads one device (tp = 1); use fz_model_load_tp per rank");
+    *out = load_model(f, 0, 1, nullptr, device_ids ? device_ids[0] : 0).release();
+  });
+}
 
-    // tensor table and device sizes
-    struct Plan {
-      const TensorEntry* t;
-      uint64_t rows;
-      uint32_t cols;
-      DevMat* dst;
-      uint64_t row_offset;  // rows already placed (gate/up interleave handled separately)
-    };
-    m->layers.resize(c.n_layers);
-    std::vector<std::pair<const TensorEntry*, DevMat*>> mats;
-    auto add = [&](const std::string& name, uint64_t out_d, uint64_t in_d, DevMat* dst) {
-      const TensorEntry& t = tensor2d(g, name, out_d, in_d);
-      dst->dtype = t.dtype;
-      dst->rows = (uint32_t)out_d;
-      dst->cols = (uint32_t)in_d;
-      dst->stride = dev_row_stride(t.dtype, (uint32_t)in_d);
-      dst->gguf_bytes = gguf_bytes(t.dtype, out_d, (uint32_t)in_d);
-      mats.push_back({&t, dst});
-    };
-    add("token_embd.weight", c.vocab, H, &m->embd);
-    bool tied = g.find("output.weight") == nullptr;
-    if (!tied) add("output.weight", c.vocab, H, &m->lm_head);
-    std::vector<const TensorEntry*> gates(c.n_layers), ups(c.n_layers);
-    for (uint32_t i = 0; i < c.n_layers; i++) {
-      std::string p = "blk." + std::to_string(i) + ".";
-      Layer& L = m->layers[i];
-      add(p + "attn_q.weight", qd, H, &L.wq);
-      add(p + "attn_k.weight", kd, H, &L.wk);
-      add(p + "attn_v.weight", kd, H, &L.wv);
-      add(p + "attn_output.weight", H, qd, &L.wo);
-      add(p + "ffn_down.weight", H, F, &L.wd);
-      gates[i] = &tensor2d(g, p + "ffn_gate.weight", F, H);
-      ups[i] = &tensor2d(g, p + "ffn_up.weight", F, H);
-      need(gates[i]->dtype == ups[i]->dtype, "blk.%u ffn_gate/ffn_up dtypes differ (%u vs %u)", i, gates[i]->dtype,
-           ups[i]->dtype);
-      L.wgu.dtype = gates[i]->dtype;
-      L.wgu.rows = 2 * F;
-      L.wgu.cols = H;
-      L.wgu.stride = dev_row_stride(L.wgu.dtype, H);
-      L.wgu.gguf_bytes = 2 * gguf_bytes(L.wgu.dtype, F, H);
-    }
-    // one pool for every matrix, 256-byte aligned, in the order a decode step
-    // streams them (L2 prefetch runs from one matrix into the next)
-    uint64_t total = 0;
-    auto reserve = [&](DevMat& d) {
-      uint64_t off = total;
-      total = (total + (uint64_t)d.rows * d.stride + 255) & ~uint64_t(255);
-      return off;
-    };
-    std::vector<std::pair<DevMat*, uint64_t>> order;
-    order.push_back({&m->embd, reserve(m->embd)});
-    for (uint32_t i = 0; i < c.n_layers; i++) {
-      Layer& L = m->layers[i];
-      for (DevMat* d : {&L.wq, &L.wk, &L.wv, &L.wo, &L.wgu, &L.wd}) order.push_back({d, reserve(*d)});
-    }
-    if (!tied) order.push_back({&m->lm_head, reserve(m->lm_head)});
-    m->weights.alloc(total);
-    CK(cudaMemset(m->weights.p, 0, total));
-    uint8_t* base = m->weights.as<uint8_t>();
-    for (auto& o : order) o.first->ptr = base + o.second;
-    uint64_t max_raw = 0;
-    for (auto& pm : mats) max_raw = std::max<uint64_t>(max_raw, pm.second->gguf_bytes);
-    DevBuf staging(std::min<uint64_t>(max_raw + 16, 256ull << 20));
-    for (size_t k = 0; k < mats.size(); k++) {
-      DevMat& d = *mats[k].second;
-      uint64_t nb;
-      const uint8_t* raw = g.tensor_data(*mats[k].first, &nb);
-      upload_rows(d.dtype, raw, d.rows, d.cols, d.ptr, staging, m->stream);
-    }
-    // gate/up interleaved by row: row 2i = gate_i, row 2i+1 = up_i
-    {
-      DevBuf tmp(2 * gguf_bytes(gates[0]->dtype, 1, H) * 512 + 16);
-      for (uint32_t i = 0; i < c.n_layers; i++) {
-        DevMat& d = m->layers[i].wgu;
-        uint64_t nb;
-        const uint8_t* graw = g.tensor_data(*gates[i], &nb);
-        const uint8_t* uraw = g.tensor_data(*ups[i], &nb);
-        uint64_t rb = gguf_bytes(d.dtype, 1, H);
-        // host-side interleave in chunks, then repack
-        std::vector<uint8_t> hbuf(rb * 2 * 512);
-        for (uint32_t r0 = 0; r0 < F; r0 += 512) {
-          uint32_t nr = std::min<uint32_t>(512, F - r0);
-          for (uint32_t r = 0; r < nr; r++) {
-            memcpy(&hbuf[(2 * r) * rb], graw + (uint64_t)(r0 + r) * rb, rb);
-            memcpy(&hbuf[(2 * r + 1) * rb], uraw + (uint64_t)(r0 + r) * rb, rb);
-          }
-          CK(cudaMemcpyAsync(tmp.p, hbuf.data(), 2 * nr * rb, cudaMemcpyHostToDevice, m->stream));
-          launch_repack(d.dtype, tmp.as<uint8_t>(), d.ptr, 2 * r0, 2 * nr, d.rows, H, m->stream);
-          CK(cudaStreamSynchronize(m->stream));
-        }
-      }
-    }
-    if (tied) m->lm_head = m->embd;
-    // norms and biases
-    std::vector<float> smalls;
-    std::vector<std::pair<size_t, float**>> fix;
-    auto push = [&](const std::vector<float>& v, float** where) {
-      fix.push_back({smalls.size(), where});
-      smalls.insert(smalls.end(), v.begin(), v.end());
-      while (smalls.size() % 64) smalls.push_back(0.f);
-    };
-    for (uint32_t i = 0; i < c.n_layers; i++) {
-      std::string p = "blk." + std::to_string(i) + ".";
-      Layer& L = m->layers[i];
-      push(vec_f32(g, p + "attn_norm.weight", H), &L.attn_norm);
-      push(vec_f32(g, p + "ffn_norm.weight", H), &L.ffn_norm);
-      std::vector<float> b = vec_f32(g, p + "attn_q.bias", qd);
-      std::vector<float> bk = vec_f32(g, p + "attn_k.bias", kd), bv = vec_f32(g, p + "attn_v.bias", kd);
-      b.insert(b.end(), bk.begin(), bk.end());
-      b.insert(b.end(), bv.begin(), bv.end());
-      push(b, &L.bqkv);
-    }
-    push(vec_f32(g, "output_norm.weight", H), &m->out_norm);
-    m->smalls.alloc(smalls.size() * 4);
-    CK(cudaMemcpy(m->smalls.p, smalls.data(), smalls.size() * 4, cudaMemcpyHostToDevice));
-    for (auto& fx : fix) *fx.second = m->smalls.as<float>() + fx.first;
-    // activations
-    m->x.alloc(H * 4);
-    m->qkv.alloc((qd + 2 * kd) * 4);
-    m->ctx.alloc(qd * 4);
-    m->h.alloc(F * 4);
-    m->logits.alloc((uint64_t)c.vocab * 4);
-    auto runs = [&](DevBuf& b, uint32_t n) {
-      b.alloc((uint64_t)runs_for(n) * 64);
-      CK(cudaMemset(b.p, 0, b.n));  // padding records past the vector must read as zero
-    };
-    runs(m->runs_ctx, qd);
-    runs(m->runs_h, F);
-    // byte accounting
-    m->resident = total + smalls.size() * 4;
-    uint64_t per_tok = m->lm_head.gguf_bytes + m->embd.gguf_bytes / c.vocab + (uint64_t)H * 4;
-    for (auto& L : m->layers)
-      per_tok += L.wq.gguf_bytes + L.wk.gguf_bytes + L.wv.gguf_bytes + L.wo.gguf_bytes + L.wgu.gguf_bytes +
-                 L.wd.gguf_bytes + (uint64_t)(2 * H + qd + 2 * kd) * 4;
-    m->streamed = per_tok;
-    // optional timeline of every step kernel's CTAs, written to the named
-    // file by fz_model_free (the records of the last fz_decode_greedy call)
-    if (const char* tp = getenv("FURNACE_B200_TRACE")) {
-      const uint32_t cap = 1u << 20;
-      m->trace.alloc((uint64_t)cap * sizeof(TraceRec));
-      m->trace_path = tp;
-      trace_install(m->trace.as<TraceRec>(), cap);
-    }
-    CK(cudaStreamSynchronize(m->stream));
-    *out = m.release();
+int fz_model_load_tp(const fz_file* f, int rank, int world, const void* id, size_t n, int device, fz_model** out) {
+  return guard([&] {
+    need(f && out, "null argument");
+    need(world >= 1 && rank >= 0 && rank < world, "rank %d of %d", rank, world);
+    need(world == 1 || (id && n >= sizeof(ncclUniqueId)), "an NCCL id of %zu bytes is required", sizeof(ncclUniqueId));
+    ncclUniqueId uid{};
+    if (world > 1) memcpy(&uid, id, sizeof uid);
+    *out = load_model(f, rank, world, world > 1 ? &uid : nullptr, device).release();
+  });
+}
+
+int fz_tp_unique_id(void* id, size_t n) {
+  return guard([&] {
+    need(id && n >= sizeof(ncclUniqueId), "an id buffer of %zu bytes is required", sizeof(ncclUniqueId));
+    ncclUniqueId uid;
+    nccl_check(nccl().GetUniqueId(&uid), "ncclGetUniqueId");
+    memcpy(id, &uid, sizeof uid);
+  });
+}
+
+int fz_tp_slice_of(const fz_config* c, int rank, int world, fz_tp_slice* out) {
+  return guard([&] {
+    need(c && out, "null argument");
+    *out = tp_slice(*c, rank, world);
   });
 }
 
@@ -697,6 +857,12 @@ void fz_model_free(fz_model* m) {
   if (m->stream) {
     cudaStreamSynchronize(m->stream);
     cudaStreamDestroy(m->stream);
+  }
+  if (m->comm) {
+    try {
+      nccl().CommDestroy(m->comm);
+    } catch (...) {
+    }
   }
   if (m->trace.p) {
     try {
@@ -747,7 +913,7 @@ int fz_kv_new(fz_model* m, uint32_t max_ctx, int kv_dtype, fz_kv** out) {
     auto kv = std::make_unique<fz_kv>();
     kv->m = m;
     kv->max_ctx = max_ctx;
-    uint64_t per = (uint64_t)c.n_layers * c.n_kv_heads * max_ctx * c.head_dim * 4;
+    uint64_t per = (uint64_t)c.n_layers * m->nkv_l * max_ctx * c.head_dim * 4;  // this rank's KV heads
     kv->k.alloc(per);
     kv->v.alloc(per);
     CK(cudaMemset(kv->k.p, 0, per));
@@ -767,8 +933,8 @@ int fz_kv_new(fz_model* m, uint32_t max_ctx, int kv_dtype, fz_kv** out) {
     }
     kv->rope_cs.alloc(cs.size() * 4);
     CK(cudaMemcpy(kv->rope_cs.p, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
-    kv->splits = attention_splits(c.n_kv_heads);
-    kv->partials.alloc(attention_partial_floats(c.n_heads, c.n_kv_heads, c.head_dim, kv->splits) * 4);
+    kv->splits = attention_splits(m->nkv_l);
+    kv->partials.alloc(attention_partial_floats(m->nh_l, m->nkv_l, c.head_dim, kv->splits) * 4);
     // the split-padding entries of the accumulator block are never written
     // and must read as zero (they are weighted by 0 in the merge)
     CK(cudaMemset(kv->partials.p, 0, kv->partials.n));
@@ -809,10 +975,11 @@ int fz_kv_read(const fz_kv* kv, uint32_t layer, int which_v, uint32_t n, float* 
     need(layer < c.n_layers && n <= kv->max_ctx, "kv read out of range");
     use_device(kv->m);
     uint32_t hd = c.head_dim;
-    const float* base = (which_v ? kv->v : kv->k).as<float>() + (uint64_t)layer * c.n_kv_heads * kv->max_ctx * hd;
+    const uint32_t nkv = kv->m->nkv_l;  // this rank's KV heads
+    const float* base = (which_v ? kv->v : kv->k).as<float>() + (uint64_t)layer * nkv * kv->max_ctx * hd;
     // device [kvh][pos][hd] -> host [pos][kvh*hd]
-    for (uint32_t h = 0; h < c.n_kv_heads; h++)
-      CK(cudaMemcpy2D(out + h * hd, (size_t)c.n_kv_heads * hd * 4, base + (uint64_t)h * kv->max_ctx * hd, hd * 4,
+    for (uint32_t h = 0; h < nkv; h++)
+      CK(cudaMemcpy2D(out + h * hd, (size_t)nkv * hd * 4, base + (uint64_t)h * kv->max_ctx * hd, hd * 4,
                       hd * 4, n, cudaMemcpyDeviceToHost));
   });
 }
@@ -831,7 +998,10 @@ int fz_forward(fz_model* m, fz_kv* kv, const uint32_t* tokens, uint32_t n, float
     set_state(kv, kv->len, tokens[0], n);
     for (uint32_t i = 0; i + 1 < n; i++) CK(cudaGraphLaunch(kv->g_layers, s));
     CK(cudaGraphLaunch(kv->g_full, s));
-    if (logits) CK(cudaMemcpyAsync(logits, m->logits.p, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, s));
+    if (logits) {
+      tp_gather_logits(m, s);
+      CK(cudaMemcpyAsync(logits, m->logits.p, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, s));
+    }
     uint32_t id = 0;
     CK(cudaMemcpyAsync(&id, kv->ids.as<uint32_t>() + (n - 1), 4, cudaMemcpyDeviceToHost, s));
     check_state(kv);
@@ -862,9 +1032,11 @@ int fz_decode_greedy(fz_model* m, fz_kv* kv, uint32_t first, uint32_t n_steps, c
       set_state(kv, kv->len, first, 1);
       for (uint32_t i = 0; i < fwd; i++) {
         CK(cudaGraphLaunch(kv->g_full, s));
-        if (logits_out)
+        if (logits_out) {
+          tp_gather_logits(m, s);
           CK(cudaMemcpyAsync(logits_out + (uint64_t)i * m->cfg.vocab, m->logits.p, (size_t)m->cfg.vocab * 4,
                              cudaMemcpyDeviceToHost, s));
+        }
       }
       CK(cudaMemcpyAsync(ids_out + 1, kv->ids.p, (size_t)fwd * 4, cudaMemcpyDeviceToHost, s));
       check_state(kv);
@@ -929,7 +1101,7 @@ int fz_step_profile(fz_model* m, fz_kv* kv, uint32_t first, uint32_t reps, doubl
     check_state(kv);
     // algorithmic bytes per op kind
     const fz_config& c = m->cfg;
-    uint64_t H = c.hidden, F = c.ffn, qd = (uint64_t)c.n_heads * c.head_dim, kd = (uint64_t)c.n_kv_heads * c.head_dim;
+    uint64_t H = c.hidden, F = m->sl.ffn_n, qd = m->qd_l, kd = m->kd_l;  // this rank's widths
     for (uint32_t r = 0; r < reps; r++) {
       uint64_t pos = kv->len + r;
       bytes[FZ_OP_EMBED] += m->embd.gguf_bytes / c.vocab + H * 4;

@@ -113,6 +113,34 @@ int fz_model_bytes(const fz_model* m, uint64_t* resident, uint64_t* streamed_per
  * so a caller can order its own work or record timing events on it. */
 int fz_model_stream(const fz_model* m, void** stream, int* device);
 
+/* ---- Tensor parallelism (one process per GPU, NCCL) ----------------------
+ * No counterpart in the reference, which runs one process on one device: a
+ * rank loads its share of what Model::load (src/model.rs:520-552) loads and
+ * all ranks step together, each calling the same fz_forward /
+ * fz_decode_greedy sequence with the same tokens.  Split (Megatron style):
+ * q/k/v rows by query / KV head (attention and the KV cache stay local),
+ * o_proj input columns by the rank's heads, gate/up rows and down input
+ * columns by an FFN slice on 256-element boundaries, lm_head rows by
+ * vocabulary slice; the residual stream is summed across ranks by an NCCL
+ * all-reduce after o_proj and after down, and the greedy argmax by an
+ * all-reduce (max) of the packed (logit, index) key.  Needs n_heads and
+ * n_kv_heads divisible by world. */
+typedef struct fz_tp_slice {
+  uint32_t q_head0, q_heads;   /* query heads of this rank */
+  uint32_t kv_head0, kv_heads; /* KV heads (and KV cache) of this rank */
+  uint32_t o_col0, o_cols;     /* o_proj input columns = this rank's ctx */
+  uint32_t ffn0, ffn_n;        /* FFN slice: gate/up rows, down input columns */
+  uint32_t vocab0, vocab_n;    /* lm_head rows (all slices vocab_pad / world long) */
+  uint32_t vocab_pad;
+} fz_tp_slice;
+int fz_tp_slice_of(const fz_config* c, int rank, int world, fz_tp_slice* out);
+/* An NCCL unique id (n >= 128 bytes): made once (rank 0) and given to every
+ * rank's fz_model_load_tp. */
+int fz_tp_unique_id(void* id, size_t n);
+/* Model::load for rank `rank` of `world` on CUDA device `device`; joins the
+ * ranks' NCCL communicator (collective: every rank must call it). */
+int fz_model_load_tp(const fz_file* f, int rank, int world, const void* id, size_t n, int device, fz_model** out);
+
 /* KvCache::new (src/model.rs:330-339): max_ctx positions, f32 elements. */
 int fz_kv_new(fz_model* m, uint32_t max_ctx, int kv_dtype, fz_kv** out);
 void fz_kv_free(fz_kv* kv);
@@ -121,7 +149,8 @@ void fz_kv_free(fz_kv* kv);
 int fz_kv_len(const fz_kv* kv, uint32_t* len);
 int fz_kv_set_len(fz_kv* kv, uint32_t len);
 /* Copy layer `layer`'s cached K (which_v = 0) or V rows [0, n) to the host
- * as [n, n_kv_heads*head_dim] f32 (the reference's row layout). */
+ * as [n, n_kv_heads*head_dim] f32 (the reference's row layout); under tensor
+ * parallelism, this rank's KV heads ([n, kv_heads*head_dim]). */
 int fz_kv_read(const fz_kv* kv, uint32_t layer, int which_v, uint32_t n, float* out);
 
 /* Model::forward_cached (src/model.rs:579-592): run the tokens at positions

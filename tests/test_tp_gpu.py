@@ -1,0 +1,103 @@
+"""Tensor-parallel decode on 2 GPUs against the CPU oracle (one process per
+GPU, NCCL inside the library, gloo only to hand out the NCCL id and to
+collect results).  Needs two visible GPUs; skipped otherwise.
+
+Bars as for one GPU: greedy ids identical to the oracle at every step,
+logits within 1e-3 max-abs with identical argmax and top-5."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import furnace_b200 as fz
+from furnace_b200 import synth
+
+pytestmark = pytest.mark.gpu
+LOGIT_ABS = 1e-3
+
+
+def _ngpus():
+    try:
+        import torch
+
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def _rank(rank, world, port, path, n_prompt, n_new, q):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ids = [fz.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(ids, src=0)
+        f = fz.GgufFile.open(path)
+        m = fz.Model.load_tp(f, rank, world, ids[0], rank)
+        prompt = synth.prompt_ids(m.config.vocab, n_prompt, seed=2)
+        got_ids, got_lg = fz.generate(m, prompt, n_new, max_ctx=n_prompt + n_new, keep_logits=True)
+        q.put((rank, got_ids.tolist(), got_lg if rank == 0 else None))
+        m.close()
+        dist.barrier()
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, repr(e), None))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_tp(path, n_prompt, n_new, world=2):
+    import torch.multiprocessing as mp
+
+    from oracle import oracle
+
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, path, n_prompt, n_new, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(world):
+            r, ids, lg = q.get(timeout=600)
+            res[r] = (ids, lg)
+    finally:
+        for p in procs:
+            p.join(60)
+            if p.is_alive():
+                p.kill()
+    for r in range(world):
+        assert isinstance(res[r][0], list), f"rank {r}: {res[r][0]}"
+    ref = oracle.Model(path)
+    prompt = synth.prompt_ids(ref.vocab, n_prompt, seed=2)
+    want_ids, want_lg, _, _ = ref.generate(prompt, n_new, keep_logits=True)
+    for r in range(world):
+        assert res[r][0] == want_ids.tolist(), f"rank {r} ids differ"
+    got_lg = res[0][1]
+    for s in range(len(want_ids)):
+        err = np.abs(got_lg[s] - want_lg[s]).max()
+        assert err <= LOGIT_ABS, f"step {s}: logits max-abs {err}"
+        gt, wt = np.argsort(-got_lg[s], kind="stable")[:5], np.argsort(-want_lg[s], kind="stable")[:5]
+        assert gt.tolist() == wt.tolist(), f"step {s}: top-5"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _two_gpus():
+    if _ngpus() < 2:
+        pytest.skip("tensor parallelism needs two GPUs")
+
+
+def test_tp2_greedy_tiny(tmp_path):
+    path = synth.write(synth.spec("tiny"), str(tmp_path / "tiny.gguf"))
+    _run_tp(path, 9, 64)
+
+
+@pytest.mark.slow
+def test_tp2_greedy_c1():
+    """configs[0] (Q8_0, 14 heads / 2 KV heads) split over 2 GPUs, 128 steps."""
+    _run_tp(synth.ensure("c1"), 32, 128)
