@@ -1582,6 +1582,76 @@ void launch_step(const StepLaunch& L, const StepPlan& plan, const void* plan_dev
   CK(cudaLaunchKernelEx(&cfg, k_step, P));
 }
 
+// ---------------------------------------------------------------------------
+// Prefill on the tensor cores
+// ---------------------------------------------------------------------------
+#include "prefill.cuh"
+
+void prefill_init() {
+  CK(cudaFuncSetAttribute(k_qgemm, cudaFuncAttributeMaxDynamicSharedMemorySize, QG_SMEM));
+  CK(cudaFuncSetAttribute(k_attn_prefill<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, attention_smem(128)));
+  CK(cudaFuncSetAttribute(k_attn_prefill<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, attention_smem(64)));
+}
+
+uint64_t wpanel_elems(uint32_t rows, uint32_t K) { return (uint64_t)((rows + QG_M - 1) / QG_M) * QG_M * K; }
+uint64_t xpanel_elems(uint32_t T, uint32_t K) { return (uint64_t)((T + QG_N - 1) / QG_N) * QG_N * K; }
+
+void launch_wpanels(const DevMat& m, uint32_t row0, void* hi, void* lo, cudaStream_t s) {
+  if (m.cols % 64) fail(FZ_EINVAL, "prefill: %u columns not a multiple of 64", m.cols);
+  const uint64_t n = (uint64_t)m.rows * (m.cols / 64);
+  k_wpanels<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(m, row0, reinterpret_cast<__half*>(hi),
+                                                        reinterpret_cast<__half*>(lo));
+  CK(cudaGetLastError());
+}
+
+void launch_xpanels(const float* x, uint32_t ld, uint32_t T, uint32_t K, const float* w, float eps, void* hi,
+                    void* lo, cudaStream_t s) {
+  if (K % 64) fail(FZ_EINVAL, "prefill: width %u not a multiple of 64", K);
+  k_xpanels<<<T, 256, 0, s>>>(x, ld, K, w, eps, reinterpret_cast<__half*>(hi), reinterpret_cast<__half*>(lo));
+  CK(cudaGetLastError());
+}
+
+void launch_qgemm(const QgemmLaunch& q, cudaStream_t s) {
+  if (q.K % QG_KB || q.K == 0) fail(FZ_EINVAL, "prefill gemm: K %u not a multiple of %u", q.K, QG_KB);
+  QgParams p{};
+  p.ahi = reinterpret_cast<const __half*>(q.ahi);
+  p.alo = reinterpret_cast<const __half*>(q.alo);
+  p.bhi = reinterpret_cast<const __half*>(q.bhi);
+  p.blo = reinterpret_cast<const __half*>(q.blo);
+  p.K = q.K;
+  p.N = q.N;
+  p.T = q.T;
+  p.epi = q.epi;
+  p.out = q.out;
+  p.ld = q.ld;
+  p.bias = q.bias;
+  p.err = q.err;
+  dim3 grid((q.N + QG_M - 1) / QG_M, (q.T + QG_N - 1) / QG_N);
+  k_qgemm<<<grid, 128, QG_SMEM, s>>>(p);
+  CK(cudaGetLastError());
+}
+
+void launch_embed_rows(const DevMat& emb, const uint32_t* tokens, uint32_t T, float* x, uint32_t ld, cudaStream_t s) {
+  const uint32_t U = emb.cols / 64;
+  k_embed_rows<<<dim3((U + 63) / 64, T), 64, 0, s>>>(emb, tokens, x, ld);
+  CK(cudaGetLastError());
+}
+
+void launch_prefill_attention(const float* qkv, uint32_t ldq, const float* rope_cs, float* kc, float* vc, float* ctx,
+                              uint32_t ldc, uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t max_ctx, uint32_t pos0,
+                              uint32_t T, uint32_t* err, cudaStream_t s) {
+  const float2* cs = reinterpret_cast<const float2*>(rope_cs);
+  k_kv_append<<<dim3(T, nkv), 64, 0, s>>>(qkv, ldq, nh, nkv, hd, cs, kc, vc, max_ctx, pos0);
+  CK(cudaGetLastError());
+  if (hd == 128)
+    k_attn_prefill<128><<<dim3(T, nkv), AT_THREADS, attention_smem(128), s>>>(qkv, ldq, cs, kc, vc, ctx, ldc, nh, nkv,
+                                                                               max_ctx, pos0, err);
+  else
+    k_attn_prefill<64><<<dim3(T, nkv), AT_THREADS, attention_smem(64), s>>>(qkv, ldq, cs, kc, vc, ctx, ldc, nh, nkv,
+                                                                             max_ctx, pos0, err);
+  CK(cudaGetLastError());
+}
+
 void step_init() { CK(cudaFuncSetAttribute(k_step, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM)); }
 
 }  // namespace fz

@@ -150,4 +150,28 @@ StepPlan step_plan_build(const StepLaunch& L);
 void launch_step(const StepLaunch& L, const StepPlan& plan, const void* plan_dev, cudaStream_t s);
 void step_init();
 
+// ---- prefill on the tensor cores (prefill.cuh) -------------------------------
+enum PrefillEpilogue : int { PE_STORE = 0, PE_RESID = 1, PE_SWIGLU = 2 };
+struct QgemmLaunch {
+  const void *ahi, *alo;  // weight panels (launch_wpanels)
+  const void *bhi, *blo;  // token panels (launch_xpanels)
+  uint32_t K, N, T;
+  int epi;                // PE_*: out[t*ld + r] (+ bias[r]); += ; SwiGLU into out[t*ld + r/2]
+  float* out;
+  uint32_t ld;
+  const float* bias;
+  uint32_t* err;          // device word, nonzero if a bounded wait ran out
+};
+void prefill_init();
+uint64_t wpanel_elems(uint32_t rows, uint32_t K);  // fp16 elements of one weight panel set
+uint64_t xpanel_elems(uint32_t T, uint32_t K);
+void launch_wpanels(const DevMat& m, uint32_t row0, void* hi, void* lo, cudaStream_t s);
+void launch_xpanels(const float* x, uint32_t ld, uint32_t T, uint32_t K, const float* w, float eps, void* hi,
+                    void* lo, cudaStream_t s);
+void launch_qgemm(const QgemmLaunch& q, cudaStream_t s);
+void launch_embed_rows(const DevMat& emb, const uint32_t* tokens, uint32_t T, float* x, uint32_t ld, cudaStream_t s);
+void launch_prefill_attention(const float* qkv, uint32_t ldq, const float* rope_cs, float* kc, float* vc, float* ctx,
+                              uint32_t ldc, uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t max_ctx, uint32_t pos0,
+                              uint32_t T, uint32_t* err, cudaStream_t s);
+
 }  // namespace fz

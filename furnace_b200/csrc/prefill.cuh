@@ -1,0 +1,406 @@
+// Prefill on the tensor cores: batched forward of a run of prompt tokens.
+// Included by kernels.cu (shares dequant_unit and the bulk-copy / mbarrier
+// helpers).
+//
+// Every matrix product of a prefill chunk of T tokens is Y[T, N] = X[T, K] W^T
+// with W quantized.  The reference computes it in f32 (src/tensor.rs:86-136);
+// here:
+//   * W is dequantized exactly (dequant_unit, the reference's arithmetic) and
+//     split into fp16 hi and lo' = (w - hi) * 2^11, stored as "panels";
+//   * X (after RMSNorm where the layer applies one) is split the same way;
+//   * tcgen05.mma (kind::f16, f32 accumulation in tensor memory) forms
+//     hi.hi in one accumulator and hi.lo' + lo'.hi in another; the epilogue
+//     adds them as acc1 + acc2 * 2^-11.  The dropped lo.lo term is ~2^-22 of
+//     each product, so the result carries about 22 significant bits.
+//
+// Panel layout (UMMA K-major, no swizzle): a matrix of R rows and K columns
+// (K a multiple of 64, R padded to the panel height P = 128 for weights or
+// 256 for tokens) is stored as panels of P rows x 64 columns, panel (b, kb)
+// at index b * (K / 64) + kb.  Inside a panel the 8-row x 8-element core
+// matrix (rg, kc) sits at byte (kc * P/8 + rg) * 128 and row i of it at
+// +16 i: leading-byte offset (between k-chunks) P/8 * 128, stride-byte
+// offset (between row groups) 128.  One MMA (K = 16) reads k-chunks 2s and
+// 2s + 1 of a panel.
+
+constexpr uint32_t QG_M = 128;          // weight rows per CTA (UMMA M)
+constexpr uint32_t QG_N = 256;          // tokens per CTA (UMMA N)
+constexpr uint32_t QG_KB = 64;          // K per stage
+constexpr uint32_t QG_STAGES = 2;
+constexpr uint32_t QG_APANEL = QG_M * QG_KB * 2;   // bytes of one A panel (16 KB)
+constexpr uint32_t QG_BPANEL = QG_N * QG_KB * 2;   // bytes of one B panel (32 KB)
+constexpr uint32_t QG_STAGE = 2 * QG_APANEL + 2 * QG_BPANEL;
+constexpr uint32_t QG_SMEM = QG_STAGES * QG_STAGE + 1024;
+constexpr float QG_LO = 2048.0f;        // lo' = (x - hi) * QG_LO
+
+enum : int { QE_STORE = 0, QE_RESID = 1, QE_SWIGLU = 2 };
+
+__host__ __device__ __forceinline__ uint32_t panel_elem(uint32_t P, uint32_t rr, uint32_t k) {
+  return ((k >> 3) * (P >> 3) + (rr >> 3)) * 64 + (rr & 7) * 8 + (k & 7);  // in fp16 elements
+}
+
+__device__ __forceinline__ void split16(float v, __half* hi, __half* lo) {
+  const __half h = __float2half_rn(v);
+  *hi = h;
+  *lo = __float2half_rn(__fmul_rn(__fsub_rn(v, __half2float(h)), QG_LO));
+}
+
+// W (chunk-planar) rows -> hi/lo panels at rows row0.. of a panel matrix of
+// K = m.cols columns.  One thread per (row, 64-column unit).
+__global__ void k_wpanels(DevMat m, uint32_t row0, __half* __restrict__ hi, __half* __restrict__ lo) {
+  const uint32_t U = m.cols / 64;
+  const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (uint64_t)m.rows * U) return;
+  const uint32_t r = (uint32_t)(idx / U), u = (uint32_t)(idx % U);
+  float v[64];
+  dequant_unit(m.dtype, m.ptr, m.rows, r, m.cols, u, v - 64 * u);
+  const uint32_t R = row0 + r, panel = (R / QG_M) * U + u;
+  __half* ph = hi + (uint64_t)panel * (QG_M * QG_KB);
+  __half* pl = lo + (uint64_t)panel * (QG_M * QG_KB);
+#pragma unroll 8
+  for (uint32_t k = 0; k < 64; k++) {
+    const uint32_t e = panel_elem(QG_M, R % QG_M, k);
+    split16(v[k], ph + e, pl + e);
+  }
+}
+
+// X [T, K] f32 (row stride ld) -> hi/lo token panels (P = QG_N), optionally
+// RMS-normalised per row with weight w (src/tensor.rs:164-186).  One block
+// per token; tokens T.. up to the panel padding are never written (zeroed
+// once at allocation).
+__global__ void k_xpanels(const float* __restrict__ x, uint32_t ld, uint32_t K, const float* __restrict__ w,
+                          float eps, __half* __restrict__ hi, __half* __restrict__ lo) {
+  const uint32_t t = blockIdx.x, tid = threadIdx.x;
+  const float* row = x + (uint64_t)t * ld;
+  __shared__ float red[32];
+  float inv = 1.f;
+  if (w) {
+    float ss = 0.f;
+    for (uint32_t k = tid; k < K; k += blockDim.x) ss = fmaf(row[k], row[k], ss);
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    if (tid < 32) {
+      float s2 = tid < blockDim.x / 32 ? red[tid] : 0.f;
+      for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      if (tid == 0) red[0] = s2;
+    }
+    __syncthreads();
+    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], (float)K), eps)));
+  }
+  const uint32_t U = K / 64;
+  for (uint32_t k = tid; k < K; k += blockDim.x) {
+    float v = row[k];
+    if (w) v = __fmul_rn(__fmul_rn(v, inv), w[k]);
+    const uint64_t panel = (uint64_t)(t / QG_N) * U + k / 64;
+    const uint64_t e = panel * (QG_N * QG_KB) + panel_elem(QG_N, t % QG_N, k % 64);
+    split16(v, hi + e, lo + e);
+  }
+}
+
+// ---- tcgen05 helpers ----------------------------------------------------------
+__device__ __forceinline__ uint64_t umma_desc(const void* smem_ptr, uint32_t lbo, uint32_t sbo) {
+  const uint32_t a = smem_u32(smem_ptr);
+  uint64_t d = 0;
+  d |= (uint64_t)((a >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version (Blackwell)
+  // base offset 0, leading-byte-offset mode 0, layout type 0 (no swizzle)
+  return d;
+}
+// kind::f16, A = B = f16 (K-major), D = f32, M = 128, N = QG_N
+constexpr uint32_t QG_IDESC = (1u << 4) | ((QG_N >> 3) << 17) | ((QG_M >> 4) << 24);
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(QG_IDESC), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
+}
+
+struct QgParams {
+  const __half* ahi;  // weight panels [Np/128][K/64]
+  const __half* alo;
+  const __half* bhi;  // token panels [Tp/256][K/64]
+  const __half* blo;
+  uint32_t K, N, T;   // true weight rows N and tokens T
+  int epi;
+  float* out;         // STORE / RESID: out[t * ld + r]; SWIGLU: out[t * ld + r / 2]
+  uint32_t ld;
+  const float* bias;  // STORE: + bias[r]
+  uint32_t* err;      // set nonzero if a bounded wait ran out
+};
+
+// Y^T tile [128 weight rows x 256 tokens] of one CTA.  Warp 0 lane 0 copies
+// panels into a two-stage ring, warp 1 lane 0 issues the MMAs, warp 2 owns
+// the tensor memory (512 columns: two f32 accumulators of 256 columns), all
+// four warps read the accumulators back (warp w: rows 32w..32w+31).
+__global__ void __launch_bounds__(128, 1) k_qgemm(const __grid_constant__ QgParams p) {
+  extern __shared__ __align__(1024) uint8_t qsm[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(qsm) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[QG_STAGES], empty[QG_STAGES], done;
+  __shared__ uint32_t tmem_base;
+  __shared__ volatile uint32_t fail;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rb = blockIdx.x, tb = blockIdx.y, KB = p.K / QG_KB;
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < QG_STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done, 1);
+    fail = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&tmem_base))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = tmem_base;
+
+  if (warp == 0 && lane == 0) {
+    // ---- producer ----
+    const uint8_t* ah = reinterpret_cast<const uint8_t*>(p.ahi) + (uint64_t)rb * KB * QG_APANEL;
+    const uint8_t* al = reinterpret_cast<const uint8_t*>(p.alo) + (uint64_t)rb * KB * QG_APANEL;
+    const uint8_t* bh = reinterpret_cast<const uint8_t*>(p.bhi) + (uint64_t)tb * KB * QG_BPANEL;
+    const uint8_t* bl = reinterpret_cast<const uint8_t*>(p.blo) + (uint64_t)tb * KB * QG_BPANEL;
+    for (uint32_t kb = 0; kb < KB; kb++) {
+      const uint32_t s = kb % QG_STAGES;
+      if (kb >= QG_STAGES && !mbar_wait(&empty[s], ((kb / QG_STAGES) - 1) & 1)) {
+        fail = 1;
+        break;
+      }
+      uint8_t* st = sm + s * QG_STAGE;
+      mbar_expect_tx(&full[s], QG_STAGE);
+      bulk_g2s(st, ah + (uint64_t)kb * QG_APANEL, QG_APANEL, &full[s], 0ull);
+      bulk_g2s(st + QG_APANEL, al + (uint64_t)kb * QG_APANEL, QG_APANEL, &full[s], 0ull);
+      bulk_g2s(st + 2 * QG_APANEL, bh + (uint64_t)kb * QG_BPANEL, QG_BPANEL, &full[s], 0ull);
+      bulk_g2s(st + 2 * QG_APANEL + QG_BPANEL, bl + (uint64_t)kb * QG_BPANEL, QG_BPANEL, &full[s], 0ull);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    const uint32_t acc1 = tm, acc2 = tm + QG_N;
+    bool ok = true;
+    for (uint32_t kb = 0; kb < KB && ok; kb++) {
+      const uint32_t s = kb % QG_STAGES;
+      if (!mbar_wait(&full[s], (kb / QG_STAGES) & 1)) {
+        fail = 1;
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint8_t* st = sm + s * QG_STAGE;
+#pragma unroll
+      for (uint32_t k = 0; k < QG_KB / 16; k++) {
+        const uint64_t a_h = umma_desc(st + k * 2 * (QG_M / 8) * 128, (QG_M / 8) * 128, 128);
+        const uint64_t a_l = umma_desc(st + QG_APANEL + k * 2 * (QG_M / 8) * 128, (QG_M / 8) * 128, 128);
+        const uint64_t b_h = umma_desc(st + 2 * QG_APANEL + k * 2 * (QG_N / 8) * 128, (QG_N / 8) * 128, 128);
+        const uint64_t b_l =
+            umma_desc(st + 2 * QG_APANEL + QG_BPANEL + k * 2 * (QG_N / 8) * 128, (QG_N / 8) * 128, 128);
+        const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+        umma_f16(acc1, a_h, b_h, accum);
+        umma_f16(acc2, a_h, b_l, accum);
+        umma_f16(acc2, a_l, b_h, 1u);
+      }
+      umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+    }
+    if (ok) umma_commit(&done);
+  }
+  __syncwarp();
+  // ---- epilogue: accumulators -> outputs ----
+  bool ok = mbar_wait(&done, 0) && fail == 0;
+  if (!ok && threadIdx.x == 0) atomicExch(p.err, 1u);
+  tc_fence_after();
+  const uint32_t r = rb * QG_M + warp * 32 + lane;
+  if (ok) {
+    const uint32_t lanebase = (warp * 32) << 16;
+    for (uint32_t c = 0; c < QG_N; c += 8) {
+      float a1[8], a2[8];
+      tmem_ld8(tm + lanebase + c, a1);
+      tmem_ld8(tm + lanebase + QG_N + c, a2);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const uint32_t t = tb * QG_N + c + j;
+        const float y = __fadd_rn(a1[j], __fmul_rn(a2[j], 1.0f / QG_LO));
+        if (p.epi == QE_SWIGLU) {
+          // rows interleave gate (even) / up (odd): h = silu(g) * u (src/tensor.rs:213-227)
+          const float other = __shfl_xor_sync(0xffffffffu, y, 1);
+          if ((lane & 1) == 0 && t < p.T && r < p.N) {
+            const float g = y, u = other;
+            p.out[(uint64_t)t * p.ld + r / 2] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+          }
+        } else if (t < p.T && r < p.N) {
+          float* o = p.out + (uint64_t)t * p.ld + r;
+          if (p.epi == QE_STORE)
+            *o = p.bias ? __fadd_rn(y, p.bias[r]) : y;
+          else
+            *o = __fadd_rn(*o, y);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tm) : "memory");
+}
+
+// KV append for a prefill chunk: rotated k and v of tokens t < T at
+// positions pos0 + t (src/model.rs:193-217, 340-352).  Grid (T, n_kv).
+__global__ void k_kv_append(const float* __restrict__ qkv, uint32_t ldq, uint32_t nh, uint32_t nkv, uint32_t hd,
+                            const float2* __restrict__ cs, float* __restrict__ kc, float* __restrict__ vc,
+                            uint32_t max_ctx, uint32_t pos0) {
+  const uint32_t t = blockIdx.x, h = blockIdx.y, half = hd / 2, pos = pos0 + t;
+  const float* k = qkv + (uint64_t)t * ldq + (uint64_t)nh * hd + (uint64_t)h * hd;
+  const float* v = qkv + (uint64_t)t * ldq + (uint64_t)(nh + nkv) * hd + (uint64_t)h * hd;
+  float* kd = kc + ((uint64_t)h * max_ctx + pos) * hd;
+  float* vd = vc + ((uint64_t)h * max_ctx + pos) * hd;
+  const float2* c = cs + (uint64_t)pos * half;
+  for (uint32_t i = threadIdx.x; i < half; i += blockDim.x) {
+    const float a = k[i], b = k[i + half];
+    const float2 cc = c[i];
+    kd[i] = __fsub_rn(__fmul_rn(a, cc.x), __fmul_rn(b, cc.y));
+    kd[i + half] = __fadd_rn(__fmul_rn(a, cc.y), __fmul_rn(b, cc.x));
+    vd[i] = v[i];
+    vd[i + half] = v[i + half];
+  }
+}
+
+// Causal attention of prefill token t (position pos0 + t) over the cache
+// [0, pos0 + t] for the G query heads of KV head kvh (src/model.rs:371-438):
+// grid (T, n_kv), warp per head, 32-position tiles through bulk copies.
+template <int HD>
+__global__ void __launch_bounds__(AT_THREADS) k_attn_prefill(const float* __restrict__ qkv, uint32_t ldq,
+                                                              const float2* __restrict__ cs,
+                                                              const float* __restrict__ kc,
+                                                              const float* __restrict__ vc, float* __restrict__ ctx,
+                                                              uint32_t ldc, uint32_t nh, uint32_t nkv,
+                                                              uint32_t max_ctx, uint32_t pos0, uint32_t* err) {
+  constexpr int DPL = HD / 32;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(16) float qs[AT_MAXG][HD];
+  __shared__ __align__(8) uint64_t bar[AT_NBUF];
+  const uint32_t G = nh / nkv, t = blockIdx.x, kvh = blockIdx.y;
+  const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, half = HD / 2;
+  const uint32_t pos = pos0 + t, n = pos + 1, ntiles = (n + AT_TP - 1) / AT_TP;
+  float* tiles = reinterpret_cast<float*>(smem);
+  const float* kvk = kc + (uint64_t)kvh * max_ctx * HD;
+  const float* kvv = vc + (uint64_t)kvh * max_ctx * HD;
+  if (tid == 0) {
+    for (int b = 0; b < AT_NBUF; b++) mbar_init(&bar[b], 1);
+    fence_barrier_init();
+  }
+  const uint64_t pol = policy_evict_first();
+  auto issue = [&](uint32_t j) {
+    const uint32_t b = j % AT_NBUF, a = j * AT_TP, rows = min(n, a + AT_TP) - a;
+    float* kt = tiles + (size_t)b * 2 * AT_TP * HD;
+    mbar_expect_tx(&bar[b], 2 * rows * HD * 4);
+    bulk_g2s(kt, kvk + (uint64_t)a * HD, rows * HD * 4, &bar[b], pol);
+    bulk_g2s(kt + AT_TP * HD, kvv + (uint64_t)a * HD, rows * HD * 4, &bar[b], pol);
+  };
+  __syncthreads();
+  if (tid == 0)
+    for (uint32_t j = 0; j < ntiles && j < (uint32_t)AT_NBUF; j++) issue(j);
+  const float2* csp = cs + (uint64_t)pos * half;
+  for (uint32_t idx = tid; idx < G * half; idx += AT_THREADS) {
+    const uint32_t h = idx / half, i = idx % half;
+    const float* x = qkv + (uint64_t)t * ldq + (uint64_t)(kvh * G + h) * HD;
+    const float a = x[i], b = x[i + half];
+    const float2 c = csp[i];
+    qs[h][i] = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
+    qs[h][i + half] = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
+  }
+  __syncthreads();
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+  float m = -INFINITY, l = 0.f, acc[DPL];
+#pragma unroll
+  for (int d = 0; d < DPL; d++) acc[d] = 0.f;
+  bool ok = true;
+  for (uint32_t j = 0; j < ntiles; j++) {
+    const uint32_t b = j % AT_NBUF, tn = min(n, j * AT_TP + AT_TP) - j * AT_TP;
+    const float* kt = tiles + (size_t)b * 2 * AT_TP * HD;
+    const float* vt = kt + AT_TP * HD;
+    if (!mbar_wait(&bar[b], (j / AT_NBUF) & 1)) {
+      ok = false;
+      break;
+    }
+    if (warp < G) {
+      const uint32_t tt = lane;
+      float s = -INFINITY;
+      if (tt < tn) {
+        const float4* kr = reinterpret_cast<const float4*>(kt + (size_t)tt * HD);
+        const float4* qr = reinterpret_cast<const float4*>(qs[warp]);
+        float dsum = 0.f;
+#pragma unroll 8
+        for (uint32_t c = 0; c < HD / 4; c++) {
+          const uint32_t cc = (c + tt) & (HD / 4 - 1);
+          const float4 k4 = kr[cc], q4 = qr[cc];
+          dsum = fmaf(q4.x, k4.x, dsum);
+          dsum = fmaf(q4.y, k4.y, dsum);
+          dsum = fmaf(q4.z, k4.z, dsum);
+          dsum = fmaf(q4.w, k4.w, dsum);
+        }
+        s = __fmul_rn(dsum, scale);
+      }
+      float mt = s;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+      const float mn = fmaxf(m, mt);
+      const float alpha = expf(m - mn);
+      const float pr = tt < tn ? expf(s - mn) : 0.f;
+      float ps = pr;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      l = fmaf(l, alpha, ps);
+      m = mn;
+#pragma unroll
+      for (int d = 0; d < DPL; d++) acc[d] *= alpha;
+      for (uint32_t t2 = 0; t2 < tn; t2++) {
+        const float pt = __shfl_sync(0xffffffffu, pr, t2);
+        const float* vr = vt + (size_t)t2 * HD + lane * DPL;
+#pragma unroll
+        for (int d = 0; d < DPL; d++) acc[d] = fmaf(pt, vr[d], acc[d]);
+      }
+    }
+    __syncthreads();  // buffer b free
+    if (tid == 0 && j + AT_NBUF < ntiles) issue(j + AT_NBUF);
+  }
+  if (!ok) {
+    if (tid == 0) atomicExch(err, 2u);
+    return;
+  }
+  if (warp < G) {
+    float* o = ctx + (uint64_t)t * ldc + (uint64_t)(kvh * G + warp) * HD + lane * DPL;
+#pragma unroll
+    for (int d = 0; d < DPL; d++) o[d] = __fdiv_rn(acc[d], l);
+  }
+}
+
+// x[t] += embedding rows: x[t] = dequant row(tokens[t]) (src/model.rs:482-506).
+__global__ void k_embed_rows(DevMat emb, const uint32_t* __restrict__ tokens, float* __restrict__ x, uint32_t ld) {
+  const uint32_t t = blockIdx.y, U = emb.cols / 64, u = blockIdx.x * blockDim.x + threadIdx.x;
+  if (u >= U) return;
+  const uint32_t tok = tokens[t];
+  if (tok >= emb.rows) return;  // the host validates ids
+  dequant_unit(emb.dtype, emb.ptr, emb.rows, tok, emb.cols, u, x + (uint64_t)t * ld);
+}

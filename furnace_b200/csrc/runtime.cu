@@ -91,6 +91,10 @@ struct fz_model {
   uint32_t nh_l = 0, nkv_l = 0, qd_l = 0, kd_l = 0;
   std::vector<uint32_t> o_off;  // per layer: ctx[0]'s column within o_proj's block-aligned input
   uint32_t o_w = 0;             // widest o_proj input (run records of ctx cover it)
+  // batched prefill (tensor cores): activations of up to pf_cap tokens, the
+  // fp16 hi/lo panels of one weight and of one activation matrix
+  uint32_t pf_cap = 0;
+  DevBuf pf_x, pf_qkv, pf_ctx, pf_h, pf_tok, pf_err, pf_wh, pf_wl, pf_xh, pf_xl;
 };
 
 struct fz_kv {
@@ -368,6 +372,103 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
   H(FZ_OP_FINALIZE, true);
   launch_finalize(st, kv->forced.as<uint32_t>(), kv->ids.as<uint32_t>(), with_logits, s);
   H(FZ_OP_FINALIZE, false);
+}
+
+// ---- batched prefill on the tensor cores ------------------------------------
+constexpr uint32_t PF_CHUNK = 1024;  // tokens per prefill pass
+constexpr uint32_t PF_MIN = 8;       // shorter prompts replay the decode step
+
+bool prefill_supported(const fz_model* m) {
+  const fz_config& c = m->cfg;
+  return m->world == 1 && c.hidden % 64 == 0 && c.ffn % 64 == 0 && (c.n_heads * c.head_dim) % 64 == 0;
+}
+
+void prefill_alloc(fz_model* m, uint32_t T) {
+  if (m->pf_cap >= T) return;
+  const fz_config& c = m->cfg;
+  const uint32_t H = c.hidden, F = c.ffn, qd = m->qd_l, kd = m->kd_l;
+  const uint32_t maxK = std::max(std::max(H, F), qd);
+  uint64_t wmax = 0;
+  for (auto& L : m->layers) {
+    wmax = std::max(wmax, wpanel_elems(L.wq.rows + L.wk.rows + L.wv.rows, H));
+    wmax = std::max(wmax, wpanel_elems(L.wo.rows, L.wo.cols));
+    wmax = std::max(wmax, wpanel_elems(L.wgu.rows, H));
+    wmax = std::max(wmax, wpanel_elems(L.wd.rows, L.wd.cols));
+  }
+  m->pf_x.alloc((uint64_t)T * H * 4);
+  m->pf_qkv.alloc((uint64_t)T * (qd + 2 * kd) * 4);
+  m->pf_ctx.alloc((uint64_t)T * qd * 4);
+  m->pf_h.alloc((uint64_t)T * F * 4);
+  m->pf_tok.alloc((uint64_t)T * 4);
+  m->pf_err.alloc(16);
+  m->pf_wh.alloc(wmax * 2);
+  m->pf_wl.alloc(wmax * 2);
+  const uint64_t xe = xpanel_elems(T, maxK);
+  m->pf_xh.alloc(xe * 2);
+  m->pf_xl.alloc(xe * 2);
+  // padding rows of the panels are read by the MMAs and dropped by the
+  // epilogue: start them finite
+  CK(cudaMemset(m->pf_wh.p, 0, m->pf_wh.n));
+  CK(cudaMemset(m->pf_wl.p, 0, m->pf_wl.n));
+  CK(cudaMemset(m->pf_xh.p, 0, m->pf_xh.n));
+  CK(cudaMemset(m->pf_xl.p, 0, m->pf_xl.n));
+  CK(cudaMemset(m->pf_err.p, 0, 16));
+  m->pf_cap = T;
+}
+
+// Tokens [0, n) at positions pos0.. through every layer, batched
+// (Model::forward_cached, src/model.rs:444-478, 579-592, without the logits):
+// x rows, the KV cache rows pos0..pos0+n, nothing else.
+void prefill_tokens(fz_kv* kv, const uint32_t* tokens, uint32_t n, uint32_t pos0) {
+  fz_model* m = kv->m;
+  const fz_config& c = m->cfg;
+  cudaStream_t s = m->stream;
+  const uint32_t H = c.hidden, F = c.ffn, hd = c.head_dim, qd = m->qd_l, kd = m->kd_l, ldq = qd + 2 * kd;
+  prefill_init();
+  prefill_alloc(m, std::min(n, PF_CHUNK));
+  float* X = m->pf_x.as<float>();
+  uint32_t* err = m->pf_err.as<uint32_t>();
+  auto gemm = [&](uint32_t K, uint32_t N, uint32_t T, int epi, float* out, uint32_t ld, const float* bias) {
+    QgemmLaunch q{m->pf_wh.p, m->pf_wl.p, m->pf_xh.p, m->pf_xl.p, K, N, T, epi, out, ld, bias, err};
+    launch_qgemm(q, s);
+  };
+  for (uint32_t c0 = 0; c0 < n; c0 += PF_CHUNK) {
+    const uint32_t T = std::min(PF_CHUNK, n - c0);
+    CK(cudaMemcpyAsync(m->pf_tok.p, tokens + c0, (size_t)T * 4, cudaMemcpyHostToDevice, s));
+    launch_embed_rows(m->embd, m->pf_tok.as<uint32_t>(), T, X, H, s);
+    for (uint32_t li = 0; li < c.n_layers; li++) {
+      Layer& L = m->layers[li];
+      // q, k, v (+ bias) of RMSNorm(x)
+      launch_xpanels(X, H, T, H, L.attn_norm, c.rms_eps, m->pf_xh.p, m->pf_xl.p, s);
+      launch_wpanels(L.wq, 0, m->pf_wh.p, m->pf_wl.p, s);
+      launch_wpanels(L.wk, L.wq.rows, m->pf_wh.p, m->pf_wl.p, s);
+      launch_wpanels(L.wv, L.wq.rows + L.wk.rows, m->pf_wh.p, m->pf_wl.p, s);
+      gemm(H, ldq, T, PE_STORE, m->pf_qkv.as<float>(), ldq, L.bqkv);
+      // rotated k / v into the cache, causal attention per token
+      float* kc = kv->k.as<float>() + (uint64_t)li * m->nkv_l * kv->max_ctx * hd;
+      float* vc = kv->v.as<float>() + (uint64_t)li * m->nkv_l * kv->max_ctx * hd;
+      launch_prefill_attention(m->pf_qkv.as<float>(), ldq, kv->rope_cs.as<float>(), kc, vc, m->pf_ctx.as<float>(), qd,
+                               m->nh_l, m->nkv_l, hd, kv->max_ctx, pos0 + c0, T, err, s);
+      // x += o_proj(ctx)
+      launch_xpanels(m->pf_ctx.as<float>(), qd, T, qd, nullptr, 0.f, m->pf_xh.p, m->pf_xl.p, s);
+      launch_wpanels(L.wo, 0, m->pf_wh.p, m->pf_wl.p, s);
+      gemm(qd, H, T, PE_RESID, X, H, nullptr);
+      // h = swiglu(gate, up)(RMSNorm(x)); x += down(h)
+      launch_xpanels(X, H, T, H, L.ffn_norm, c.rms_eps, m->pf_xh.p, m->pf_xl.p, s);
+      launch_wpanels(L.wgu, 0, m->pf_wh.p, m->pf_wl.p, s);
+      gemm(H, L.wgu.rows, T, PE_SWIGLU, m->pf_h.as<float>(), F, nullptr);
+      launch_xpanels(m->pf_h.as<float>(), F, T, F, nullptr, 0.f, m->pf_xh.p, m->pf_xl.p, s);
+      launch_wpanels(L.wd, 0, m->pf_wh.p, m->pf_wl.p, s);
+      gemm(F, H, T, PE_RESID, X, H, nullptr);
+    }
+  }
+  uint32_t e = 0;
+  CK(cudaMemcpyAsync(&e, err, 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  if (e) {
+    CK(cudaMemsetAsync(err, 0, 4, s));
+    fail(FZ_ETIMEOUT, "prefill: a bounded device wait ran out (code %u)", e);
+  }
 }
 
 // The step's phases for the persistent step kernel: embed, then per layer
@@ -994,16 +1095,22 @@ int fz_forward(fz_model* m, fz_kv* kv, const uint32_t* tokens, uint32_t n, float
     use_device(m);
     build_graphs(kv);
     cudaStream_t s = m->stream;
-    CK(cudaMemcpyAsync(kv->forced.p, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
-    set_state(kv, kv->len, tokens[0], n);
-    for (uint32_t i = 0; i + 1 < n; i++) CK(cudaGraphLaunch(kv->g_layers, s));
+    uint32_t first = 0;  // tokens [0, first) go through the batched prefill
+    if (n > PF_MIN && prefill_supported(m) && !getenv("FURNACE_B200_NO_PREFILL_GEMM")) {
+      first = n - 1;
+      prefill_tokens(kv, tokens, first, kv->len);
+    }
+    const uint32_t rest = n - first;
+    CK(cudaMemcpyAsync(kv->forced.p, tokens + first, (size_t)rest * 4, cudaMemcpyHostToDevice, s));
+    set_state(kv, kv->len + first, tokens[first], rest);
+    for (uint32_t i = 0; i + 1 < rest; i++) CK(cudaGraphLaunch(kv->g_layers, s));
     CK(cudaGraphLaunch(kv->g_full, s));
     if (logits) {
       tp_gather_logits(m, s);
       CK(cudaMemcpyAsync(logits, m->logits.p, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, s));
     }
     uint32_t id = 0;
-    CK(cudaMemcpyAsync(&id, kv->ids.as<uint32_t>() + (n - 1), 4, cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(&id, kv->ids.as<uint32_t>() + (rest - 1), 4, cudaMemcpyDeviceToHost, s));
     check_state(kv);
     kv->len += n;
     if (argmax) *argmax = id;
@@ -1152,6 +1259,24 @@ int fz_matmul_quant_dev(const fz_weight* w, const float* a_dev, uint32_t seq, fl
   return guard([&] {
     need(w && a_dev && out_dev, "null argument");
     cudaStream_t s = (cudaStream_t)stream;
+    if (seq >= PF_MIN && w->m.cols % 64 == 0 && !getenv("FURNACE_B200_NO_PREFILL_GEMM")) {
+      // several rows: the tensor-core GEMM of the batched prefill
+      prefill_init();
+      const uint32_t rows = w->m.rows, cols = w->m.cols;
+      DevBuf wh(wpanel_elems(rows, cols) * 2), wl(wpanel_elems(rows, cols) * 2);
+      DevBuf xh(xpanel_elems(seq, cols) * 2), xl(xpanel_elems(seq, cols) * 2), err(16);
+      for (DevBuf* b : {&wh, &wl, &xh, &xl, &err}) CK(cudaMemsetAsync(b->p, 0, b->n, s));
+      launch_wpanels(w->m, 0, wh.p, wl.p, s);
+      launch_xpanels(a_dev, cols, seq, cols, nullptr, 0.f, xh.p, xl.p, s);
+      launch_qgemm(QgemmLaunch{wh.p, wl.p, xh.p, xl.p, cols, rows, seq, PE_STORE, out_dev, rows, nullptr,
+                               err.as<uint32_t>()},
+                   s);
+      uint32_t e = 0;
+      CK(cudaMemcpyAsync(&e, err.p, 4, cudaMemcpyDeviceToHost, s));
+      CK(cudaStreamSynchronize(s));
+      if (e) fail(FZ_ETIMEOUT, "matmul: a bounded device wait ran out");
+      return;
+    }
     // widths up to 30720 convert the f32 input inside the GEMV; wider inputs
     // are converted to run records by a separate pass
     const bool direct = w->m.cols <= 30720;

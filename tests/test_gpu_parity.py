@@ -23,6 +23,7 @@ GOLD = os.path.join(os.path.dirname(__file__), "golden")
 TYPES = {"Q8_0": (8, 32, 34), "Q5_0": (6, 32, 22), "Q4_K": (12, 256, 144), "Q6_K": (14, 256, 210)}
 GEMV_REL = 1e-4
 LOGIT_ABS = 1e-3
+TOP5_TIE = 1e-4  # see _check_top5
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -94,6 +95,20 @@ def test_gemv_vs_oracle(orc, name, rows, cols):
     assert err <= GEMV_REL, err
 
 
+@pytest.mark.parametrize("name", list(TYPES))
+@pytest.mark.parametrize("rows,cols,seq", [(130, 512, 37), (520, 3584, 300), (64, 18944, 9)])
+def test_prefill_gemm_vs_oracle(orc, name, rows, cols, seq):
+    """Several input rows take the tensor-core GEMM of the batched prefill
+    (fp16 hi/lo split, tcgen05); same bar as the GEMV."""
+    dt = TYPES[name][0]
+    raw = synth.random_tensor(rows, cols, dt, seed=rows * 5 + cols + seq)
+    x = np.random.default_rng(rows + seq).normal(0, 1, size=(seq, cols)).astype(np.float32)
+    want = orc.matmul_quant(x, raw, rows, cols, dt)
+    got = fz.quant.matmul_quant(x, raw, rows, cols, dt)
+    err = np.abs(got - want).max() / np.abs(want).max()
+    assert err <= GEMV_REL, err
+
+
 def test_fused_q8_matmul_reference_case():
     """src/quant.rs:331-357 on the device."""
     raw = b""
@@ -135,12 +150,23 @@ def _models(path):
     return f, fz.Model.load(f), oracle.Model(path)
 
 
+def _check_top5(got, want, where=""):
+    """Top-5 identical up to near ties: the reference logit of the device's
+    i-th entry must equal the reference's i-th logit within TOP5_TIE.  Two
+    reference logits closer than that (3.6e-6 apart in one C1 step) are
+    ordered by rounding, not by the algorithm, and any f32 implementation
+    with another summation order may swap them while staying 40x inside the
+    1e-3 logit bar."""
+    gt, wt = np.argsort(-got, kind="stable")[:5], np.argsort(-want, kind="stable")[:5]
+    assert len(set(gt.tolist())) == 5
+    assert np.all(np.abs(want[gt] - want[wt]) <= TOP5_TIE), f"{where}: top-5 {gt} vs {wt}"
+
+
 def _check_logits(got, want, where=""):
     err = np.abs(got - want).max()
     assert err <= LOGIT_ABS, f"{where}: logits max-abs {err}"
     assert int(np.argmax(got)) == int(np.argmax(want)), where
-    gt, wt = np.argsort(-got, kind="stable")[:5], np.argsort(-want, kind="stable")[:5]
-    assert gt.tolist() == wt.tolist(), f"{where}: top-5 {gt} vs {wt}"
+    _check_top5(got, want, where)
     return err
 
 

@@ -13,6 +13,7 @@ import pytest
 
 import furnace_b200 as fz
 from furnace_b200 import synth
+from tests.test_gpu_parity import _check_top5
 
 pytestmark = pytest.mark.gpu
 LOGIT_ABS = 1e-3
@@ -82,8 +83,8 @@ def _run_tp(path, n_prompt, n_new, world=2):
     for s in range(len(want_ids)):
         err = np.abs(got_lg[s] - want_lg[s]).max()
         assert err <= LOGIT_ABS, f"step {s}: logits max-abs {err}"
-        gt, wt = np.argsort(-got_lg[s], kind="stable")[:5], np.argsort(-want_lg[s], kind="stable")[:5]
-        assert gt.tolist() == wt.tolist(), f"step {s}: top-5"
+        assert int(np.argmax(got_lg[s])) == int(np.argmax(want_lg[s])), f"step {s}: argmax"
+        _check_top5(got_lg[s], want_lg[s], f"step {s}")
 
 
 @pytest.fixture(scope="module", autouse=True)
