@@ -369,6 +369,11 @@ def run_ours(args, dist):
                    "kv": "f32"},
         "hbm_gbs_per_gpu": hbm, "hbm_frac_of_8tbs": hbm / 8000.0, "hbm_frac_of_measured": hbm / peak,
         "bytes_per_token": per_tok, "ms_per_token": ms / total_tokens, "prefill_s": prefill_s,
+        "prefill": {"tokens": args.prefill, "s": prefill_s, "tok_s": args.prefill / prefill_s,
+                    "path": "tcgen05 GEMM (fp16 hi/lo split, f32 accumulation) for all but the last prompt token"
+                    if tp == 1 and args.prefill > 8 else "decode step per token",
+                    "note": "host wall clock of fz_forward over the prompt, including the per-layer weight "
+                            "dequantization into GEMM panels"},
         "gpu_launches": launches_per_token * total_tokens, "clocks": clocks, "e2e": e2e, "roofline": roofline,
         "ops": ops,
     }

@@ -487,7 +487,9 @@ struct GvParams {
   uint32_t slots, slot_bytes, max_rows, pf_ahead;
   GvNext next;
   uint32_t idx_base;     // EPI_LOGITS: global index of row 0
+  uint32_t chunked_rec;  // in_runs stream per K-chunk through two buffers (long inputs)
 };
+constexpr uint32_t GV_CREC = 32 * 256;  // run records of one chunk (<= 32 units)
 
 // This CTA's row range within its segment: whole multiples of seg.align rows
 // (pairs for gate/up, 16-row runs where the epilogue writes run records).
@@ -701,9 +703,24 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
 // Consumer side of one CTA: all stages of the CTA's rows for format DT.
 // Warp w takes rows ra + w + GV_CWARPS*j (j < GV_RPW) of every stage; the
 // activation records of the whole input sit in shared memory (rec).
+// Chunk c's input records as record buffer use c (buffer c & 1, phase c / 2
+// of its mbarriers), once use c - 2 of that buffer has been released.  One
+// thread; the chunked-record mode of long inputs.
+__device__ __forceinline__ bool gv_issue_records(const GvParams& p, const ChunkInfo& ci, uint32_t c, uint8_t* crec,
+                                                 uint64_t* recbar, uint64_t* recfree) {
+  const uint32_t b = c & 1;
+  if (c >= 2 && !mbar_wait(&recfree[b], ((c - 2) >> 1) & 1)) return false;
+  asm volatile("fence.proxy.async;" ::: "memory");
+  mbar_expect_tx(&recbar[b], ci.nu * 256);
+  bulk_g2s(crec + b * GV_CREC, reinterpret_cast<const uint8_t*>(p.in_runs) + 256ull * ci.cu0, ci.nu * 256,
+           &recbar[b], 0ull);
+  return true;
+}
+
 template <uint32_t DT>
 __device__ bool gv_consume(const GvParams& p, const StageIter& it, const ChunkInfo* chunks, uint8_t* ring,
-                           uint64_t* full, uint64_t* empty, const XRun* rec, float* acc) {
+                           uint64_t* full, uint64_t* empty, const XRun* rec, float* acc, uint64_t* recbar,
+                           uint64_t* recfree) {
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t slot = 0, phase = 0;
   for (uint32_t c = 0; c < it.nch; c++) {
@@ -713,9 +730,23 @@ __device__ bool gv_consume(const GvParams& p, const StageIter& it, const ChunkIn
     // the rows of a warp interleave
     const uint32_t lu = min(lane, nu - 1);
     const float lane_on = lane < nu ? 1.f : 0.f;
+    const XRun* rb = rec;
+    if (p.chunked_rec) {
+      if (!mbar_wait(&recbar[c & 1], (c >> 1) & 1)) return false;
+      rb = reinterpret_cast<const XRun*>(reinterpret_cast<const uint8_t*>(rec) + (c & 1) * GV_CREC) -
+           4 * chunks[c].cu0;
+    }
     XRun xr[4];
 #pragma unroll
-    for (uint32_t j = 0; j < 4; j++) xr[j] = load_run(rec, chunks[c].cu0 + lu, j);
+    for (uint32_t j = 0; j < 4; j++) xr[j] = load_run(rb, chunks[c].cu0 + lu, j);
+    if (p.chunked_rec) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&recfree[c & 1]);
+      if (threadIdx.x == 0 && c + 2 < it.nch &&
+          !gv_issue_records(p, chunks[c + 2], c + 2, reinterpret_cast<uint8_t*>(const_cast<XRun*>(rec)), recbar,
+                            recfree))
+        return false;
+    }
     for (uint32_t ra = it.r0; ra < it.r1; ra += GV_ROWS) {
       if (!mbar_wait(&full[slot], phase)) return false;
       const uint8_t* tile = ring + (size_t)slot * p.slot_bytes;
@@ -754,7 +785,9 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
   const uint32_t NX = runs_for_dev(p.cols);
   uint8_t* ring = smem;
   XRun* rec = reinterpret_cast<XRun*>(ring + (size_t)p.slots * p.slot_bytes);
-  float* acc = reinterpret_cast<float*>(rec + NX);
+  float* acc = p.chunked_rec ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(rec) + 2 * GV_CREC)
+                             : reinterpret_cast<float*>(rec + NX);
+  __shared__ __align__(8) uint64_t crecbar[2], crecfree[2];
   __shared__ float red[GV_CWARPS];
   __shared__ unsigned long long kred[GV_CWARPS];
   __shared__ ChunkInfo chunks[GV_MAX_CH];
@@ -769,6 +802,10 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
       mbar_init(&empty[s], GV_CWARPS);
     }
     mbar_init(&recbar, 1);
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&crecbar[b], 1);
+      mbar_init(&crecfree[b], GV_CWARPS);
+    }
     fence_barrier_init();
   }
   __syncthreads();
@@ -842,7 +879,12 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
   for (uint32_t r = ctid; r < p.max_rows; r += GV_NT) acc[r] = 0.f;
   pdl_wait();  // the predecessor's output (this GEMV's input) is complete
   if (ctid == 0) tr.mark(1);
-  if (p.in_runs) {
+  if (p.in_runs && p.chunked_rec) {
+    // records of a long input stream per chunk (gv_consume): the first two
+    if (ctid == 0 && it.n_stages)
+      for (uint32_t c = 0; c < 2 && c < it.nch; c++)
+        gv_issue_records(p, chunks[c], c, reinterpret_cast<uint8_t*>(rec), crecbar, crecfree);
+  } else if (p.in_runs) {
     // records written by the producing kernel: one bulk copy
     if (ctid == 0) {
       mbar_expect_tx(&recbar, NX * 64);
@@ -908,10 +950,10 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
   bool ok = true;
   if (it.n_stages) {
     switch (it.dt) {
-      case FZ_Q4_K: ok = gv_consume<FZ_Q4_K>(p, it, chunks, ring, full, empty, rec, acc); break;
-      case FZ_Q6_K: ok = gv_consume<FZ_Q6_K>(p, it, chunks, ring, full, empty, rec, acc); break;
-      case FZ_Q8_0: ok = gv_consume<FZ_Q8_0>(p, it, chunks, ring, full, empty, rec, acc); break;
-      case FZ_Q5_0: ok = gv_consume<FZ_Q5_0>(p, it, chunks, ring, full, empty, rec, acc); break;
+      case FZ_Q4_K: ok = gv_consume<FZ_Q4_K>(p, it, chunks, ring, full, empty, rec, acc, crecbar, crecfree); break;
+      case FZ_Q6_K: ok = gv_consume<FZ_Q6_K>(p, it, chunks, ring, full, empty, rec, acc, crecbar, crecfree); break;
+      case FZ_Q8_0: ok = gv_consume<FZ_Q8_0>(p, it, chunks, ring, full, empty, rec, acc, crecbar, crecfree); break;
+      case FZ_Q5_0: ok = gv_consume<FZ_Q5_0>(p, it, chunks, ring, full, empty, rec, acc, crecbar, crecfree); break;
     }
   }
   if (!ok) {
@@ -1070,6 +1112,11 @@ void launch_gemv(const GemvLaunch& g, cudaStream_t st) {
   }
   slot = (slot + 127) & ~127u;
   uint32_t fixed = runs_for(cols) * 64 + 4 * max_rows + 128;
+  if (g.in_runs && fixed + 2 * slot > GV_SMEM) {
+    // a long record input (ffn hidden of the large configs): stream it
+    p.chunked_rec = 1;
+    fixed = 2 * GV_CREC + 4 * max_rows + 128;
+  }
   if (fixed + 2 * slot > GV_SMEM) fail(FZ_EINVAL, "gemv: %u rows per block exceed shared memory", max_rows);
   uint32_t slots = std::min<uint32_t>(GV_MAX_SLOTS, (GV_SMEM - fixed) / slot);
   p.slots = slots;

@@ -375,7 +375,7 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
 }
 
 // ---- batched prefill on the tensor cores ------------------------------------
-constexpr uint32_t PF_CHUNK = 1024;  // tokens per prefill pass
+constexpr uint32_t PF_CHUNK = 8192;  // tokens per prefill pass (each weight is dequantized once per pass)
 constexpr uint32_t PF_MIN = 8;       // shorter prompts replay the decode step
 
 bool prefill_supported(const fz_model* m) {

@@ -265,6 +265,16 @@ def test_greedy_128_steps_c1_step_kernel(monkeypatch):
 
 
 @pytest.mark.slow
+@pytest.mark.parametrize("name", ["c4", "c5"])
+def test_greedy_truncated_c4_c5(name):
+    """configs[3] (Q5_0 attention, Q6_K FFN and output, 40/8 heads, hidden
+    5120) and configs[4] (Q4_K_M mix with Q5_0/Q8_0 ffn_down fallbacks,
+    hidden 8192), truncated to 2 layers so the CPU oracle stays fast: a
+    40-token prompt (batched prefill) and 32 greedy steps."""
+    _greedy_parity(synth.ensure(name, n_layers=2), 40, 32)
+
+
+@pytest.mark.slow
 def test_greedy_128_steps_c2():
     """Qwen2.5-1.5B shape, Q4_K_M mix, 128-token prompt, 128 steps."""
     _greedy_parity(synth.ensure("c2"), 128, 128)
