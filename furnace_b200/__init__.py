@@ -42,6 +42,7 @@ EXPORTS = [
     "fz_kv_set_len", "fz_kv_read", "fz_forward", "fz_decode_greedy", "fz_dequant", "fz_matmul_quant",
     "fz_weight_upload", "fz_weight_free", "fz_matmul_quant_dev", "fz_step_profile", "fz_model_stream",
     "fz_dequant_dev_noalloc", "fz_tp_slice_of", "fz_tp_unique_id", "fz_model_load_tp",
+    "fz_sampler_new", "fz_sampler_free", "fz_sampler_draws", "fz_sample_logits", "fz_sample", "fz_generate",
 ]
 
 OPS = ["embed", "qkv", "rope_append", "attention", "o_proj", "gate_up", "down", "lm_head", "finalize"]
@@ -124,6 +125,12 @@ def load_library(build_if_missing: bool = True):
         "fz_tp_slice_of": (I, [P, I, I, P]),
         "fz_tp_unique_id": (I, [P, S]),
         "fz_model_load_tp": (I, [P, I, I, P, S, I, pp]),
+        "fz_sampler_new": (I, [C.c_float, U32, C.c_float, C.c_float, U64, pp]),
+        "fz_sampler_free": (None, [P]),
+        "fz_sampler_draws": (I, [P, C.POINTER(U64)]),
+        "fz_sample_logits": (I, [P, fp, S, u32p, S, u32p]),
+        "fz_sample": (I, [P, P, u32p, U32, u32p]),
+        "fz_generate": (I, [P, P, P, u32p, U32, U32, u32p, U32, u32p, u32p]),
         "fz_model_stream": (I, [P, pp, C.POINTER(I)]),
         "fz_step_profile": (I, [P, P, U32, U32, C.POINTER(C.c_double), C.POINTER(C.c_double), u32p]),
     }
@@ -417,6 +424,62 @@ class quant:
         _check(load_library().fz_matmul_quant(_fp(a), a.shape[0], buf.ctypes.data, buf.size, d_out, d_in, dtype,
                                               _fp(out)))
         return out
+
+
+class Sampler:
+    """Sampler (src/sampler.rs:57-155): temperature (0 = greedy), top_k (0 =
+    off), top_p (1 = off), repeat_penalty (1 = off), PCG32 seed."""
+
+    def __init__(self, temperature: float, top_k: int, top_p: float, repeat_penalty: float, seed: int):
+        h = C.c_void_p()
+        _check(load_library().fz_sampler_new(temperature, top_k, top_p, repeat_penalty, seed, C.byref(h)))
+        self._h = h
+
+    def close(self):
+        if self._h:
+            load_library().fz_sampler_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def draws(self) -> int:
+        d = C.c_uint64()
+        _check(load_library().fz_sampler_draws(self._h, C.byref(d)))
+        return d.value
+
+    def sample(self, logits, recent=()) -> int:
+        """Sampler::sample on host logits."""
+        lg = np.ascontiguousarray(logits, dtype=np.float32)
+        r = np.ascontiguousarray(recent, dtype=np.uint32) if len(recent) else np.zeros(1, np.uint32)
+        out = C.c_uint32()
+        _check(load_library().fz_sample_logits(self._h, _fp(lg), lg.size, _u32p(r), len(recent), C.byref(out)))
+        return out.value
+
+    def sample_model(self, model: "Model", recent=()) -> int:
+        """Sampler::sample on the model's last logits, on the device."""
+        r = np.ascontiguousarray(recent, dtype=np.uint32) if len(recent) else np.zeros(1, np.uint32)
+        out = C.c_uint32()
+        _check(load_library().fz_sample(model._h, self._h, _u32p(r), len(recent), C.byref(out)))
+        return out.value
+
+
+def generate_sampled(model: Model, prompt_ids, max_new: int, sampler: Sampler, stop_ids=(),
+                     max_ctx: int | None = None) -> np.ndarray:
+    """generate (src/generate.rs:83-157) with any sampler (fz_generate)."""
+    p = np.ascontiguousarray(prompt_ids, dtype=np.uint32)
+    max_ctx = max_ctx or min(model.config.context_length, 4096)
+    cache = KvCache(model, max_ctx)
+    st = np.ascontiguousarray(stop_ids, dtype=np.uint32) if len(stop_ids) else np.zeros(1, np.uint32)
+    out = np.zeros(max(max_new, 1), np.uint32)
+    n = C.c_uint32()
+    _check(load_library().fz_generate(model._h, cache._h, sampler._h, _u32p(p), p.size, max_new, _u32p(st),
+                                      len(stop_ids), _u32p(out), C.byref(n)))
+    cache.close()
+    return out[: n.value]
 
 
 def generate(model: Model, prompt_ids, max_new: int, stop_ids=(), max_ctx: int | None = None, keep_logits=False):

@@ -44,8 +44,10 @@ def build_cuda(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale(LIB, deps):
         return LIB
     objs = []
+    # host code keeps the reference's f32 operation order (no FMA contraction):
+    # the sampler's softmax / top-p arithmetic must match it exactly
     flags = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
-                    "--expt-relaxed-constexpr"]
+                    "-Xcompiler", "-ffp-contract=off", "--expt-relaxed-constexpr"]
     if verbose:
         flags += ["-Xptxas", "-v"]
     for s in srcs:

@@ -1699,6 +1699,91 @@ void launch_prefill_attention(const float* qkv, uint32_t ldq, const float* rope_
   CK(cudaGetLastError());
 }
 
+// ---------------------------------------------------------------------------
+// Sampling support (src/sampler.rs:39-155): repeat penalty, temperature and
+// top-k selection on the device.  Keys (orderable(l / temp) << 32 | ~index)
+// sort descending by value and ascending by index on ties, the order of the
+// reference's sort of (id, l / temp); the host finishes softmax, top-p and
+// the draw from the k survivors.
+// ---------------------------------------------------------------------------
+constexpr uint32_t TK_BLOCK = 2048;  // logits per pass-1 block
+constexpr uint32_t TK_MERGE = 8192;  // keys of the pass-2 sort
+
+__device__ __forceinline__ void bitonic_desc(unsigned long long* keys, uint32_t n) {
+  for (uint32_t size = 2; size <= n; size <<= 1)
+    for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+      __syncthreads();
+      for (uint32_t i = threadIdx.x; i < n / 2; i += blockDim.x) {
+        const uint32_t pos = 2 * i - (i & (stride - 1)), partner = pos + stride;
+        const bool desc = (pos & size) == 0;
+        const unsigned long long a = keys[pos], b = keys[partner];
+        if ((a < b) == desc) {
+          keys[pos] = b;
+          keys[partner] = a;
+        }
+      }
+    }
+  __syncthreads();
+}
+
+// Pass 1: the top k of each block of TK_BLOCK logits (penalised, scaled).
+__global__ void k_topk1(const float* __restrict__ logits, uint32_t V, const uint32_t* __restrict__ recent, uint32_t nr,
+                        float pen, float temp, uint32_t k, unsigned long long* __restrict__ out) {
+  __shared__ unsigned long long keys[TK_BLOCK];
+  __shared__ uint32_t rs[64];
+  if (threadIdx.x < nr) rs[threadIdx.x] = recent[threadIdx.x];
+  __syncthreads();
+  for (uint32_t j = threadIdx.x; j < TK_BLOCK; j += blockDim.x) {
+    const uint32_t i = blockIdx.x * TK_BLOCK + j;
+    unsigned long long key = 0;
+    if (i < V) {
+      float l = logits[i];
+      if (pen != 1.0f) {  // apply_repeat_penalty (src/sampler.rs:39-55): once per distinct recent token
+        bool seen = false;
+        for (uint32_t r = 0; r < nr; r++) seen |= rs[r] == i;
+        if (seen) l = l > 0.0f ? __fdiv_rn(l, pen) : __fmul_rn(l, pen);
+      }
+      key = argmax_key(__fdiv_rn(l, temp), i);
+    }
+    keys[j] = key;
+  }
+  bitonic_desc(keys, TK_BLOCK);
+  for (uint32_t j = threadIdx.x; j < k; j += blockDim.x) out[(uint64_t)blockIdx.x * k + j] = keys[j];
+}
+
+// Pass 2: the top k of all blocks' survivors.
+__global__ void k_topk2(const unsigned long long* __restrict__ in, uint32_t n, uint32_t k,
+                        unsigned long long* __restrict__ out) {
+  extern __shared__ unsigned long long mkeys[];
+  uint32_t m = 2;
+  while (m < n) m <<= 1;
+  for (uint32_t j = threadIdx.x; j < m; j += blockDim.x) mkeys[j] = j < n ? in[j] : 0ull;
+  bitonic_desc(mkeys, m);
+  for (uint32_t j = threadIdx.x; j < k; j += blockDim.x) out[j] = mkeys[j];
+}
+
+uint32_t topk_max() { return 64; }
+
+void launch_topk(const float* logits, uint32_t V, const uint32_t* recent, uint32_t nr, float pen, float temp,
+                 uint32_t k, void* scratch, void* out, cudaStream_t s) {
+  if (k == 0 || k > topk_max() || nr > 64) fail(FZ_EINVAL, "top-k %u / %u recent tokens unsupported on the device", k, nr);
+  const uint32_t nb = (V + TK_BLOCK - 1) / TK_BLOCK;
+  if (nb * k > TK_MERGE) fail(FZ_EINVAL, "top-k: vocabulary %u too large for k = %u", V, k);
+  unsigned long long* mid = reinterpret_cast<unsigned long long*>(scratch);
+  k_topk1<<<nb, 256, 0, s>>>(logits, V, recent, nr, pen, temp, k, mid);
+  CK(cudaGetLastError());
+  uint32_t m = 2;
+  while (m < nb * k) m <<= 1;
+  k_topk2<<<1, 1024, m * sizeof(unsigned long long), s>>>(mid, nb * k, k, reinterpret_cast<unsigned long long*>(out));
+  CK(cudaGetLastError());
+}
+
+size_t topk_scratch_bytes(uint32_t V) { return (size_t)((V + TK_BLOCK - 1) / TK_BLOCK) * topk_max() * 8 + 64; }
+
+void sampler_init() {
+  CK(cudaFuncSetAttribute(k_topk2, cudaFuncAttributeMaxDynamicSharedMemorySize, TK_MERGE * 8));
+}
+
 void step_init() { CK(cudaFuncSetAttribute(k_step, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM)); }
 
 }  // namespace fz

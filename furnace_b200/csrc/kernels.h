@@ -150,6 +150,15 @@ StepPlan step_plan_build(const StepLaunch& L);
 void launch_step(const StepLaunch& L, const StepPlan& plan, const void* plan_dev, cudaStream_t s);
 void step_init();
 
+// ---- sampling (src/sampler.rs) ------------------------------------------------
+// Top k (k <= topk_max()) of the repeat-penalised, temperature-scaled logits as
+// packed keys (orderable value << 32 | ~index), descending; recent: <= 64 ids.
+void sampler_init();
+uint32_t topk_max();
+size_t topk_scratch_bytes(uint32_t V);
+void launch_topk(const float* logits, uint32_t V, const uint32_t* recent, uint32_t nr, float pen, float temp,
+                 uint32_t k, void* scratch, void* out, cudaStream_t s);
+
 // ---- prefill on the tensor cores (prefill.cuh) -------------------------------
 enum PrefillEpilogue : int { PE_STORE = 0, PE_RESID = 1, PE_SWIGLU = 2 };
 struct QgemmLaunch {

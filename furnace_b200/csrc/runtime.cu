@@ -4,6 +4,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -95,6 +96,7 @@ struct fz_model {
   // fp16 hi/lo panels of one weight and of one activation matrix
   uint32_t pf_cap = 0;
   DevBuf pf_x, pf_qkv, pf_ctx, pf_h, pf_tok, pf_err, pf_wh, pf_wl, pf_xh, pf_xl;
+  DevBuf smp_scratch, smp_out;  // device top-k of the sampler
 };
 
 struct fz_kv {
@@ -113,6 +115,22 @@ struct fz_kv {
 struct fz_weight {
   DevBuf buf, runs;
   DevMat m;
+};
+
+// Sampler (src/sampler.rs:57-155) with its PCG32 stream (src/sampler.rs:6-34).
+struct fz_sampler {
+  float temperature = 0.f, top_p = 1.f, repeat_penalty = 1.f;
+  uint32_t top_k = 0;
+  uint64_t state = 0, inc = (0xda3e39cb94b95bdbull << 1) | 1;
+  uint64_t draws = 0;
+  uint32_t next_u32() {
+    const uint64_t old = state;
+    state = old * 6364136223846793005ull + inc;
+    const uint32_t xs = (uint32_t)(((old >> 18) ^ old) >> 27), rot = (uint32_t)(old >> 59);
+    return (xs >> rot) | (xs << ((32 - rot) & 31));
+  }
+  float next_f32() { return (float)(next_u32() >> 8) / (float)(1u << 24); }
+  bool greedy() const { return temperature == 0.0f || top_k == 1; }
 };
 
 namespace {
@@ -523,6 +541,104 @@ StepLaunch step_launch(fz_kv* kv, const std::vector<StepPhase>& ph, bool with_lo
   L.ids_out = kv->ids.as<uint32_t>();
   L.has_logits = with_logits;
   return L;
+}
+
+// ---- sampling (src/sampler.rs) ------------------------------------------------
+// Softmax, top-p, renormalisation and the draw over candidates (id, l / temp)
+// sorted by value descending, id ascending on ties: Sampler::filtered's tail
+// and Sampler::sample's walk (src/sampler.rs:96-108, 126-154), in the
+// reference's f32 operation order.
+uint32_t sampler_finish(fz_sampler* s, std::vector<std::pair<uint32_t, float>>& c) {
+  const float mx = c[0].second;
+  float sum = 0.0f;
+  for (auto& e : c) {
+    e.second = expf(e.second - mx);
+    sum += e.second;
+  }
+  for (auto& e : c) e.second /= sum;
+  if (s->top_p < 1.0f) {
+    float cum = 0.0f;
+    size_t keep = c.size();
+    for (size_t i = 0; i < c.size(); i++) {
+      cum += c[i].second;
+      if (cum >= s->top_p) {
+        keep = i + 1;
+        break;
+      }
+    }
+    c.resize(keep);
+    float t = 0.0f;
+    for (auto& e : c) t += e.second;
+    for (auto& e : c) e.second /= t;
+  }
+  const float u = s->next_f32();
+  s->draws++;
+  float cum = 0.0f;
+  for (auto& e : c) {
+    cum += e.second;
+    if (u < cum) return e.first;
+  }
+  return c.back().first;
+}
+
+// Sampler::sample on host logits (src/sampler.rs:86-108).
+uint32_t sample_host(fz_sampler* s, const float* logits, size_t n, const uint32_t* recent, size_t nr) {
+  std::vector<float> lg(logits, logits + n);
+  if (s->repeat_penalty != 1.0f) {  // apply_repeat_penalty (src/sampler.rs:39-55)
+    std::vector<uint32_t> seen;
+    for (size_t i = 0; i < nr; i++) {
+      const uint32_t t = recent[i];
+      if (t >= n || std::find(seen.begin(), seen.end(), t) != seen.end()) continue;
+      seen.push_back(t);
+      lg[t] = lg[t] > 0.0f ? lg[t] / s->repeat_penalty : lg[t] * s->repeat_penalty;
+    }
+  }
+  if (s->greedy()) {  // first max (src/generate.rs:69-77)
+    size_t best = 0;
+    for (size_t i = 1; i < n; i++)
+      if (lg[i] > lg[best]) best = i;
+    return (uint32_t)best;
+  }
+  std::vector<std::pair<uint32_t, float>> c(n);
+  for (size_t i = 0; i < n; i++) c[i] = {(uint32_t)i, lg[i] / s->temperature};
+  std::stable_sort(c.begin(), c.end(), [](const auto& a, const auto& b) { return a.second > b.second; });
+  if (s->top_k > 0 && s->top_k < c.size()) c.resize(s->top_k);
+  return sampler_finish(s, c);
+}
+
+// Sampler::sample on the model's current logits: penalty, temperature and
+// top-k on the device, only the k survivors cross to the host.
+uint32_t sample_device(fz_model* m, fz_sampler* s, const uint32_t* recent, uint32_t nr) {
+  const fz_config& c = m->cfg;
+  cudaStream_t st = m->stream;
+  const bool greedy = s->greedy();
+  const uint32_t k = greedy ? 1 : s->top_k;
+  if (k == 0 || k > topk_max()) {  // the whole vocabulary is a candidate: host path
+    std::vector<float> lg(c.vocab);
+    CK(cudaMemcpyAsync(lg.data(), m->logits.p, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    return sample_host(s, lg.data(), lg.size(), recent, nr);
+  }
+  sampler_init();
+  if (!m->smp_scratch.p) {
+    m->smp_scratch.alloc(topk_scratch_bytes(c.vocab));
+    m->smp_out.alloc(topk_max() * 8 + 64 * 4);
+  }
+  uint32_t* rdev = reinterpret_cast<uint32_t*>(m->smp_out.as<uint8_t>() + topk_max() * 8);
+  if (nr) CK(cudaMemcpyAsync(rdev, recent, nr * 4, cudaMemcpyHostToDevice, st));
+  launch_topk(m->logits.as<float>(), c.vocab, rdev, nr, s->repeat_penalty, greedy ? 1.0f : s->temperature, k,
+              m->smp_scratch.p, m->smp_out.p, st);
+  std::vector<unsigned long long> keys(k);
+  CK(cudaMemcpyAsync(keys.data(), m->smp_out.p, k * 8, cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  std::vector<std::pair<uint32_t, float>> cand(k);
+  for (uint32_t i = 0; i < k; i++) {
+    const uint32_t ord = (uint32_t)(keys[i] >> 32), idx = 0xFFFFFFFFu - (uint32_t)(keys[i] & 0xFFFFFFFFull);
+    const uint32_t bits = (ord & 0x80000000u) ? (ord & 0x7FFFFFFFu) : ~ord;
+    cand[i] = {idx, __builtin_bit_cast(float, bits)};
+  }
+  if (greedy) return cand[0].first;
+  return sampler_finish(s, cand);
 }
 
 // The step is captured as separate kernels (programmatic dependent launches)
@@ -1163,6 +1279,89 @@ int fz_decode_greedy(fz_model* m, fz_kv* kv, uint32_t first, uint32_t n_steps, c
       kv->len += used;
     }
     if (n_out) *n_out = written;
+  });
+}
+
+int fz_sampler_new(float temperature, uint32_t top_k, float top_p, float repeat_penalty, uint64_t seed,
+                   fz_sampler** out) {
+  return guard([&] {
+    need(out != nullptr, "null argument");
+    need(temperature >= 0.0f && top_p > 0.0f && top_p <= 1.0f && repeat_penalty > 0.0f, "sampler settings out of range");
+    auto s = std::make_unique<fz_sampler>();
+    s->temperature = temperature;
+    s->top_k = top_k;
+    s->top_p = top_p;
+    s->repeat_penalty = repeat_penalty;
+    // Pcg32::new (src/sampler.rs:12-19): one step, add the seed, one step
+    s->next_u32();
+    s->state += seed;
+    s->next_u32();
+    *out = s.release();
+  });
+}
+
+void fz_sampler_free(fz_sampler* s) { delete s; }
+
+int fz_sampler_draws(const fz_sampler* s, uint64_t* draws) {
+  return guard([&] {
+    need(s && draws, "null argument");
+    *draws = s->draws;
+  });
+}
+
+int fz_sample_logits(fz_sampler* s, const float* logits, size_t n, const uint32_t* recent, size_t n_recent,
+                     uint32_t* out) {
+  return guard([&] {
+    need(s && logits && out && n > 0 && (recent || n_recent == 0), "null argument");
+    *out = sample_host(s, logits, n, recent, n_recent);
+  });
+}
+
+int fz_sample(fz_model* m, fz_sampler* s, const uint32_t* recent, uint32_t n_recent, uint32_t* out) {
+  return guard([&] {
+    need(m && s && out && (recent || n_recent == 0), "null argument");
+    need(n_recent <= 64, "at most 64 recent tokens (the reference's repeat window)");
+    use_device(m);
+    tp_gather_logits(m, m->stream);
+    *out = sample_device(m, s, recent, n_recent);
+  });
+}
+
+int fz_generate(fz_model* m, fz_kv* kv, fz_sampler* s, const uint32_t* prompt, uint32_t n_prompt, uint32_t max_new,
+                const uint32_t* stop_ids, uint32_t n_stop, uint32_t* ids_out, uint32_t* n_out) {
+  return guard([&] {
+    need(m && kv && kv->m == m && s && prompt && n_prompt > 0 && ids_out && n_out, "null or mismatched handles");
+    need(n_stop == 0 || stop_ids, "null stop ids");
+    *n_out = 0;
+    need((uint64_t)kv->len + n_prompt + (max_new ? max_new - 1 : 0) <= kv->max_ctx,
+         "prompt (%u) + max tokens (%u) exceeds the cache (%u of %u used)", n_prompt, max_new, kv->len, kv->max_ctx);
+    if (max_new == 0) return;
+    auto check = [](int rc) {
+      if (rc) throw Error(rc, fz::last_error());
+    };
+    if (s->greedy() && s->repeat_penalty == 1.0f) {
+      // greedy: the device feeds each argmax back itself (fz_decode_greedy)
+      uint32_t first = 0;
+      check(fz_forward(m, kv, prompt, n_prompt, nullptr, &first));
+      check(fz_decode_greedy(m, kv, first, max_new, stop_ids, n_stop, ids_out, nullptr, n_out));
+      return;
+    }
+    std::vector<uint32_t> context(prompt, prompt + n_prompt);
+    check(fz_forward(m, kv, prompt, n_prompt, nullptr, nullptr));
+    uint32_t n = 0;
+    for (uint32_t step = 0; step < max_new; step++) {
+      const size_t window = context.size() > 64 ? context.size() - 64 : 0;  // repeat window (src/sampler.rs:74)
+      uint32_t next = 0;
+      check(fz_sample(m, s, context.data() + window, (uint32_t)(context.size() - window), &next));
+      bool stop = false;
+      for (uint32_t i = 0; i < n_stop; i++) stop |= stop_ids[i] == next;
+      if (stop) break;
+      ids_out[n++] = next;
+      context.push_back(next);
+      if (step + 1 == max_new) break;
+      check(fz_forward(m, kv, &next, 1, nullptr, nullptr));
+    }
+    *n_out = n;
   });
 }
 

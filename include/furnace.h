@@ -170,6 +170,32 @@ int fz_forward(fz_model* m, fz_kv* kv, const uint32_t* tokens, uint32_t n, float
 int fz_decode_greedy(fz_model* m, fz_kv* kv, uint32_t first, uint32_t n_steps, const uint32_t* stop_ids,
                      uint32_t n_stop, uint32_t* ids_out, float* logits_out, uint32_t* n_out);
 
+/* ---- Sampling (src/sampler.rs) and the generate loop (src/generate.rs) ---- */
+typedef struct fz_sampler fz_sampler;
+/* Sampler::new (src/sampler.rs:68-78): temperature (0 = greedy), top_k (0 =
+ * off), top_p (1 = off), repeat_penalty (1 = off), PCG32 seed. */
+int fz_sampler_new(float temperature, uint32_t top_k, float top_p, float repeat_penalty, uint64_t seed,
+                   fz_sampler** out);
+void fz_sampler_free(fz_sampler* s);
+/* Sampler::draws (src/sampler.rs:82-84). */
+int fz_sampler_draws(const fz_sampler* s, uint64_t* draws);
+/* Sampler::sample (src/sampler.rs:86-108) on host logits [n] with the recent
+ * context (the repeat window). */
+int fz_sample_logits(fz_sampler* s, const float* logits, size_t n, const uint32_t* recent, size_t n_recent,
+                     uint32_t* out);
+/* Sampler::sample on the model's logits of its last forward, without copying
+ * them back: penalty, temperature and top-k (k <= 64) run on the device and
+ * only the k candidates reach the host, which finishes softmax, top-p and
+ * the PCG32 draw in the reference's f32 order.  top_k = 0 or > 64 copies the
+ * logits and samples on the host.  n_recent <= 64. */
+int fz_sample(fz_model* m, fz_sampler* s, const uint32_t* recent, uint32_t n_recent, uint32_t* out);
+/* generate (src/generate.rs:83-157) from kv->len: prefill the prompt, then
+ * sample up to max_new ids (max_new - 1 decode forwards), stopping before any
+ * stop id.  Greedy settings without a penalty use fz_decode_greedy's
+ * device-fed loop.  *n_out = ids written. */
+int fz_generate(fz_model* m, fz_kv* kv, fz_sampler* s, const uint32_t* prompt, uint32_t n_prompt, uint32_t max_new,
+                const uint32_t* stop_ids, uint32_t n_stop, uint32_t* ids_out, uint32_t* n_out);
+
 /* Per-op decode timings, the device counterpart of the reference's perf
  * counters (src/perf.rs:25-39, reported by `run --timings`): runs `reps`
  * greedy decode steps from kv.len WITHOUT the graph, with CUDA events around

@@ -252,6 +252,23 @@ def test_greedy_stop_ids(tiny, orc):
     assert got.tolist() == want.tolist()
 
 
+@pytest.mark.parametrize("temp,top_k,top_p,pen", [(0.7, 40, 0.9, 1.0), (1.0, 0, 0.95, 1.2), (0.8, 8, 1.0, 1.3)])
+def test_sampled_generate_matches_oracle(tiny, temp, top_k, top_p, pen):
+    """generate with a sampler (fz_generate): top-k on the device, the draw on
+    the host (top_k 0 samples the whole vocabulary on the host); same seed,
+    same ids as the oracle's generate."""
+    from oracle import oracle
+
+    f = fz.GgufFile.open(tiny)
+    dev = fz.Model.load(f)
+    ref = oracle.Model(tiny)
+    ids = synth.prompt_ids(ref.vocab, 12, seed=8)
+    want, _, _, _ = ref.generate(ids, 48, sampler=oracle.Sampler(temp, top_k, top_p, pen, 77), max_ctx=64)
+    smp = fz.Sampler(temp, top_k, top_p, pen, 77)
+    got = fz.generate_sampled(dev, ids, 48, smp, max_ctx=64)
+    assert got.tolist() == want.tolist()
+
+
 @pytest.mark.slow
 def test_greedy_128_steps_c1():
     """Qwen2.5-0.5B shape, Q8_0, 32-token prompt, 128 greedy steps."""
