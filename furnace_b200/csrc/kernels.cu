@@ -65,7 +65,7 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)_
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
-// Optional per-CTA timeline of the step kernels (%globaltimer, ns), recorded
+// Optional per-CTA timeline of the decode-step kernels (%globaltimer, ns), recorded
 // by thread 0 of every CTA while a trace buffer is installed (trace_enable):
 // t[0] start, t[1] after the wait on the predecessor, t[2] input ready,
 // t[3] main loop done, t[4] end.  Off (one global load per CTA) otherwise.
@@ -877,6 +877,21 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
   // ---------------- consumers ----------------
   const uint32_t ctid = tid;
   for (uint32_t r = ctid; r < p.max_rows; r += GV_NT) acc[r] = 0.f;
+  // f32 input: x in buf[0..7] and the RMSNorm weight in buf[8..15] when
+  // normalising, else x in buf[0..15] (the host bounds cols).  The weight is
+  // constant: its loads are issued before the wait on the predecessor.
+  const float4* x4 = reinterpret_cast<const float4*>(p.x);
+  const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
+  const uint32_t n4 = p.cols / 4;
+  const bool norm = !p.in_runs && p.norm_w != nullptr;
+  float4 buf[16];
+  if (norm) {
+#pragma unroll
+    for (int j = 8; j < 16; j++) {
+      const uint32_t i4 = ctid + GV_NT * (j - 8);
+      buf[j] = i4 < n4 ? w4[i4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
   pdl_wait();  // the predecessor's output (this GEMV's input) is complete
   if (ctid == 0) tr.mark(1);
   if (p.in_runs && p.chunked_rec) {
@@ -895,19 +910,13 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
       return;
     }
   } else {
-    // f32 input (RMS-normalised when norm_w is set) -> records; every load of
-    // this thread in flight at once (x in buf[0..7], weight in buf[8..15] when
-    // normalising, else x in buf[0..15]; the host bounds cols)
-    const float4* x4 = reinterpret_cast<const float4*>(p.x);
-    const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
-    const uint32_t n4 = p.cols / 4;
-    const bool norm = p.norm_w != nullptr;
-    float4 buf[16];
+    // f32 input (RMS-normalised when norm_w is set) -> records; every x load
+    // of this thread in flight at once
 #pragma unroll
     for (int j = 0; j < 16; j++) {
-      const bool isw = norm && j >= 8;
-      const uint32_t i4 = ctid + GV_NT * (isw ? j - 8 : j);
-      buf[j] = i4 < n4 ? (isw ? w4[i4] : x4[i4]) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (norm && j >= 8) break;
+      const uint32_t i4 = ctid + GV_NT * j;
+      buf[j] = i4 < n4 ? x4[i4] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float inv = 1.f;
     if (norm) {
@@ -1028,7 +1037,7 @@ constexpr uint32_t GV_SMEM = 200 * 1024;   // one block per SM
 constexpr uint32_t GV_PF_AHEAD = 96 * 1024;
 constexpr uint32_t GV_PF_NEXT = 64 * 1024;
 
-// Install (cap > 0) or remove (cap == 0) the step-kernel trace buffer.
+// Install (cap > 0) or remove (cap == 0) the decode-step trace buffer.
 void trace_install(TraceRec* buf, uint32_t cap) {
   CK(cudaMemcpyToSymbol(g_trace, &buf, sizeof buf));
   CK(cudaMemcpyToSymbol(g_trace_cap, &cap, sizeof cap));
@@ -1281,17 +1290,17 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
       if (t < tn) {
         const float4* kr = reinterpret_cast<const float4*>(kt + (size_t)t * HD);
         const float4* qr = reinterpret_cast<const float4*>(qs[warp]);
-        float dsum = 0.f;
+        float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;  // four independent chains
 #pragma unroll 8
         for (uint32_t c = 0; c < HD / 4; c++) {
           uint32_t cc = (c + t) & (HD / 4 - 1);
           float4 k4 = kr[cc], q4 = qr[cc];
-          dsum = fmaf(q4.x, k4.x, dsum);
-          dsum = fmaf(q4.y, k4.y, dsum);
-          dsum = fmaf(q4.z, k4.z, dsum);
-          dsum = fmaf(q4.w, k4.w, dsum);
+          d0 = fmaf(q4.x, k4.x, d0);
+          d1 = fmaf(q4.y, k4.y, d1);
+          d2 = fmaf(q4.z, k4.z, d2);
+          d3 = fmaf(q4.w, k4.w, d3);
         }
-        s = __fmul_rn(dsum, scale);
+        s = __fmul_rn((d0 + d1) + (d2 + d3), scale);
       }
       float mt = s;
 #pragma unroll
@@ -1306,11 +1315,20 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
       m = mn;
 #pragma unroll
       for (int d = 0; d < DPL; d++) acc[d] *= alpha;
+#pragma unroll 8
       for (uint32_t t2 = 0; t2 < tn; t2++) {
         const float pt = __shfl_sync(0xffffffffu, pr, t2);
         const float* vr = vt + (size_t)t2 * HD + lane * DPL;
+        if (DPL == 4) {  // one 16-byte load per lane: consecutive lanes, no bank conflict
+          const float4 v4 = *reinterpret_cast<const float4*>(vr);
+          acc[0] = fmaf(pt, v4.x, acc[0]);
+          acc[1] = fmaf(pt, v4.y, acc[1]);
+          acc[2] = fmaf(pt, v4.z, acc[2]);
+          acc[3] = fmaf(pt, v4.w, acc[3]);
+        } else {
 #pragma unroll
-        for (int d = 0; d < DPL; d++) acc[d] = fmaf(pt, vr[d], acc[d]);
+          for (int d = 0; d < DPL; d++) acc[d] = fmaf(pt, vr[d], acc[d]);
+        }
       }
     }
     __syncthreads();  // buffer b free
@@ -1403,8 +1421,9 @@ __global__ void k_attn_combine(const float* __restrict__ partials, float* __rest
   if (threadIdx.x == 0) tr.mark(4);
 }
 
+// Two CTAs per SM: more warps in flight hide the latency-bound tile loop.
 uint32_t attention_splits(uint32_t n_kv) {
-  uint32_t s = ((uint32_t)num_sms() + n_kv - 1) / n_kv;
+  uint32_t s = (2 * (uint32_t)num_sms() + n_kv - 1) / n_kv;
   return s < 1 ? 1 : s > AT_MAXS ? AT_MAXS : s;
 }
 
@@ -1465,170 +1484,6 @@ void launch_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, b
 
 // ---------------------------------------------------------------------------
 // Persistent decode step
-// ---------------------------------------------------------------------------
-#include "step_kernel.cuh"
-
-uint32_t step_attention_splits(uint32_t n_kv) { return std::max<uint32_t>(1, (uint32_t)num_sms() / n_kv); }
-
-static uint32_t step_u_bytes(const StepLaunch& L) {
-  uint32_t u = 0;
-  for (uint32_t i = 0; i < L.nph; i++) {
-    const StepPhase& ph = L.phases[i];
-    if (ph.kind == SP_ATTN) u = std::max<uint32_t>(u, (uint32_t)SK_NBUF * 2 * SK_TP * ph.a.hd * 4);
-    if (ph.kind == SP_GEMV && ph.g.x) u = std::max<uint32_t>(u, runs_for(ph.g.seg[0].w.cols) * 64);
-  }
-  return (u + 127) & ~127u;
-}
-
-// Host copy of cta_rows (the device's row split of one segment).
-static void host_cta_rows(const GvSeg& s, uint32_t b, uint32_t* r0, uint32_t* r1) {
-  uint32_t n = s.cta_end - s.cta_begin, lb = b - s.cta_begin, units = s.rows / s.align;
-  *r0 = s.align * (uint32_t)((uint64_t)units * lb / n);
-  *r1 = lb + 1 == n ? s.rows : s.align * (uint32_t)((uint64_t)units * (lb + 1) / n);
-}
-
-StepPlan step_plan_build(const StepLaunch& L) {
-  const uint32_t grid = (uint32_t)num_sms();
-  StepPlan plan;
-  plan.nph = L.nph;
-  plan.u_bytes = step_u_bytes(L);
-  plan.ring_bytes = SK_SMEM - plan.u_bytes - 2 * SK_CREC - SK_ACC;
-  std::vector<PhaseRec> rec((size_t)L.nph * grid);
-  memset(rec.data(), 0, rec.size() * sizeof(PhaseRec));
-  std::vector<std::vector<StageRec>> st(grid);
-  for (uint32_t i = 0; i < L.nph; i++) {
-    const StepPhase& sp = L.phases[i];
-    if (sp.kind == SP_EMBED) {
-      for (uint32_t b = 0; b < grid; b++) rec[(size_t)i * grid + b].kind = PH_EMBED;
-    } else if (sp.kind == SP_ATTN) {
-      const AttnLaunch& a = sp.a;
-      if (a.hd != 64 && a.hd != 128) fail(FZ_EINVAL, "head_dim %u unsupported (64 or 128)", a.hd);
-      const uint32_t G = a.n_heads / a.n_kv;
-      if (G > AT_MAXG || a.n_heads % a.n_kv) fail(FZ_EINVAL, "attention: GQA group %u unsupported", G);
-      if (a.splits * a.n_kv > grid || a.splits < 1) fail(FZ_EINVAL, "attention: %u splits x %u KV heads", a.splits, a.n_kv);
-      for (uint32_t b = 0; b < grid; b++) {
-        PhaseRec& d = rec[(size_t)i * grid + b];
-        d.kind = PH_ATTN;
-        d.qkv = a.qkv;
-        d.kc = a.kcache;
-        d.vc = a.vcache;
-        d.ctx = a.ctx;
-        d.ctx_runs = reinterpret_cast<XRun*>(a.ctx_runs);
-        d.nh = a.n_heads;
-        d.nkv = a.n_kv;
-        d.hd = a.hd;
-        d.S = a.splits;
-        d.active = b < a.splits * a.n_kv;
-        d.kvh = d.active ? b / a.splits : 0;
-        d.split = d.active ? b % a.splits : 0;
-      }
-    } else {
-      const GemvLaunch& g = sp.g;
-      const uint32_t cols = g.seg[0].w.cols;
-      for (int k = 0; k < g.nseg; k++)
-        if (g.seg[k].w.cols != cols) fail(FZ_EINVAL, "gemv segments disagree on input width");
-      if (!g.in_runs && !g.x) fail(FZ_EINVAL, "gemv: no input activation");
-      if (g.x && (cols / 4 > (g.norm_w ? 8u : 16u) * GV_NT || cols % 32))
-        fail(FZ_EINVAL, "gemv: input width %u unsupported for an f32 input", cols);
-      if (lay_nch(cols) > GV_MAX_CH) fail(FZ_EINVAL, "gemv: input width %u too large", cols);
-      if (g.epilogue == EPI_SWIGLU && !g.out_runs) fail(FZ_EINVAL, "step: SwiGLU phase without output records");
-      GvSeg segs[3];
-      fill_segs(g, segs);
-      for (uint32_t b = 0; b < grid; b++) {
-        PhaseRec& d = rec[(size_t)i * grid + b];
-        d.kind = PH_GEMV;
-        d.epi = g.epilogue;
-        d.cols = cols;
-        d.x = g.x;
-        d.norm_w = g.norm_w;
-        d.eps = g.eps;
-        d.in_runs = reinterpret_cast<const XRun*>(g.in_runs);
-        d.out_runs = reinterpret_cast<XRun*>(g.out_runs);
-        int si = 0;
-        while (si + 1 < g.nseg && b >= segs[si].cta_end) si++;
-        const GvSeg& sg = segs[si];
-        if (b < sg.cta_begin || b >= sg.cta_end) continue;
-        uint32_t r0, r1;
-        host_cta_rows(sg, b, &r0, &r1);
-        if (r1 <= r0) continue;
-        if ((r1 - r0) * 4 > SK_ACC) fail(FZ_EINVAL, "step: %u rows per block exceed the accumulators", r1 - r0);
-        d.active = 1;
-        d.dt = sg.dtype;
-        d.r0 = r0;
-        d.r1 = r1;
-        d.nch = lay_nch(cols);
-        d.out = sg.out;
-        d.bias = sg.bias;
-        for (uint32_t c = 0; c < d.nch; c++) {
-          const uint32_t nu = lay_cu0(sg.dtype, cols, c + 1) - lay_cu0(sg.dtype, cols, c);
-          const uint32_t tb = lay_chunk_bytes(sg.dtype, nu);
-          if (GV_ROWS * tb > plan.ring_bytes) fail(FZ_EINVAL, "step: a weight stage exceeds the %u-byte ring", plan.ring_bytes);
-          const uint8_t* plane = sg.w + (uint64_t)sg.rows * lay_chunk_off(sg.dtype, cols, c);
-          for (uint32_t ra = r0; ra < r1; ra += GV_ROWS)
-            st[b].push_back(StageRec{plane + (uint64_t)ra * tb, (std::min(ra + GV_ROWS, r1) - ra) * tb, 0});
-        }
-      }
-    }
-  }
-  // blob: [PhaseRec nph x grid][stage_first[grid]][stage lists, each ended by
-  // a zero record and padded to whole blocks][SL_NB zero blocks]
-  std::vector<uint32_t> first(grid);
-  std::vector<StageRec> all;
-  for (uint32_t b = 0; b < grid; b++) {
-    first[b] = (uint32_t)all.size();
-    all.insert(all.end(), st[b].begin(), st[b].end());
-    all.push_back(StageRec{nullptr, 0, 0});
-    while (all.size() % SL_BLK) all.push_back(StageRec{nullptr, 0, 0});
-  }
-  all.resize(all.size() + SL_NB * SL_BLK, StageRec{nullptr, 0, 0});
-  const size_t rec_bytes = rec.size() * sizeof(PhaseRec);
-  plan.off_stage_first = rec_bytes;
-  plan.off_stages = (rec_bytes + grid * 4 + 255) & ~(size_t)255;
-  plan.blob.assign(plan.off_stages + all.size() * sizeof(StageRec), 0);
-  memcpy(plan.blob.data(), rec.data(), rec_bytes);
-  memcpy(plan.blob.data() + plan.off_stage_first, first.data(), grid * 4);
-  memcpy(plan.blob.data() + plan.off_stages, all.data(), all.size() * sizeof(StageRec));
-  return plan;
-}
-
-void launch_step(const StepLaunch& L, const StepPlan& plan, const void* plan_dev, cudaStream_t s) {
-  SkParams P{};
-  const uint8_t* base = reinterpret_cast<const uint8_t*>(plan_dev);
-  P.rec = reinterpret_cast<const PhaseRec*>(base);
-  P.stage_first = reinterpret_cast<const uint32_t*>(base + plan.off_stage_first);
-  P.stages = reinterpret_cast<const StageRec*>(base + plan.off_stages);
-  P.nph = plan.nph;
-  P.u_bytes = plan.u_bytes;
-  P.ring_bytes = plan.ring_bytes;
-  P.pf_ahead = SK_PF_AHEAD;
-  P.st = L.state;
-  P.bar = L.bar;
-  P.attn_cnt = L.attn_cnt;
-  P.partials = L.partials;
-  P.rope_cs = reinterpret_cast<const float2*>(L.rope_cs);
-  P.max_ctx = L.max_ctx;
-  P.emb = L.emb.ptr;
-  P.emb_dt = L.emb.dtype;
-  P.emb_rows = L.emb.rows;
-  P.emb_cols = L.emb.cols;
-  P.x = L.x;
-  P.forced = L.forced;
-  P.ids_out = L.ids_out;
-  P.has_logits = L.has_logits ? 1 : 0;
-  CK(cudaMemsetAsync(L.bar, 0, sizeof(uint32_t), s));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((uint32_t)num_sms());
-  cfg.blockDim = dim3(GV_THREADS);
-  cfg.dynamicSmemBytes = SK_SMEM;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  CK(cudaLaunchKernelEx(&cfg, k_step, P));
-}
-
 // ---------------------------------------------------------------------------
 // Prefill on the tensor cores
 // ---------------------------------------------------------------------------
@@ -1784,6 +1639,5 @@ void sampler_init() {
   CK(cudaFuncSetAttribute(k_topk2, cudaFuncAttributeMaxDynamicSharedMemorySize, TK_MERGE * 8));
 }
 
-void step_init() { CK(cudaFuncSetAttribute(k_step, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM)); }
 
 }  // namespace fz

@@ -46,7 +46,7 @@ struct StepState {
 enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_LOGITS = 3 };
 
 // Step-kernel timeline record (see trace_install): one per CTA per launch.
-enum TraceTag : uint32_t { TR_GEMV = 0, TR_ATTN = 8, TR_COMBINE = 9, TR_STEP = 16 };  // TR_GEMV + epilogue, TR_STEP + phase kind
+enum TraceTag : uint32_t { TR_GEMV = 0, TR_ATTN = 8, TR_COMBINE = 9 };  // TR_GEMV + epilogue
 struct TraceRec {
   uint32_t tag, cta, aux, pad;
   uint64_t t[6];
@@ -113,42 +113,6 @@ int num_sms();
 void kernels_init();
 void attention_init();
 
-// ---- persistent decode step (one kernel per token) -------------------------
-enum StepPhaseKind : int { SP_EMBED = 0, SP_GEMV = 1, SP_ATTN = 2 };
-struct StepPhase {
-  int kind = SP_GEMV;
-  GemvLaunch g;
-  AttnLaunch a{};
-};
-struct StepLaunch {
-  const StepPhase* phases = nullptr;
-  uint32_t nph = 0;
-  StepState* state = nullptr;
-  uint32_t* bar = nullptr;       // grid barrier counter (device, 4 bytes)
-  uint32_t* attn_cnt = nullptr;  // one counter per KV head (device, zeroed once)
-  float* partials = nullptr;     // attention_partial_floats(nh, nkv, hd, step_attention_splits(nkv))
-  const float* rope_cs = nullptr;
-  uint32_t max_ctx = 0;
-  DevMat emb;
-  float* x = nullptr;
-  const uint32_t* forced = nullptr;
-  uint32_t* ids_out = nullptr;
-  bool has_logits = false;
-};
-uint32_t step_attention_splits(uint32_t n_kv);
-// Per-CTA plan of one step variant: phase records and weight-stage lists,
-// as one blob for device memory (offsets into it below).
-struct StepPlan {
-  std::vector<uint8_t> blob;
-  size_t off_stage_first = 0, off_stages = 0;
-  uint32_t nph = 0, ring_bytes = 0, u_bytes = 0;
-};
-// Check every limit and build the plan of L.
-StepPlan step_plan_build(const StepLaunch& L);
-// Zero the barrier counter and launch the step kernel (one token); plan_dev
-// holds plan.blob.
-void launch_step(const StepLaunch& L, const StepPlan& plan, const void* plan_dev, cudaStream_t s);
-void step_init();
 
 // ---- sampling (src/sampler.rs) ------------------------------------------------
 // Top k (k <= topk_max()) of the repeat-penalised, temperature-scaled logits as

@@ -83,7 +83,7 @@ struct fz_model {
   // activations (f32) and the run records GEMVs read (see kernels.cu)
   DevBuf x, qkv, ctx, h, logits;
   DevBuf runs_ctx, runs_h;  // attention output and ffn hidden as run records
-  DevBuf trace;             // step-kernel timeline (FURNACE_B200_TRACE=<file>)
+  DevBuf trace;             // decode-step timeline (FURNACE_B200_TRACE=<file>)
   std::string trace_path;
   // tensor parallelism: this rank's share (world == 1: everything)
   int rank = 0, world = 1;
@@ -103,8 +103,6 @@ struct fz_kv {
   fz_model* m = nullptr;
   uint32_t max_ctx = 0, len = 0, splits = 0;
   DevBuf k, v, rope_cs, partials, state, forced, ids;
-  DevBuf plan_full, plan_layers, bar, attn_cnt;  // persistent step kernel
-  StepPlan sp_full, sp_layers;
   cudaGraphExec_t g_full = nullptr, g_layers = nullptr;
   ~fz_kv() {
     if (g_full) cudaGraphExecDestroy(g_full);
@@ -489,59 +487,6 @@ void prefill_tokens(fz_kv* kv, const uint32_t* tokens, uint32_t n, uint32_t pos0
   }
 }
 
-// The step's phases for the persistent step kernel: embed, then per layer
-// qkv, attention, o_proj, gate_up, down, then lm_head when with_logits.
-std::vector<StepPhase> step_phases(fz_kv* kv, bool with_logits) {
-  const fz_config& c = kv->m->cfg;
-  std::vector<GemvLaunch> gl = step_gemvs(kv);
-  const uint32_t splits = step_attention_splits(kv->m->nkv_l);
-  std::vector<StepPhase> ph;
-  StepPhase e;
-  e.kind = SP_EMBED;
-  ph.push_back(e);
-  for (uint32_t li = 0; li < c.n_layers; li++) {
-    for (int k = 0; k < 4; k++) {
-      StepPhase g;
-      g.kind = SP_GEMV;
-      g.g = gl[4 * li + k];
-      g.g.next = nullptr;
-      ph.push_back(g);
-      if (k == 0) {
-        StepPhase a;
-        a.kind = SP_ATTN;
-        a.a = layer_attention(kv, li, splits);
-        ph.push_back(a);
-      }
-    }
-  }
-  if (with_logits) {
-    StepPhase g;
-    g.kind = SP_GEMV;
-    g.g = gl[4 * c.n_layers];
-    g.g.next = nullptr;
-    ph.push_back(g);
-  }
-  return ph;
-}
-
-StepLaunch step_launch(fz_kv* kv, const std::vector<StepPhase>& ph, bool with_logits) {
-  fz_model* m = kv->m;
-  StepLaunch L;
-  L.phases = ph.data();
-  L.nph = (uint32_t)ph.size();
-  L.state = kv->state.as<StepState>();
-  L.bar = kv->bar.as<uint32_t>();
-  L.attn_cnt = kv->attn_cnt.as<uint32_t>();
-  L.partials = kv->partials.as<float>();
-  L.rope_cs = kv->rope_cs.as<float>();
-  L.max_ctx = kv->max_ctx;
-  L.emb = m->embd;
-  L.x = m->x.as<float>();
-  L.forced = kv->forced.as<uint32_t>();
-  L.ids_out = kv->ids.as<uint32_t>();
-  L.has_logits = with_logits;
-  return L;
-}
 
 // ---- sampling (src/sampler.rs) ------------------------------------------------
 // Softmax, top-p, renormalisation and the draw over candidates (id, l / temp)
@@ -641,46 +586,16 @@ uint32_t sample_device(fz_model* m, fz_sampler* s, const uint32_t* recent, uint3
   return sampler_finish(s, cand);
 }
 
-// The step is captured as separate kernels (programmatic dependent launches)
-// unless FURNACE_B200_STEP=fused selects the persistent step kernel, which is
-// parity-tested but slower on B200 today: its grid barriers (~2.6 us each,
-// five per layer) and latency-bound attention phase cost more than the kernel
-// boundaries they replace.
-bool fused_step() {
-  const char* e = getenv("FURNACE_B200_STEP");
-  return e && strcmp(e, "fused") == 0;
-}
-
+// The step is captured as separate kernels chained by programmatic dependent
+// launches: one graph with the logits (lm_head + argmax), one without.
 void build_graphs(fz_kv* kv) {
   if (kv->g_full) return;
   cudaStream_t s = kv->m->stream;
-  const bool fused = fused_step() && kv->m->world == 1;
-  std::vector<StepPhase> ph[2];
-  if (fused) {
-    step_init();
-    kv->bar.alloc(16);
-    kv->attn_cnt.alloc(4 * kv->m->nkv_l + 16);
-    CK(cudaMemset(kv->attn_cnt.p, 0, kv->attn_cnt.n));
-    for (int variant = 0; variant < 2; variant++) {
-      ph[variant] = step_phases(kv, variant == 0);
-      DevBuf& plan = variant == 0 ? kv->plan_full : kv->plan_layers;
-      StepPlan& sp = variant == 0 ? kv->sp_full : kv->sp_layers;
-      sp = step_plan_build(step_launch(kv, ph[variant], variant == 0));
-      plan.alloc(sp.blob.size());
-      CK(cudaMemcpy(plan.p, sp.blob.data(), sp.blob.size(), cudaMemcpyHostToDevice));
-      sp.blob.clear();
-      sp.blob.shrink_to_fit();
-    }
-  }
   for (int variant = 0; variant < 2; variant++) {
     cudaGraph_t g;
     CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
     try {
-      if (fused)
-        launch_step(step_launch(kv, ph[variant], variant == 0), variant == 0 ? kv->sp_full : kv->sp_layers,
-                    (variant == 0 ? kv->plan_full : kv->plan_layers).p, s);
-      else
-        record_step(kv, variant == 0, s);
+      record_step(kv, variant == 0, s);
     } catch (...) {
       cudaStreamEndCapture(s, &g);
       if (g) cudaGraphDestroy(g);
@@ -1017,7 +932,7 @@ std::unique_ptr<fz_model> load_model(const fz_file* f, int rank, int world, cons
     need(id != nullptr, "tensor parallelism needs an NCCL id");
     nccl_check(nccl().CommInitRank(&m->comm, world, *id, rank), "ncclCommInitRank");
   }
-  // optional timeline of every step kernel's CTAs, written to the named
+  // optional timeline of every decode-step kernel's CTAs, written to the named
   // file by fz_model_free (the records of the last fz_decode_greedy call)
   if (const char* tp = getenv("FURNACE_B200_TRACE")) {
     const uint32_t cap = 1u << 20;

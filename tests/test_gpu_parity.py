@@ -220,26 +220,6 @@ def test_greedy_128_steps_tiny(tiny):
     _greedy_parity(tiny, 9, 128, seed=4)
 
 
-def test_greedy_128_steps_tiny_step_kernel(tiny, monkeypatch):
-    """The persistent step kernel (one launch per token) reaches the same ids
-    and logits; the variant is chosen when a KV cache builds its graphs."""
-    monkeypatch.setenv("FURNACE_B200_STEP", "fused")
-    _greedy_parity(tiny, 9, 128, seed=4)
-
-
-def test_forward_step_kernel_matches_oracle(tiny, monkeypatch):
-    monkeypatch.setenv("FURNACE_B200_STEP", "fused")
-    f, dev, ref = _models(tiny)
-    ids = synth.prompt_ids(ref.vocab, 7, seed=3)
-    kd, kr = fz.KvCache(dev, 64), ref.kv_new(64)
-    got, am = dev.forward(ids, kd)
-    _check_logits(got, ref.forward_cached(ids, kr), "prefill")
-    for layer in range(ref.n_layers):
-        for which in (0, 1):
-            a, b = kd.read(layer, which, 7), kr.read(layer, which, 7)
-            assert np.abs(a - b).max() <= 1e-4 * max(1.0, np.abs(b).max()), (layer, which)
-
-
 def test_greedy_stop_ids(tiny, orc):
     ref = orc.Model(tiny)
     ids = synth.prompt_ids(ref.vocab, 5, seed=6)
@@ -272,12 +252,6 @@ def test_sampled_generate_matches_oracle(tiny, temp, top_k, top_p, pen):
 @pytest.mark.slow
 def test_greedy_128_steps_c1():
     """Qwen2.5-0.5B shape, Q8_0, 32-token prompt, 128 greedy steps."""
-    _greedy_parity(synth.ensure("c1"), 32, 128)
-
-
-@pytest.mark.slow
-def test_greedy_128_steps_c1_step_kernel(monkeypatch):
-    monkeypatch.setenv("FURNACE_B200_STEP", "fused")
     _greedy_parity(synth.ensure("c1"), 32, 128)
 
 
