@@ -459,12 +459,20 @@ constexpr int GV_NT = GV_CWARPS * 32;              // consumer threads
 constexpr int GV_MAX_SLOTS = 8;
 constexpr int GV_MAX_CH = 32;                      // chunks per row (cols <= 65536)
 
+// Chunk geometry of one matrix (layout.cuh), computed on the host: chunk c
+// covers units [cu0[c], cu0[c+1]) and starts off[c] bytes into a row.
+struct GvChunks {
+  uint16_t cu0[GV_MAX_CH + 1];
+  uint32_t off[GV_MAX_CH + 1];
+};
+
 struct GvSeg {
   const uint8_t* w;
   uint32_t rows, dtype, cols;
   const float* bias;
   float* out;
   uint32_t cta_begin, cta_end, align;
+  GvChunks ch;
 };
 
 struct GvNext {
@@ -540,11 +548,11 @@ struct ChunkInfo {
 };
 
 __device__ __forceinline__ void chunk_info(const StageIter& it, uint32_t c, ChunkInfo* ci) {
-  uint32_t u0 = lay_cu0(it.dt, it.cols, c), u1 = lay_cu0(it.dt, it.cols, c + 1);
-  ci->cu0 = u0;
-  ci->nu = u1 - u0;
-  ci->tb = lay_chunk_bytes(it.dt, u1 - u0);
-  ci->plane = it.s->w + (uint64_t)it.s->rows * lay_chunk_off(it.dt, it.cols, c);
+  const GvChunks& ch = it.s->ch;
+  ci->cu0 = ch.cu0[c];
+  ci->nu = ch.cu0[c + 1] - ch.cu0[c];
+  ci->tb = ch.off[c + 1] - ch.off[c];
+  ci->plane = it.s->w + (uint64_t)it.s->rows * ch.off[c];
 }
 
 // ---- dot-product helpers ----------------------------------------------------
@@ -1080,7 +1088,13 @@ static void fill_segs(const GemvLaunch& g, GvSeg* out) {
     share = std::max<uint32_t>(1, std::min(share, units));
     uint32_t per = (units + share - 1) / share;
     uint32_t n = (units + per - 1) / per;
-    out[i] = GvSeg{w.ptr, w.rows, w.dtype, w.cols, g.seg[i].bias, g.seg[i].out, begin, begin + n, align};
+    out[i] = GvSeg{w.ptr, w.rows, w.dtype, w.cols, g.seg[i].bias, g.seg[i].out, begin, begin + n, align, {}};
+    const uint32_t nch = lay_nch(w.cols);
+    if (nch > GV_MAX_CH) fail(FZ_EINVAL, "gemv: input width %u too large", w.cols);
+    for (uint32_t c = 0; c <= nch; c++) {
+      out[i].ch.cu0[c] = (uint16_t)lay_cu0(w.dtype, w.cols, c);
+      out[i].ch.off[c] = lay_chunk_off(w.dtype, w.cols, c);
+    }
     begin += n;
   }
 }
