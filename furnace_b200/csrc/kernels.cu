@@ -1361,13 +1361,16 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
 }
 
 // Merge the split partials: ctx[h][d] = sum_s w_s acc_s[d] / sum_s w_s l_s,
-// w_s = exp(m_s - max_s m_s).  Grid nh, block hd.  Each thread reads its
-// split values as consecutive float4s, all issued before they are used.
+// w_s = exp(m_s - max_s m_s).  Grid nh, block hd.  Every load of a thread --
+// its acc values and, per warp, the head's split statistics -- is issued
+// right after the wait, so the merge costs one L2 round trip; each warp
+// reduces the statistics itself (no block barrier before the sums).
 constexpr int AT_MAXS = 256;
+constexpr int AT_ACC_REGS = 24;  // float4 acc loads held in registers (splits <= 96 in one pass)
 __global__ void k_attn_combine(const float* __restrict__ partials, float* __restrict__ ctx, XRun* __restrict__ ctx_runs,
                                uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t S, StepState* st, uint32_t run0) {
-  __shared__ float ws[AT_MAXS], ls[AT_MAXS];
-  __shared__ float s_den;
+  __shared__ float ws[4][AT_MAXS];
+  __shared__ float sv[128];
   Tracer tr;
   if (threadIdx.x == 0) {
     tr.begin(TR_COMBINE, gridDim.x);
@@ -1377,58 +1380,56 @@ __global__ void k_attn_combine(const float* __restrict__ partials, float* __rest
   if (threadIdx.x == 0) tr.mark(1);
   (void)st;
   const uint32_t G = nh / nkv, h = blockIdx.x, kvh = h / G, hg = h % G, d = threadIdx.x;
+  const uint32_t lane = d & 31, warp = d >> 5;
   const uint32_t Spad = (S + 3) & ~3u;
   const float2* stats = reinterpret_cast<const float2*>(partials) + ((uint64_t)kvh * G + hg) * S;
   const float4* acc4 =
       reinterpret_cast<const float4*>(partials + ((2 * (uint64_t)nkv * G * S + 3) & ~3ull) + (((uint64_t)h) * hd + d) * Spad);
-  // all of this thread's acc values in flight at once (S <= 64 in one pass)
-  float4 av[16];
+  float4 av[AT_ACC_REGS];
 #pragma unroll
-  for (int k = 0; k < 16; k++) av[k] = (4u * k < Spad) ? acc4[k] : make_float4(0.f, 0.f, 0.f, 0.f);
-  for (uint32_t s2 = threadIdx.x; s2 < S; s2 += blockDim.x) {
-    float2 v = stats[s2];
-    ws[s2] = v.x;
-    ls[s2] = v.y;
+  for (int k = 0; k < AT_ACC_REGS; k++) av[k] = (4u * k < Spad) ? acc4[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+  float2 sm[AT_MAXS / 32];
+#pragma unroll
+  for (int k = 0; k < AT_MAXS / 32; k++) {
+    const uint32_t s2 = lane + 32 * k;
+    sm[k] = s2 < S ? stats[s2] : make_float2(-INFINITY, 0.f);
   }
-  for (uint32_t s2 = S + threadIdx.x; s2 < Spad; s2 += blockDim.x) ws[s2] = ls[s2] = 0.f;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float M = -INFINITY;
-    for (uint32_t s2 = threadIdx.x; s2 < S; s2 += 32) M = fmaxf(M, ws[s2]);
+  float M = -INFINITY;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    float den = 0.f;
-    for (uint32_t s2 = threadIdx.x; s2 < S; s2 += 32) {
-      float ms = ws[s2];
-      float w = ms == -INFINITY ? 0.f : expf(ms - M);
-      ws[s2] = w;
-      den = fmaf(w, ls[s2], den);
-    }
+  for (int k = 0; k < AT_MAXS / 32; k++) M = fmaxf(M, sm[k].x);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-    if (threadIdx.x == 0) s_den = den;
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float den = 0.f;
+#pragma unroll
+  for (int k = 0; k < AT_MAXS / 32; k++) {
+    const uint32_t s2 = lane + 32 * k;
+    const float w = sm[k].x == -INFINITY ? 0.f : expf(sm[k].x - M);
+    if (s2 < Spad) ws[warp][s2] = w;
+    den = fmaf(w, sm[k].y, den);
   }
-  __syncthreads();
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+  __syncwarp();
+  const float* w = ws[warp];
   float num = 0.f;
 #pragma unroll
-  for (int k = 0; k < 16; k++) {
+  for (int k = 0; k < AT_ACC_REGS; k++) {
     if (4u * k >= Spad) break;
-    num = fmaf(ws[4 * k], av[k].x, num);
-    num = fmaf(ws[4 * k + 1], av[k].y, num);
-    num = fmaf(ws[4 * k + 2], av[k].z, num);
-    num = fmaf(ws[4 * k + 3], av[k].w, num);
+    num = fmaf(w[4 * k], av[k].x, num);
+    num = fmaf(w[4 * k + 1], av[k].y, num);
+    num = fmaf(w[4 * k + 2], av[k].z, num);
+    num = fmaf(w[4 * k + 3], av[k].w, num);
   }
-  for (uint32_t k = 16; 4 * k < Spad; k++) {
+  for (uint32_t k = AT_ACC_REGS; 4 * k < Spad; k++) {
     float4 a4 = acc4[k];
-    num = fmaf(ws[4 * k], a4.x, num);
-    num = fmaf(ws[4 * k + 1], a4.y, num);
-    num = fmaf(ws[4 * k + 2], a4.z, num);
-    num = fmaf(ws[4 * k + 3], a4.w, num);
+    num = fmaf(w[4 * k], a4.x, num);
+    num = fmaf(w[4 * k + 1], a4.y, num);
+    num = fmaf(w[4 * k + 2], a4.z, num);
+    num = fmaf(w[4 * k + 3], a4.w, num);
   }
-  const float v = __fdiv_rn(num, s_den);
+  const float v = __fdiv_rn(num, den);
   ctx[(uint64_t)h * hd + d] = v;
   // run records of ctx (the o_proj input): 8 runs per 128-wide head
-  __shared__ float sv[128];
   sv[d] = v;
   __syncthreads();
   values_to_runs(sv, hd, nullptr, ctx_runs, run0 + h * (hd / 16), d, hd);
