@@ -17,11 +17,13 @@ e2e   : the same metric through the public C-ABI call (fz_decode_greedy)
         restatement in oracle/, the reference itself cannot be built here)
         timed on the host cores, one decode token per step.
 
-With --gpus N > 1 (torchrun, one process per GPU) the model is split
-tensor-parallel over TP = the largest of N, N/2, ... that divides the head and
-KV-head counts (C3: 4), one NCCL communicator per TP group, and N / TP groups
-decode independent streams: value = total tokens/s of all groups; scaling
-"strong" when one group spans all N GPUs.
+With --gpus N > 1 (torchrun, one process per GPU) the ranks form N / TP
+groups of --tp TP consecutive ranks (default 1).  A group decodes one stream,
+tensor-parallel over its TP GPUs (one NCCL communicator per group), and the
+groups decode independent streams: value = total tokens/s of all groups;
+scaling "strong" when one group spans all N GPUs, else "weak".  The default
+(independent replicas) is the highest whole-job throughput for a model that
+fits one GPU; --tp N measures one stream split over all N GPUs.
 """
 
 from __future__ import annotations
@@ -54,6 +56,7 @@ def parse():
     ap.add_argument("--config", default=CONFIG)
     ap.add_argument("--prefill", type=int, default=PREFILL)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel group size (divides --gpus)")
     return ap.parse_args()
 
 
@@ -283,9 +286,9 @@ def run_ours(args, dist):
     cud.set_device(dev)
     f = fz.GgufFile.open(path)
     # tensor-parallel groups of `tp` consecutive ranks (see the module docstring)
-    tp = dist.world
-    while tp > 1 and (spec.n_heads % tp or spec.n_kv_heads % tp or dist.world % tp):
-        tp //= 2
+    tp = max(1, min(args.tp, dist.world))
+    if dist.world % tp or spec.n_heads % tp or spec.n_kv_heads % tp:
+        raise SystemExit(f"--tp {tp} must divide --gpus {dist.world} and the head counts")
     groups = dist.world // tp
     if tp > 1:
         ids = dist.bcast([fz.tp_unique_id() for _ in range(groups)] if dist.rank == 0 else None)

@@ -1500,6 +1500,83 @@ void launch_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, b
 // ---------------------------------------------------------------------------
 // Persistent decode step
 // ---------------------------------------------------------------------------
+// Tensor-parallel all-reduce of the residual stream as a one-shot push over
+// peer memory (NVLink): every rank stores its partial x into its slot of
+// every rank's receive buffer, each element as one 8-byte word
+// {value, epoch} (an 8-byte store is seen whole or not at all), then each
+// rank polls its own slots until every word carries this call's epoch and
+// sums the W slots in rank order, so every rank holds the identical sum.  No
+// fence or flag round trip: the data is its own flag.  A rank's buffer
+// (exported by CUDA IPC) is uint2 recv[2][W][H]; the parity of the call picks
+// the half, so a rank one call ahead never overwrites a slot still being read.
+// cnt[b] counts CTA b's calls on this rank; all ranks make the same calls, so
+// the epochs agree.  A word that does not arrive within 2 s sets error 7.
+// ---------------------------------------------------------------------------
+constexpr long long AR_SPIN_NS = 2000000000ll;
+
+__device__ __forceinline__ void st_volatile_u2(uint2* p, uint2 v) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
+}
+__device__ __forceinline__ uint2 ld_volatile_u2(const uint2* p) {
+  uint2 v;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(256) k_ar_push(float* __restrict__ x, uint32_t H, uint32_t W, uint32_t rank,
+                                                 ArPeers peers, uint32_t* __restrict__ cnt, StepState* st) {
+  __shared__ uint32_t s_e, s_ok;
+  const uint32_t b = blockIdx.x, tid = threadIdx.x;
+  if (tid == 0) {
+    pdl_trigger();
+    s_e = cnt[b] + 1;
+    s_ok = 1;
+  }
+  pdl_wait();  // x holds this rank's partial
+  __syncthreads();
+  const uint32_t e = s_e, par = e & 1;
+  const uint32_t per = (H + gridDim.x - 1) / gridDim.x;
+  const uint32_t i0 = min(b * per, H), i1 = min(i0 + per, H);
+  // 1. push {value, epoch} of this CTA's range into every rank's slot `rank`
+  for (uint32_t i = i0 + tid; i < i1; i += blockDim.x) {
+    const uint2 w = make_uint2(__float_as_uint(x[i]), e);
+    for (uint32_t q = 0; q < W; q++)
+      st_volatile_u2(reinterpret_cast<uint2*>(peers.buf[q]) + ((uint64_t)par * W + rank) * H + i, w);
+  }
+  // 2. poll the W slots of this range and sum them in rank order
+  const uint2* recv = reinterpret_cast<const uint2*>(peers.buf[rank]) + (uint64_t)par * W * H;
+  for (uint32_t i = i0 + tid; i < i1; i += blockDim.x) {
+    float acc = 0.f;
+    for (uint32_t q = 0; q < W; q++) {
+      const uint2* wp = recv + (uint64_t)q * H + i;
+      uint2 w = ld_volatile_u2(wp);
+      if (w.y != e) {
+        const uint64_t t0 = gtimer();
+        while ((w = ld_volatile_u2(wp)).y != e) {
+          if (gtimer() - t0 > (uint64_t)AR_SPIN_NS || !*(volatile uint32_t*)&s_ok) {
+            atomicExch(&st->error, 7u);
+            s_ok = 0;
+            break;
+          }
+        }
+      }
+      acc += __uint_as_float(w.x);
+    }
+    x[i] = acc;
+  }
+  __syncthreads();
+  if (tid == 0 && s_ok) cnt[b] = e;
+}
+
+uint64_t ar_buffer_bytes(uint32_t H, uint32_t W) { return 2ull * W * H * 8; }
+
+void launch_ar_push(float* x, uint32_t H, uint32_t W, uint32_t rank, const ArPeers& peers, uint32_t* cnt,
+                    StepState* st, cudaStream_t s) {
+  if (W > AR_MAX_RANKS) fail(FZ_EINVAL, "all-reduce: %u ranks > %d", W, AR_MAX_RANKS);
+  launch_pdl(k_ar_push, dim3(AR_CTAS), dim3(256), 0, s, x, H, W, rank, peers, cnt, st);
+}
+
+// ---------------------------------------------------------------------------
 // Prefill on the tensor cores
 // ---------------------------------------------------------------------------
 #include "prefill.cuh"

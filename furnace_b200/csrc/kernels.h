@@ -106,6 +106,19 @@ void launch_attention(const AttnLaunch& a, cudaStream_t s);
 uint32_t attention_splits(uint32_t n_kv);
 uint64_t attention_partial_floats(uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t splits);
 
+// One-shot push all-reduce (sum) of x[H] over W tensor-parallel ranks through
+// peer memory; buf[q] is rank q's receive buffer of ar_buffer_bytes(H, W)
+// bytes as mapped in this process (buf[rank] the local one, zeroed once);
+// cnt holds AR_CTAS zeroed call counters of this rank.
+constexpr int AR_MAX_RANKS = 8;
+constexpr int AR_CTAS = 8;
+struct ArPeers {
+  float* buf[AR_MAX_RANKS];
+};
+uint64_t ar_buffer_bytes(uint32_t H, uint32_t W);
+void launch_ar_push(float* x, uint32_t H, uint32_t W, uint32_t rank, const ArPeers& peers, uint32_t* cnt,
+                    StepState* st, cudaStream_t s);
+
 // Step bookkeeping after the logits (argmax -> ids_out, next token, pos++).
 void launch_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, bool has_logits, cudaStream_t s);
 

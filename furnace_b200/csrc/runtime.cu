@@ -88,6 +88,11 @@ struct fz_model {
   // tensor parallelism: this rank's share (world == 1: everything)
   int rank = 0, world = 1;
   ncclComm_t comm = nullptr;
+  // one-shot push all-reduce: this rank's receive buffer (exported by CUDA
+  // IPC), the peers' buffers as mapped here, per-CTA call counters
+  DevBuf ar_buf, ar_cnt;
+  ArPeers ar_peers{};
+  bool ar_p2p = false;
   fz_tp_slice sl{};
   uint32_t nh_l = 0, nkv_l = 0, qd_l = 0, kd_l = 0;
   std::vector<uint32_t> o_off;  // per layer: ctx[0]'s column within o_proj's block-aligned input
@@ -332,8 +337,15 @@ AttnLaunch layer_attention(fz_kv* kv, uint32_t li, uint32_t splits) {
 }
 
 // Sum of the ranks' residual-stream partials (tensor parallelism).
-void tp_allreduce_x(fz_model* m, cudaStream_t s) {
+// Sum of the ranks' residual-stream partials (tensor parallelism): the
+// one-shot push over peer memory, or NCCL where peer mappings are unavailable
+// or FURNACE_B200_TP_ALLREDUCE=nccl asks for it.
+void tp_allreduce_x(fz_model* m, StepState* st, cudaStream_t s) {
   if (m->world == 1) return;
+  if (m->ar_p2p) {
+    launch_ar_push(m->x.as<float>(), m->cfg.hidden, m->world, m->rank, m->ar_peers, m->ar_cnt.as<uint32_t>(), st, s);
+    return;
+  }
   nccl_check(nccl().AllReduce(m->x.p, m->x.p, m->cfg.hidden, ncclFloat32, ncclSum, m->comm, s), "ncclAllReduce");
 }
 
@@ -365,14 +377,14 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
     H(FZ_OP_ATTN, false);
     H(FZ_OP_OPROJ, true);
     launch_gemv(gl[4 * li + 1], s);
-    tp_allreduce_x(m, s);
+    tp_allreduce_x(m, st, s);
     H(FZ_OP_OPROJ, false);
     H(FZ_OP_GATEUP, true);
     launch_gemv(gl[4 * li + 2], s);
     H(FZ_OP_GATEUP, false);
     H(FZ_OP_DOWN, true);
     launch_gemv(gl[4 * li + 3], s);
-    tp_allreduce_x(m, s);
+    tp_allreduce_x(m, st, s);
     H(FZ_OP_DOWN, false);
   }
   if (with_logits) {
@@ -747,6 +759,48 @@ namespace {
 
 // Model::load (src/model.rs:520-552) for rank `rank` of `world`: the rank's
 // slice of every matrix, uploaded raw and repacked into the device layout.
+// Receive buffers of the one-shot all-reduce: every rank exports its buffer
+// by CUDA IPC, the handles travel by NCCL all-gather, and each rank maps the
+// others'.  Collective: every rank calls it once while loading.
+void tp_p2p_setup(fz_model* m) {
+  const char* e = getenv("FURNACE_B200_TP_ALLREDUCE");
+  const bool want = !(e && strcmp(e, "nccl") == 0);
+  const uint32_t W = (uint32_t)m->world;
+  need(W <= (uint32_t)AR_MAX_RANKS, "tensor parallelism over %u ranks > %d", W, AR_MAX_RANKS);
+  m->ar_buf.alloc(ar_buffer_bytes(m->cfg.hidden, W));
+  CK(cudaMemset(m->ar_buf.p, 0, m->ar_buf.n));
+  m->ar_cnt.alloc(AR_CTAS * 4);
+  CK(cudaMemset(m->ar_cnt.p, 0, m->ar_cnt.n));
+  // every rank takes part in the exchange (the same collective steps on all
+  // ranks); a rank that cannot export marks its handle invalid
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  std::vector<uint8_t> mine(72, 0), all(72 * W);
+  cudaIpcMemHandle_t h{};
+  const bool ok = want && cudaIpcGetMemHandle(&h, m->ar_buf.p) == cudaSuccess;
+  cudaGetLastError();
+  memcpy(mine.data(), &h, 64);
+  mine[64] = ok ? 1 : 0;
+  DevBuf d(72ull * W);
+  CK(cudaMemcpy(d.as<uint8_t>() + 72ull * m->rank, mine.data(), 72, cudaMemcpyHostToDevice));
+  nccl_check(nccl().AllGather(d.as<uint8_t>() + 72ull * m->rank, d.p, 72, ncclUint8, m->comm, m->stream),
+             "ncclAllGather");
+  CK(cudaStreamSynchronize(m->stream));
+  CK(cudaMemcpy(all.data(), d.p, all.size(), cudaMemcpyDeviceToHost));
+  bool all_ok = true;
+  for (uint32_t q = 0; q < W; q++) all_ok = all_ok && all[72 * q + 64] == 1;
+  if (!all_ok) return;  // NCCL all-reduce
+  m->ar_peers.buf[m->rank] = m->ar_buf.as<float>();
+  for (uint32_t q = 0; q < W; q++) {
+    if (q == (uint32_t)m->rank) continue;
+    cudaIpcMemHandle_t hq;
+    memcpy(&hq, all.data() + 72 * q, 64);
+    void* p = nullptr;
+    CK(cudaIpcOpenMemHandle(&p, hq, cudaIpcMemLazyEnablePeerAccess));
+    m->ar_peers.buf[q] = static_cast<float*>(p);
+  }
+  m->ar_p2p = true;
+}
+
 std::unique_ptr<fz_model> load_model(const fz_file* f, int rank, int world, const ncclUniqueId* id, int device) {
   need(f != nullptr, "null argument");
   const GgufFile& g = *f->g;
@@ -931,6 +985,7 @@ std::unique_ptr<fz_model> load_model(const fz_file* f, int rank, int world, cons
   if (world > 1) {
     need(id != nullptr, "tensor parallelism needs an NCCL id");
     nccl_check(nccl().CommInitRank(&m->comm, world, *id, rank), "ncclCommInitRank");
+    tp_p2p_setup(m.get());
   }
   // optional timeline of every decode-step kernel's CTAs, written to the named
   // file by fz_model_free (the records of the last fz_decode_greedy call)
@@ -990,6 +1045,9 @@ void fz_model_free(fz_model* m) {
     cudaStreamSynchronize(m->stream);
     cudaStreamDestroy(m->stream);
   }
+  if (m->ar_p2p)
+    for (int q = 0; q < m->world; q++)
+      if (q != m->rank && m->ar_peers.buf[q]) cudaIpcCloseMemHandle(m->ar_peers.buf[q]);
   if (m->comm) {
     try {
       nccl().CommDestroy(m->comm);
