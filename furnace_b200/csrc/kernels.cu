@@ -496,6 +496,12 @@ struct GvParams {
   GvNext next;
   uint32_t idx_base;     // EPI_LOGITS: global index of row 0
   uint32_t chunked_rec;  // in_runs stream per K-chunk through two buffers (long inputs)
+  // tensor-parallel exchange through peer memory (GemvLaunch::ar_*)
+  ArPeers ar_peers;
+  uint32_t ar_w, ar_rank, ar_k, ar_h;
+  const uint32_t* ar_base;
+  int ar_push, ar_pull;
+  float* x_out;          // ar_pull: this CTA's slice of the summed x goes here
 };
 constexpr uint32_t GV_CREC = 32 * 256;  // run records of one chunk (<= 32 units)
 
@@ -787,6 +793,64 @@ __device__ bool gv_consume(const GvParams& p, const StageIter& it, const ChunkIn
   return true;
 }
 
+// ---- tensor-parallel exchange of the residual stream -----------------------
+// After o_proj and after down every rank holds a partial of the new residual
+// x (rank 0's includes the old x).  The GEMV epilogue stores each row's
+// partial into the rank's slot of every rank's receive buffer as one 8-byte
+// word {value, epoch} (an 8-byte store is seen whole or not at all), over
+// NVLink.  The next RMS-normalised GEMV (gate_up, qkv, lm_head) polls its
+// own buffer until every word of every slot carries the exchange's epoch and
+// sums the W slots in rank order as its input, so every rank computes the
+// identical x; each of its CTAs also writes its slice of x for the next
+// residual add.  No fence or flag round trip: the data is its own flag.  A
+// buffer (exported by CUDA IPC) is uint2 recv[2][W][H]; the epoch's parity
+// picks the half, so a rank one exchange ahead never overwrites a slot that
+// is still being read (a rank's exchange e+2 needs every rank's e+1, which
+// each rank sends only after it read e).  epoch = *ar_base + k + 1, where
+// ar_base advances by the step's exchange count at every step's end and k
+// numbers the exchanges inside the step; all ranks run the same steps.  A
+// word that does not arrive within 2 s sets error 7.
+constexpr long long AR_SPIN_NS = 2000000000ll;
+
+uint64_t ar_buffer_bytes(uint32_t H, uint32_t W) { return 2ull * W * H * 8; }
+
+__device__ __forceinline__ void st_volatile_u2(uint2* p, uint2 v) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
+}
+__device__ __forceinline__ uint4 ld_volatile_u4(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+// Elements 4i..4i+3 of the exchanged x: the sum of the W ranks' words in rank
+// order, each word polled until it carries epoch e.  False on the time limit.
+__device__ __forceinline__ bool ar_pull4(const GvParams& p, uint32_t e, uint32_t i, float4* out) {
+  const uint4* slot = reinterpret_cast<const uint4*>(p.ar_peers.buf[p.ar_rank]) + ((uint64_t)(e & 1) * p.ar_w * p.ar_h) / 2;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (uint32_t q = 0; q < p.ar_w; q++) {
+    const uint4* w = slot + ((uint64_t)q * p.ar_h) / 2 + 2 * i;  // words 4i, 4i+1 | 4i+2, 4i+3
+    uint4 a = ld_volatile_u4(w), b = ld_volatile_u4(w + 1);
+    if (a.y != e || a.w != e || b.y != e || b.w != e) {
+      const uint64_t t0 = gtimer();
+      while (a.y != e || a.w != e || b.y != e || b.w != e) {
+        if (gtimer() - t0 > (uint64_t)AR_SPIN_NS) return false;
+        a = ld_volatile_u4(w);
+        b = ld_volatile_u4(w + 1);
+      }
+    }
+    acc.x += __uint_as_float(a.x);
+    acc.y += __uint_as_float(a.z);
+    acc.z += __uint_as_float(b.x);
+    acc.w += __uint_as_float(b.z);
+  }
+  *out = acc;
+  return true;
+}
+
 __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ GvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -839,7 +903,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
       const ChunkInfo ci = chunks[c];
       for (uint32_t ra = it.r0; ra < it.r1; ra += GV_ROWS, i++) {
         if (i >= p.slots && !mbar_wait(&empty[slot], phase ^ 1)) {
-          atomicExch(&p.state->error, 4u);
+          if (p.state) atomicExch(&p.state->error, 4u);
           return;
         }
         uint32_t bytes = (min(ra + GV_ROWS, it.r1) - ra) * ci.tb;
@@ -914,9 +978,25 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
       bulk_g2s(rec, p.in_runs, NX * 64, &recbar, 0ull);
     }
     if (!mbar_wait(&recbar, 0)) {
-      if (lane == 0) atomicExch(&p.state->error, 3u);
+      if (lane == 0 && p.state) atomicExch(&p.state->error, 3u);
       return;
     }
+  } else if (p.ar_pull) {
+    // tensor parallelism: x = the sum of the ranks' exchanged partials; this
+    // CTA writes its slice of x (src/model.rs:470, :477 summed over ranks)
+    const uint32_t e = *p.ar_base + p.ar_k + 1;
+    const uint32_t s0 = blockIdx.x * n4 / gridDim.x, s1 = (blockIdx.x + 1) * n4 / gridDim.x;
+    bool okp = true;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const uint32_t i4 = ctid + GV_NT * j;
+      buf[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i4 < n4) {
+        okp = ar_pull4(p, e, i4, &buf[j]) && okp;
+        if (i4 >= s0 && i4 < s1) reinterpret_cast<float4*>(p.x_out)[i4] = buf[j];
+      }
+    }
+    if (!okp && p.state) atomicExch(&p.state->error, 7u);
   } else {
     // f32 input (RMS-normalised when norm_w is set) -> records; every x load
     // of this thread in flight at once
@@ -926,6 +1006,8 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
       const uint32_t i4 = ctid + GV_NT * j;
       buf[j] = i4 < n4 ? x4[i4] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+  }
+  if (!p.in_runs) {
     float inv = 1.f;
     if (norm) {
       float ss = 0.f;
@@ -974,7 +1056,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
     }
   }
   if (!ok) {
-    if (lane == 0) atomicExch(&p.state->error, 3u);
+    if (lane == 0 && p.state) atomicExch(&p.state->error, 3u);
     return;
   }
   named_sync(1, GV_NT);
@@ -988,6 +1070,18 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
     for (uint32_t i = ctid; i < nrows; i += GV_NT) {
       uint32_t row = it.r0 + i;
       s.out[row] = s.bias ? __fadd_rn(acc[i], s.bias[row]) : acc[i];
+    }
+  } else if (p.epilogue == EPI_RESID && p.ar_push) {
+    // tensor parallelism: this rank's partial of x + W v (rank 0 adds x) to
+    // every rank's slot (the exchange above)
+    const uint32_t e = *p.ar_base + p.ar_k + 1;
+    const uint64_t slot = ((uint64_t)(e & 1) * p.ar_w + p.ar_rank) * p.ar_h;
+    for (uint32_t i = ctid; i < nrows; i += GV_NT) {
+      const uint32_t row = it.r0 + i;
+      const float v = p.ar_rank == 0 ? __fadd_rn(s.out[row], acc[i]) : acc[i];
+      const uint2 w = make_uint2(__float_as_uint(v), e);
+      for (uint32_t q = 0; q < p.ar_w; q++)
+        st_volatile_u2(reinterpret_cast<uint2*>(p.ar_peers.buf[q]) + slot + row, w);
     }
   } else if (p.epilogue == EPI_RESID) {
     // x += W v (src/model.rs:470, :477)
@@ -1126,6 +1220,23 @@ void launch_gemv(const GemvLaunch& g, cudaStream_t st) {
   p.state = g.state;
   p.out_runs = reinterpret_cast<XRun*>(g.out_runs);
   p.idx_base = g.idx_base;
+  if (g.ar_push || g.ar_pull) {
+    if (!g.ar_base || g.ar_w < 2 || g.ar_w > (uint32_t)AR_MAX_RANKS || g.ar_h % 4 || !g.state)
+      fail(FZ_EINVAL, "gemv: bad tensor-parallel exchange");
+    if (g.ar_pull && (g.in_runs || !g.norm_w || cols != g.ar_h))
+      fail(FZ_EINVAL, "gemv: the exchange feeds an RMS-normalised f32 input only");
+    if (g.ar_push && (g.epilogue != EPI_RESID || g.seg[0].w.rows != g.ar_h))
+      fail(FZ_EINVAL, "gemv: the exchange is fed by a residual epilogue only");
+    p.ar_peers = g.ar_peers;
+    p.ar_w = g.ar_w;
+    p.ar_rank = g.ar_rank;
+    p.ar_k = g.ar_k;
+    p.ar_h = g.ar_h;
+    p.ar_base = g.ar_base;
+    p.ar_push = g.ar_push;
+    p.ar_pull = g.ar_pull;
+    p.x_out = const_cast<float*>(g.x);
+  }
   uint32_t max_rows = 0, slot = 0;
   for (int i = 0; i < g.nseg; i++) {
     const GvSeg& s = p.seg[i];
@@ -1477,9 +1588,11 @@ void launch_attention(const AttnLaunch& a, cudaStream_t s) {
 // Step bookkeeping: the sampled id (first max, src/generate.rs:69-77), the
 // next input token (forced prompt token or the id itself), pos += 1.
 // ---------------------------------------------------------------------------
-__global__ void k_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, int has_logits) {
+__global__ void k_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, int has_logits,
+                           uint32_t* ar_base, uint32_t ar_step) {
   pdl_trigger();
   pdl_wait();
+  if (ar_base) *ar_base += ar_step;
   uint32_t step = st->step;
   if (has_logits) {
     uint32_t id = 0xFFFFFFFFu - (uint32_t)(st->argmax_key & 0xFFFFFFFFull);
@@ -1493,87 +1606,9 @@ __global__ void k_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_
   st->pos = st->pos + 1;
 }
 
-void launch_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, bool has_logits, cudaStream_t s) {
-  launch_pdl(k_finalize, dim3(1), dim3(1), 0, s, st, forced, ids_out, has_logits ? 1 : 0);
-}
-
-// ---------------------------------------------------------------------------
-// Persistent decode step
-// ---------------------------------------------------------------------------
-// Tensor-parallel all-reduce of the residual stream as a one-shot push over
-// peer memory (NVLink): every rank stores its partial x into its slot of
-// every rank's receive buffer, each element as one 8-byte word
-// {value, epoch} (an 8-byte store is seen whole or not at all), then each
-// rank polls its own slots until every word carries this call's epoch and
-// sums the W slots in rank order, so every rank holds the identical sum.  No
-// fence or flag round trip: the data is its own flag.  A rank's buffer
-// (exported by CUDA IPC) is uint2 recv[2][W][H]; the parity of the call picks
-// the half, so a rank one call ahead never overwrites a slot still being read.
-// cnt[b] counts CTA b's calls on this rank; all ranks make the same calls, so
-// the epochs agree.  A word that does not arrive within 2 s sets error 7.
-// ---------------------------------------------------------------------------
-constexpr long long AR_SPIN_NS = 2000000000ll;
-
-__device__ __forceinline__ void st_volatile_u2(uint2* p, uint2 v) {
-  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
-}
-__device__ __forceinline__ uint2 ld_volatile_u2(const uint2* p) {
-  uint2 v;
-  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
-  return v;
-}
-
-__global__ void __launch_bounds__(256) k_ar_push(float* __restrict__ x, uint32_t H, uint32_t W, uint32_t rank,
-                                                 ArPeers peers, uint32_t* __restrict__ cnt, StepState* st) {
-  __shared__ uint32_t s_e, s_ok;
-  const uint32_t b = blockIdx.x, tid = threadIdx.x;
-  if (tid == 0) {
-    pdl_trigger();
-    s_e = cnt[b] + 1;
-    s_ok = 1;
-  }
-  pdl_wait();  // x holds this rank's partial
-  __syncthreads();
-  const uint32_t e = s_e, par = e & 1;
-  const uint32_t per = (H + gridDim.x - 1) / gridDim.x;
-  const uint32_t i0 = min(b * per, H), i1 = min(i0 + per, H);
-  // 1. push {value, epoch} of this CTA's range into every rank's slot `rank`
-  for (uint32_t i = i0 + tid; i < i1; i += blockDim.x) {
-    const uint2 w = make_uint2(__float_as_uint(x[i]), e);
-    for (uint32_t q = 0; q < W; q++)
-      st_volatile_u2(reinterpret_cast<uint2*>(peers.buf[q]) + ((uint64_t)par * W + rank) * H + i, w);
-  }
-  // 2. poll the W slots of this range and sum them in rank order
-  const uint2* recv = reinterpret_cast<const uint2*>(peers.buf[rank]) + (uint64_t)par * W * H;
-  for (uint32_t i = i0 + tid; i < i1; i += blockDim.x) {
-    float acc = 0.f;
-    for (uint32_t q = 0; q < W; q++) {
-      const uint2* wp = recv + (uint64_t)q * H + i;
-      uint2 w = ld_volatile_u2(wp);
-      if (w.y != e) {
-        const uint64_t t0 = gtimer();
-        while ((w = ld_volatile_u2(wp)).y != e) {
-          if (gtimer() - t0 > (uint64_t)AR_SPIN_NS || !*(volatile uint32_t*)&s_ok) {
-            atomicExch(&st->error, 7u);
-            s_ok = 0;
-            break;
-          }
-        }
-      }
-      acc += __uint_as_float(w.x);
-    }
-    x[i] = acc;
-  }
-  __syncthreads();
-  if (tid == 0 && s_ok) cnt[b] = e;
-}
-
-uint64_t ar_buffer_bytes(uint32_t H, uint32_t W) { return 2ull * W * H * 8; }
-
-void launch_ar_push(float* x, uint32_t H, uint32_t W, uint32_t rank, const ArPeers& peers, uint32_t* cnt,
-                    StepState* st, cudaStream_t s) {
-  if (W > AR_MAX_RANKS) fail(FZ_EINVAL, "all-reduce: %u ranks > %d", W, AR_MAX_RANKS);
-  launch_pdl(k_ar_push, dim3(AR_CTAS), dim3(256), 0, s, x, H, W, rank, peers, cnt, st);
+void launch_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, bool has_logits, cudaStream_t s,
+                     uint32_t* ar_base, uint32_t ar_step) {
+  launch_pdl(k_finalize, dim3(1), dim3(1), 0, s, st, forced, ids_out, has_logits ? 1 : 0, ar_base, ar_step);
 }
 
 // ---------------------------------------------------------------------------

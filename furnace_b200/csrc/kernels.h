@@ -60,6 +60,15 @@ uint32_t trace_count();
 uint32_t runs_for(uint32_t cols);
 void launch_to_runs(const float* x, uint32_t cols, void* runs, uint32_t nruns, cudaStream_t s);
 
+// Tensor-parallel exchange of the residual stream through peer memory (see
+// kernels.cu): buf[q] is rank q's receive buffer of ar_buffer_bytes(H, W)
+// bytes as mapped in this process (buf[rank] the local one, zeroed once).
+constexpr int AR_MAX_RANKS = 8;
+struct ArPeers {
+  float* buf[AR_MAX_RANKS];
+};
+uint64_t ar_buffer_bytes(uint32_t H, uint32_t W);
+
 // Up to 3 weight segments sharing one input vector (q|k|v).
 struct GemvSeg {
   DevMat w;
@@ -79,6 +88,14 @@ struct GemvLaunch {
   void* out_runs = nullptr;         // SWIGLU: records of the next GEMV's input
   const GemvLaunch* next = nullptr; // the next GEMV of the step (L2 prefetch)
   uint32_t idx_base = 0;            // EPI_LOGITS: global index of row 0 (vocab slice)
+  // tensor parallelism, exchange k of the step (epoch *ar_base + k + 1):
+  // ar_push: the RESID epilogue sends its rows' partial (plus x on rank 0)
+  // to every rank instead of updating x; ar_pull: the f32 prologue sums the
+  // W partials of every element as its input and writes its slice of x
+  ArPeers ar_peers{};
+  uint32_t ar_w = 0, ar_rank = 0, ar_k = 0, ar_h = 0;
+  const uint32_t* ar_base = nullptr;
+  int ar_push = 0, ar_pull = 0;
 };
 
 void launch_gemv(const GemvLaunch& g, cudaStream_t s);
@@ -106,21 +123,10 @@ void launch_attention(const AttnLaunch& a, cudaStream_t s);
 uint32_t attention_splits(uint32_t n_kv);
 uint64_t attention_partial_floats(uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t splits);
 
-// One-shot push all-reduce (sum) of x[H] over W tensor-parallel ranks through
-// peer memory; buf[q] is rank q's receive buffer of ar_buffer_bytes(H, W)
-// bytes as mapped in this process (buf[rank] the local one, zeroed once);
-// cnt holds AR_CTAS zeroed call counters of this rank.
-constexpr int AR_MAX_RANKS = 8;
-constexpr int AR_CTAS = 8;
-struct ArPeers {
-  float* buf[AR_MAX_RANKS];
-};
-uint64_t ar_buffer_bytes(uint32_t H, uint32_t W);
-void launch_ar_push(float* x, uint32_t H, uint32_t W, uint32_t rank, const ArPeers& peers, uint32_t* cnt,
-                    StepState* st, cudaStream_t s);
-
-// Step bookkeeping after the logits (argmax -> ids_out, next token, pos++).
-void launch_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, bool has_logits, cudaStream_t s);
+// Step bookkeeping after the logits (argmax -> ids_out, next token, pos++;
+// ar_base, when set, advances by ar_step: the step's exchanges).
+void launch_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, bool has_logits, cudaStream_t s,
+                     uint32_t* ar_base = nullptr, uint32_t ar_step = 0);
 
 int num_sms();
 void kernels_init();

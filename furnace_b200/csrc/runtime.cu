@@ -88,9 +88,9 @@ struct fz_model {
   // tensor parallelism: this rank's share (world == 1: everything)
   int rank = 0, world = 1;
   ncclComm_t comm = nullptr;
-  // one-shot push all-reduce: this rank's receive buffer (exported by CUDA
-  // IPC), the peers' buffers as mapped here, per-CTA call counters
-  DevBuf ar_buf, ar_cnt;
+  // residual exchange through peer memory: this rank's receive buffer
+  // (exported by CUDA IPC), the peers' buffers as mapped here, the epoch base
+  DevBuf ar_buf, ar_base;
   ArPeers ar_peers{};
   bool ar_p2p = false;
   fz_tp_slice sl{};
@@ -281,10 +281,23 @@ std::vector<GemvLaunch> step_gemvs(fz_kv* kv) {
   const uint32_t qd = m->qd_l, kd = m->kd_l;  // this rank's q / k widths
   // tensor parallelism: o_proj and down partial sums of ranks > 0 overwrite
   // x, rank 0 adds its partial to x, and the all-reduce that follows sums them
-  const int resid = m->rank == 0 ? EPI_RESID : EPI_STORE;
+  const bool xch = m->world > 1 && m->ar_p2p;  // exchange through peer memory
+  const int resid = m->rank == 0 || xch ? EPI_RESID : EPI_STORE;
   float* x = m->x.as<float>();
   float* qkv = m->qkv.as<float>();
   std::vector<GemvLaunch> gl(4 * c.n_layers + 1);
+  // exchange k of the step: pushed by o_proj (2 li) and down (2 li + 1),
+  // pulled by the next RMS-normalised GEMV
+  auto ar = [&](GemvLaunch& g, uint32_t k, bool push) {
+    if (!xch) return;
+    g.ar_peers = m->ar_peers;
+    g.ar_w = m->world;
+    g.ar_rank = m->rank;
+    g.ar_k = k;
+    g.ar_h = c.hidden;
+    g.ar_base = m->ar_base.as<uint32_t>();
+    (push ? g.ar_push : g.ar_pull) = 1;
+  };
   for (uint32_t li = 0; li < c.n_layers; li++) {
     Layer& L = m->layers[li];
     GemvLaunch& g = gl[4 * li];
@@ -311,6 +324,11 @@ std::vector<GemvLaunch> step_gemvs(fz_kv* kv) {
     gd.seg[0] = GemvSeg{L.wd, nullptr, x};
     gd.in_runs = m->runs_h.p;
     gd.epilogue = resid;
+    if (li > 0) ar(g, 2 * li - 1, false);
+    ar(go, 2 * li, true);
+    ar(gu, 2 * li, false);
+    ar(gd, 2 * li + 1, true);
+    for (GemvLaunch* p : {&g, &go, &gu, &gd}) p->state = st;
   }
   GemvLaunch& lm = gl[4 * c.n_layers];
   lm.seg[0] = GemvSeg{m->lm_head, nullptr, m->logits.as<float>() + m->sl.vocab0};
@@ -320,6 +338,7 @@ std::vector<GemvLaunch> step_gemvs(fz_kv* kv) {
   lm.eps = c.rms_eps;
   lm.epilogue = EPI_LOGITS;
   lm.state = st;
+  ar(lm, 2 * c.n_layers - 1, false);
   return gl;
 }
 
@@ -337,15 +356,11 @@ AttnLaunch layer_attention(fz_kv* kv, uint32_t li, uint32_t splits) {
 }
 
 // Sum of the ranks' residual-stream partials (tensor parallelism).
-// Sum of the ranks' residual-stream partials (tensor parallelism): the
-// one-shot push over peer memory, or NCCL where peer mappings are unavailable
-// or FURNACE_B200_TP_ALLREDUCE=nccl asks for it.
-void tp_allreduce_x(fz_model* m, StepState* st, cudaStream_t s) {
-  if (m->world == 1) return;
-  if (m->ar_p2p) {
-    launch_ar_push(m->x.as<float>(), m->cfg.hidden, m->world, m->rank, m->ar_peers, m->ar_cnt.as<uint32_t>(), st, s);
-    return;
-  }
+// Sum of the ranks' residual-stream partials (tensor parallelism) where the
+// peer-memory exchange inside the GEMVs is unavailable (a rank could not
+// export its buffer, or FURNACE_B200_TP_ALLREDUCE=nccl): ncclAllReduce.
+void tp_allreduce_x(fz_model* m, cudaStream_t s) {
+  if (m->world == 1 || m->ar_p2p) return;
   nccl_check(nccl().AllReduce(m->x.p, m->x.p, m->cfg.hidden, ncclFloat32, ncclSum, m->comm, s), "ncclAllReduce");
 }
 
@@ -377,14 +392,14 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
     H(FZ_OP_ATTN, false);
     H(FZ_OP_OPROJ, true);
     launch_gemv(gl[4 * li + 1], s);
-    tp_allreduce_x(m, st, s);
+    tp_allreduce_x(m, s);
     H(FZ_OP_OPROJ, false);
     H(FZ_OP_GATEUP, true);
     launch_gemv(gl[4 * li + 2], s);
     H(FZ_OP_GATEUP, false);
     H(FZ_OP_DOWN, true);
     launch_gemv(gl[4 * li + 3], s);
-    tp_allreduce_x(m, st, s);
+    tp_allreduce_x(m, s);
     H(FZ_OP_DOWN, false);
   }
   if (with_logits) {
@@ -398,7 +413,9 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
     H(FZ_OP_LMHEAD, false);
   }
   H(FZ_OP_FINALIZE, true);
-  launch_finalize(st, kv->forced.as<uint32_t>(), kv->ids.as<uint32_t>(), with_logits, s);
+  const bool xch = m->world > 1 && m->ar_p2p;
+  launch_finalize(st, kv->forced.as<uint32_t>(), kv->ids.as<uint32_t>(), with_logits, s,
+                  xch ? m->ar_base.as<uint32_t>() : nullptr, xch ? 2 * c.n_layers : 0);
   H(FZ_OP_FINALIZE, false);
 }
 
@@ -644,8 +661,8 @@ void check_state(fz_kv* kv) {
   StepState st;
   CK(cudaMemcpyAsync(&st, kv->state.p, sizeof st, cudaMemcpyDeviceToHost, kv->m->stream));
   CK(cudaStreamSynchronize(kv->m->stream));
-  // codes 1-2: token >= vocab, position >= max_ctx; 3-5: a bounded device
-  // wait (input records, ring slot, KV tile) ran out
+  // codes 1-2: token >= vocab, position >= max_ctx; 3-5 and 7: a bounded
+  // device wait (input records, ring slot, KV tile; residual exchange) ran out
   if (st.error >= 3) fail(FZ_ETIMEOUT, "a bounded device wait ran out (code %u)", st.error);
   if (st.error) fail(FZ_EINVAL, "device step rejected its input (code %u)", st.error);
 }
@@ -759,7 +776,7 @@ namespace {
 
 // Model::load (src/model.rs:520-552) for rank `rank` of `world`: the rank's
 // slice of every matrix, uploaded raw and repacked into the device layout.
-// Receive buffers of the one-shot all-reduce: every rank exports its buffer
+// Receive buffers of the residual exchange: every rank exports its buffer
 // by CUDA IPC, the handles travel by NCCL all-gather, and each rank maps the
 // others'.  Collective: every rank calls it once while loading.
 void tp_p2p_setup(fz_model* m) {
@@ -767,10 +784,11 @@ void tp_p2p_setup(fz_model* m) {
   const bool want = !(e && strcmp(e, "nccl") == 0);
   const uint32_t W = (uint32_t)m->world;
   need(W <= (uint32_t)AR_MAX_RANKS, "tensor parallelism over %u ranks > %d", W, AR_MAX_RANKS);
+  need(m->cfg.hidden % 4 == 0, "hidden %u not a multiple of 4", m->cfg.hidden);
   m->ar_buf.alloc(ar_buffer_bytes(m->cfg.hidden, W));
   CK(cudaMemset(m->ar_buf.p, 0, m->ar_buf.n));
-  m->ar_cnt.alloc(AR_CTAS * 4);
-  CK(cudaMemset(m->ar_cnt.p, 0, m->ar_cnt.n));
+  m->ar_base.alloc(16);
+  CK(cudaMemset(m->ar_base.p, 0, m->ar_base.n));
   // every rank takes part in the exchange (the same collective steps on all
   // ranks); a rank that cannot export marks its handle invalid
   static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
