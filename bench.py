@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--prefill", type=int, default=PREFILL)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel group size (divides --gpus)")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="layer-truncated variant of the config (same per-layer shapes; for large configs)")
     return ap.parse_args()
 
 
@@ -243,8 +245,8 @@ def run_reference(args, dist):
 
     if dist.rank != 0:
         return
-    path = synth.ensure(args.config)
-    spec = synth.spec(args.config)
+    path = synth.ensure(args.config, args.layers)
+    spec = synth.spec(args.config, args.layers)
     cores = os.cpu_count() or 1
     oracle.set_threads(cores)
     m = oracle.Model(path)
@@ -276,11 +278,11 @@ def run_ours(args, dist):
     import furnace_b200 as fz
     from furnace_b200 import synth
 
-    spec = synth.spec(args.config)
+    spec = synth.spec(args.config, args.layers)
     if dist.rank == 0:
-        path = synth.ensure(args.config)
+        path = synth.ensure(args.config, args.layers)
     dist.barrier()
-    path = synth.ensure(args.config)
+    path = synth.ensure(args.config, args.layers)
     dev = dist.local
     cud = Cudart()
     cud.set_device(dev)
