@@ -292,11 +292,13 @@ def run_ours(args, dist):
     if dist.world % tp or spec.n_heads % tp or spec.n_kv_heads % tp:
         raise SystemExit(f"--tp {tp} must divide --gpus {dist.world} and the head counts")
     groups = dist.world // tp
+    t_load = time.perf_counter()
     if tp > 1:
         ids = dist.bcast([fz.tp_unique_id() for _ in range(groups)] if dist.rank == 0 else None)
         model = fz.Model.load_tp(f, dist.rank % tp, tp, ids[dist.rank // tp], dev)
     else:
         model = fz.Model.load(f, devices=[dev])
+    load_s = time.perf_counter() - t_load
     cfg = model.config
     resident, per_tok = model.param_bytes()
     stream, _ = model.stream()
@@ -374,6 +376,9 @@ def run_ours(args, dist):
                    "kv": "f32"},
         "hbm_gbs_per_gpu": hbm, "hbm_frac_of_8tbs": hbm / 8000.0, "hbm_frac_of_measured": hbm / peak,
         "bytes_per_token": per_tok, "ms_per_token": ms / total_tokens, "prefill_s": prefill_s,
+        "load": {"s": load_s, "gb": resident / 1e9,
+                 "note": "host wall clock of fz_model_load(_tp): GGUF bytes of this rank's share from the "
+                         "page cache to the device and the repack into the chunk layout"},
         "prefill": {"tokens": args.prefill, "s": prefill_s, "tok_s": args.prefill / prefill_s,
                     "path": "tcgen05 GEMM (fp16 hi/lo split, f32 accumulation) for all but the last prompt token"
                     if tp == 1 and args.prefill > 8 else "decode step per token",

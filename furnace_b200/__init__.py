@@ -39,7 +39,7 @@ EXPORTS = [
     "fz_last_error", "fz_version", "fz_open", "fz_open_bytes", "fz_file_free", "fz_file_info", "fz_tensor_at",
     "fz_tensor", "fz_meta_u32", "fz_meta_f32", "fz_meta_str", "fz_meta_array_len", "fz_config_from_gguf",
     "fz_model_load", "fz_model_free", "fz_model_config", "fz_model_bytes", "fz_kv_new", "fz_kv_free", "fz_kv_len",
-    "fz_kv_set_len", "fz_kv_read", "fz_forward", "fz_decode_greedy", "fz_dequant", "fz_matmul_quant",
+    "fz_kv_set_len", "fz_kv_read", "fz_forward", "fz_forward_last", "fz_decode_greedy", "fz_dequant", "fz_matmul_quant",
     "fz_weight_upload", "fz_weight_free", "fz_matmul_quant_dev", "fz_step_profile", "fz_model_stream",
     "fz_dequant_dev_noalloc", "fz_tp_slice_of", "fz_tp_unique_id", "fz_model_load_tp",
     "fz_sampler_new", "fz_sampler_free", "fz_sampler_draws", "fz_sample_logits", "fz_sample", "fz_generate",
@@ -115,6 +115,7 @@ def load_library(build_if_missing: bool = True):
         "fz_kv_set_len": (I, [P, U32]),
         "fz_kv_read": (I, [P, U32, I, U32, fp]),
         "fz_forward": (I, [P, P, u32p, U32, fp, u32p]),
+        "fz_forward_last": (I, [P, u32p, U32, fp, u32p]),
         "fz_decode_greedy": (I, [P, P, U32, U32, u32p, U32, u32p, fp, u32p]),
         "fz_dequant": (I, [U32, P, S, S, fp]),
         "fz_matmul_quant": (I, [fp, U32, P, S, U32, U32, U32, fp]),
@@ -336,6 +337,16 @@ class Model:
         out = np.zeros(self.config.vocab, np.float32) if want_logits else None
         _check(load_library().fz_forward(self._h, cache._h, _u32p(t), t.size, _fp(out) if want_logits else None,
                                          C.byref(am)))
+        return out, am.value
+
+    def forward_last(self, tokens, want_logits: bool = True):
+        """Model::forward_last (src/model.rs:569-575), the uncached forward over
+        positions 0..n-1: (logits or None, argmax id)."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32).reshape(-1)
+        am = C.c_uint32()
+        out = np.zeros(self.config.vocab, np.float32) if want_logits else None
+        _check(load_library().fz_forward_last(self._h, _u32p(t), t.size, _fp(out) if want_logits else None,
+                                              C.byref(am)))
         return out, am.value
 
     def stream(self):

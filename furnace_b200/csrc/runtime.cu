@@ -1224,6 +1224,20 @@ int fz_forward(fz_model* m, fz_kv* kv, const uint32_t* tokens, uint32_t n, float
   });
 }
 
+int fz_forward_last(fz_model* m, const uint32_t* tokens, uint32_t n, float* logits, uint32_t* argmax) {
+  return guard([&] {
+    need(m && tokens && n > 0, "forward_last with no tokens");
+    // the uncached forward over positions 0..n-1 is the cached one from an
+    // empty cache: a scratch cache of n positions, freed on every path
+    fz_kv* kv = nullptr;
+    int rc = fz_kv_new(m, n, 0, &kv);
+    if (rc != FZ_OK) fail(rc, "%s", fz_last_error());
+    std::unique_ptr<fz_kv, void (*)(fz_kv*)> hold(kv, fz_kv_free);
+    rc = fz_forward(m, kv, tokens, n, logits, argmax);
+    if (rc != FZ_OK) fail(rc, "%s", fz_last_error());
+  });
+}
+
 int fz_decode_greedy(fz_model* m, fz_kv* kv, uint32_t first, uint32_t n_steps, const uint32_t* stop_ids,
                      uint32_t n_stop, uint32_t* ids_out, float* logits_out, uint32_t* n_out) {
   return guard([&] {

@@ -159,6 +159,13 @@ int fz_kv_read(const fz_kv* kv, uint32_t layer, int which_v, uint32_t n, float* 
  * src/generate.rs:69-77; argmax may be NULL). */
 int fz_forward(fz_model* m, fz_kv* kv, const uint32_t* tokens, uint32_t n, float* logits, uint32_t* argmax);
 
+/* Model::forward_last (src/model.rs:569-575): the uncached forward over
+ * positions 0 .. n-1 (the reference's --no-cache mode), returning the last
+ * position's logits [vocab] (may be NULL) and their argmax (may be NULL).  It
+ * runs forward_cached on a scratch cache of n positions, the same arithmetic
+ * as the reference's full recompute up to summation order. */
+int fz_forward_last(fz_model* m, const uint32_t* tokens, uint32_t n, float* logits, uint32_t* argmax);
+
 /* Greedy decode loop of generate (src/generate.rs:122-141) at temperature 0
  * (Sampler::sample's argmax short-circuit, src/sampler.rs:92-94): starting
  * from `first` (the token sampled from the previous logits), runs up to

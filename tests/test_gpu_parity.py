@@ -188,6 +188,21 @@ def test_forward_and_kv_cache_match_oracle(tiny):
     _check_logits(got, want, "decode")
 
 
+def test_forward_last_matches_oracle_uncached(tiny):
+    """Model::forward_last, the reference's --no-cache path, against the
+    oracle's full recompute (src/model.rs:569-575, :294-315): short prompts
+    replay the decode step, longer ones use the batched prefill."""
+    f, dev, ref = _models(tiny)
+    for n, seed in ((5, 11), (40, 12)):
+        ids = synth.prompt_ids(ref.vocab, n, seed=seed)
+        got, am = dev.forward_last(ids)
+        want = ref.forward_last(ids)
+        _check_logits(got, want, f"forward_last n={n}")
+        assert am == int(np.argmax(want))
+    with pytest.raises(fz.FurnaceError):
+        dev.forward_last([dev.config.vocab])
+
+
 def test_forward_rejects_bad_input(tiny):
     f, dev, _ = _models(tiny)
     kv = fz.KvCache(dev, 8)
