@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--prefill", type=int, default=PREFILL)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel group size (divides --gpus)")
+    ap.add_argument("--kv", default="f32", choices=["f32", "f16"],
+                    help="KV cache elements (f32: the reference's; f16: the 32B config's 8K-context cache)")
     ap.add_argument("--layers", type=int, default=None,
                     help="layer-truncated variant of the config (same per-layer shapes; for large configs)")
     return ap.parse_args()
@@ -305,7 +307,7 @@ def run_ours(args, dist):
     T = STEP_TOKENS
     total_tokens = args.steps * T
     max_ctx = args.prefill + max(args.warmup * T, 2 * T) + total_tokens + 8
-    kv = fz.KvCache(model, max_ctx)
+    kv = fz.KvCache(model, max_ctx, fz.FZ_KV_F16 if args.kv == "f16" else fz.FZ_KV_F32)
     prompt = synth.prompt_ids(cfg.vocab, args.prefill, seed=dist.rank // tp)  # one prompt per TP group
     t0 = time.perf_counter()
     _, first = model.forward(prompt, kv, want_logits=False)
@@ -373,7 +375,7 @@ def run_ours(args, dist):
                    "seq_len": args.prefill + total_tokens,
                    "parallelism": f"tp{tp}" + (f"x{groups}" if groups > 1 else ""),
                    "l2": "inputs larger than L2: %.2f GB of weights streamed per token" % (per_tok / 1e9),
-                   "kv": "f32"},
+                   "kv": args.kv},
         "hbm_gbs_per_gpu": hbm, "hbm_frac_of_8tbs": hbm / 8000.0, "hbm_frac_of_measured": hbm / peak,
         "bytes_per_token": per_tok, "ms_per_token": ms / total_tokens, "prefill_s": prefill_s,
         "load": {"s": load_s, "gb": resident / 1e9,

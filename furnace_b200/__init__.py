@@ -33,6 +33,7 @@ BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q5_0: (32, 22), Q4_K: (256, 1
 TYPE_NAMES = {F32: "F32", F16: "F16", Q5_0: "Q5_0", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
 
 FZ_OK, FZ_EINVAL, FZ_EFORMAT, FZ_EIO, FZ_ECUDA, FZ_ENOMEM, FZ_ETIMEOUT = range(7)
+FZ_KV_F32, FZ_KV_F16 = 0, 1  # KV cache element types
 
 # Every symbol include/furnace.h declares.
 EXPORTS = [
@@ -379,11 +380,14 @@ class Model:
 class KvCache:
     """KvCache (src/model.rs:321-363), resident in HBM."""
 
-    def __init__(self, model: Model, max_ctx: int):
+    def __init__(self, model: Model, max_ctx: int, kv_dtype: int = 0):
+        """kv_dtype FZ_KV_F32 (the reference's f32 cache) or FZ_KV_F16
+        (binary16 elements, rounded to nearest even when appended)."""
         self.model = model
         self.max_ctx = max_ctx
+        self.kv_dtype = kv_dtype
         h = C.c_void_p()
-        _check(load_library().fz_kv_new(model._h, max_ctx, 0, C.byref(h)))
+        _check(load_library().fz_kv_new(model._h, max_ctx, kv_dtype, C.byref(h)))
         self._h = h
 
     def close(self):
@@ -493,7 +497,8 @@ def generate_sampled(model: Model, prompt_ids, max_new: int, sampler: Sampler, s
     return out[: n.value]
 
 
-def generate(model: Model, prompt_ids, max_new: int, stop_ids=(), max_ctx: int | None = None, keep_logits=False):
+def generate(model: Model, prompt_ids, max_new: int, stop_ids=(), max_ctx: int | None = None, keep_logits=False,
+             kv_dtype: int = 0):
     """generate (src/generate.rs:83-157) with the greedy sampler
     (temperature 0): prefill once, then decode on the device.  Returns
     (ids, per-step logits or None)."""
@@ -501,7 +506,7 @@ def generate(model: Model, prompt_ids, max_new: int, stop_ids=(), max_ctx: int |
     max_ctx = max_ctx or min(model.config.context_length, 4096)
     if p.size + max_new > max_ctx:
         raise FurnaceError(FZ_EINVAL, f"prompt ({p.size}) + max tokens ({max_new}) exceeds context cap {max_ctx}")
-    cache = KvCache(model, max_ctx)
+    cache = KvCache(model, max_ctx, kv_dtype)
     logits, first = model.forward(p, cache, want_logits=keep_logits)
     ids, lg = model.decode_greedy(first, max_new, cache, stop_ids, keep_logits)
     if keep_logits:

@@ -1303,11 +1303,31 @@ constexpr int AT_MAXG = 8;
 constexpr int AT_TP = 32;    // positions per tile
 constexpr int AT_NBUF = 3;   // tiles in flight
 
-template <int HD>
+// KV cache elements: f32 (the reference's KvCache) or f16 (FZ_KV_F16: values
+// rounded to nearest even when appended, read back exactly).
+__device__ __forceinline__ float4 kv_ld4(const float* row, uint32_t c) { return reinterpret_cast<const float4*>(row)[c]; }
+__device__ __forceinline__ float4 kv_ld4(const __half* row, uint32_t c) {
+  const uint2 u = reinterpret_cast<const uint2*>(row)[c];
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ float kv_ld(const float* p) { return *p; }
+__device__ __forceinline__ float kv_ld(const __half* p) { return __half2float(*p); }
+// The value as stored: f32 unchanged, f16 rounded to nearest even.
+template <typename KT>
+__device__ __forceinline__ float kv_round(float v) {
+  return sizeof(KT) == 4 ? v : __half2float(__float2half_rn(v));
+}
+__device__ __forceinline__ void kv_st(float* p, float v) { *p = v; }
+__device__ __forceinline__ void kv_st(__half* p, float v) { *p = __float2half_rn(v); }
+
+template <int HD, typename KT>
 __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ qkv, const float2* __restrict__ cs,
-                                                      float* __restrict__ kc, float* __restrict__ vc,
+                                                      KT* __restrict__ kc, KT* __restrict__ vc,
                                                       float* __restrict__ partials, uint32_t nh, uint32_t nkv,
                                                       uint32_t max_ctx, StepState* st) {
+  constexpr uint32_t EB = sizeof(KT);
   constexpr int DPL = HD / 32;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(16) float qs[AT_MAXG][HD];
@@ -1315,9 +1335,9 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
   const uint32_t G = nh / nkv, kvh = blockIdx.y, split = blockIdx.x, S = gridDim.x;
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t half = HD / 2;
-  float* tiles = reinterpret_cast<float*>(smem);  // [NBUF][K|V][TP][HD]
-  const float* kvk = kc + (uint64_t)kvh * max_ctx * HD;
-  const float* kvv = vc + (uint64_t)kvh * max_ctx * HD;
+  KT* tiles = reinterpret_cast<KT*>(smem);  // [NBUF][K|V][TP][HD]
+  const KT* kvk = kc + (uint64_t)kvh * max_ctx * HD;
+  const KT* kvv = vc + (uint64_t)kvh * max_ctx * HD;
   Tracer tr;
   if (tid == 0) {
     tr.begin(TR_ATTN, gridDim.x * gridDim.y);
@@ -1327,8 +1347,8 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
     uint32_t p0 = min(*((volatile uint32_t*)&st->pos), max_ctx - 1);
     uint32_t per0 = (p0 + S) / S, a0 = min(split * per0, p0), a1 = min(p0, a0 + per0);
     if (a1 > a0) {
-      bulk_prefetch(kvk + (uint64_t)a0 * HD, (a1 - a0) * HD * 4);
-      bulk_prefetch(kvv + (uint64_t)a0 * HD, (a1 - a0) * HD * 4);
+      bulk_prefetch(kvk + (uint64_t)a0 * HD, (a1 - a0) * HD * EB);
+      bulk_prefetch(kvv + (uint64_t)a0 * HD, (a1 - a0) * HD * EB);
     }
     for (int b = 0; b < AT_NBUF; b++) mbar_init(&bar[b], 1);
     fence_barrier_init();
@@ -1348,11 +1368,11 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
   auto issue = [&](uint32_t j) {
     uint32_t b = j % AT_NBUF, a = t0 + j * AT_TP, e = min(min(t1, a + AT_TP), pos);
     uint32_t rows = e > a ? e - a : 0;
-    float* kt = tiles + (size_t)b * 2 * AT_TP * HD;
-    mbar_expect_tx(&bar[b], 2 * rows * HD * 4);
+    KT* kt = tiles + (size_t)b * 2 * AT_TP * HD;
+    mbar_expect_tx(&bar[b], 2 * rows * HD * EB);
     if (rows) {
-      bulk_g2s(kt, kvk + (uint64_t)a * HD, rows * HD * 4, &bar[b], pol);
-      bulk_g2s(kt + AT_TP * HD, kvv + (uint64_t)a * HD, rows * HD * 4, &bar[b], pol);
+      bulk_g2s(kt, kvk + (uint64_t)a * HD, rows * HD * EB, &bar[b], pol);
+      bulk_g2s(kt + AT_TP * HD, kvv + (uint64_t)a * HD, rows * HD * EB, &bar[b], pol);
     }
   };
   __syncthreads();  // barrier init visible
@@ -1376,16 +1396,17 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
     const float* vx = qkv + (uint64_t)(nh + nkv + kvh) * HD;
     float a = kx[tid], b = kx[tid + half];
     float2 c = csp[tid];
-    kn[0] = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
-    kn[1] = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
-    vn[0] = vx[tid];
-    vn[1] = vx[tid + half];
-    float* kdst = kc + ((uint64_t)kvh * max_ctx + pos) * HD;
-    float* vdst = vc + ((uint64_t)kvh * max_ctx + pos) * HD;
-    kdst[tid] = kn[0];
-    kdst[tid + half] = kn[1];
-    vdst[tid] = vn[0];
-    vdst[tid + half] = vn[1];
+    // the values as cached (f16: rounded), used for this position too
+    kn[0] = kv_round<KT>(__fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y)));
+    kn[1] = kv_round<KT>(__fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x)));
+    vn[0] = kv_round<KT>(vx[tid]);
+    vn[1] = kv_round<KT>(vx[tid + half]);
+    KT* kdst = kc + ((uint64_t)kvh * max_ctx + pos) * HD;
+    KT* vdst = vc + ((uint64_t)kvh * max_ctx + pos) * HD;
+    kv_st(kdst + tid, kn[0]);
+    kv_st(kdst + tid + half, kn[1]);
+    kv_st(vdst + tid, vn[0]);
+    kv_st(vdst + tid + half, vn[1]);
   }
   __syncthreads();
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
@@ -1394,18 +1415,18 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
   for (int d = 0; d < DPL; d++) acc[d] = 0.f;
   for (uint32_t j = 0; j < ntiles; j++) {
     const uint32_t b = j % AT_NBUF, a = t0 + j * AT_TP, tn = min(t1, a + AT_TP) - a;
-    float* kt = tiles + (size_t)b * 2 * AT_TP * HD;
-    float* vt = kt + AT_TP * HD;
+    KT* kt = tiles + (size_t)b * 2 * AT_TP * HD;
+    KT* vt = kt + AT_TP * HD;
     if (!mbar_wait(&bar[b], (j / AT_NBUF) & 1)) {
       if (tid == 0) st->error = 5;
       return;
     }
     if (owns_pos && pos >= a && pos < a + AT_TP) {  // block-uniform
       if (tid < half) {
-        kt[(pos - a) * HD + tid] = kn[0];
-        kt[(pos - a) * HD + tid + half] = kn[1];
-        vt[(pos - a) * HD + tid] = vn[0];
-        vt[(pos - a) * HD + tid + half] = vn[1];
+        kv_st(kt + (pos - a) * HD + tid, kn[0]);
+        kv_st(kt + (pos - a) * HD + tid + half, kn[1]);
+        kv_st(vt + (pos - a) * HD + tid, vn[0]);
+        kv_st(vt + (pos - a) * HD + tid + half, vn[1]);
       }
       __syncthreads();
     }
@@ -1413,13 +1434,13 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
       const uint32_t t = lane;
       float s = -INFINITY;
       if (t < tn) {
-        const float4* kr = reinterpret_cast<const float4*>(kt + (size_t)t * HD);
+        const KT* kr = kt + (size_t)t * HD;
         const float4* qr = reinterpret_cast<const float4*>(qs[warp]);
         float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;  // four independent chains
 #pragma unroll 8
         for (uint32_t c = 0; c < HD / 4; c++) {
           uint32_t cc = (c + t) & (HD / 4 - 1);
-          float4 k4 = kr[cc], q4 = qr[cc];
+          float4 k4 = kv_ld4(kr, cc), q4 = qr[cc];
           d0 = fmaf(q4.x, k4.x, d0);
           d1 = fmaf(q4.y, k4.y, d1);
           d2 = fmaf(q4.z, k4.z, d2);
@@ -1443,16 +1464,16 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
 #pragma unroll 8
       for (uint32_t t2 = 0; t2 < tn; t2++) {
         const float pt = __shfl_sync(0xffffffffu, pr, t2);
-        const float* vr = vt + (size_t)t2 * HD + lane * DPL;
-        if (DPL == 4) {  // one 16-byte load per lane: consecutive lanes, no bank conflict
-          const float4 v4 = *reinterpret_cast<const float4*>(vr);
+        const KT* vr = vt + (size_t)t2 * HD + lane * DPL;
+        if (DPL == 4) {  // one load per lane: consecutive lanes, no bank conflict
+          const float4 v4 = kv_ld4(vt + (size_t)t2 * HD, lane);
           acc[0] = fmaf(pt, v4.x, acc[0]);
           acc[1] = fmaf(pt, v4.y, acc[1]);
           acc[2] = fmaf(pt, v4.z, acc[2]);
           acc[3] = fmaf(pt, v4.w, acc[3]);
         } else {
 #pragma unroll
-          for (int d = 0; d < DPL; d++) acc[d] = fmaf(pt, vr[d], acc[d]);
+          for (int d = 0; d < DPL; d++) acc[d] = fmaf(pt, kv_ld(vr + d), acc[d]);
         }
       }
     }
@@ -1558,11 +1579,14 @@ uint64_t attention_partial_floats(uint32_t nh, uint32_t nkv, uint32_t hd, uint32
   return ((2ull * nkv * G * splits + 3) & ~3ull) + (uint64_t)nkv * G * hd * Spad;
 }
 
-static size_t attention_smem(uint32_t hd) { return (size_t)AT_NBUF * 2 * AT_TP * hd * 4; }
+static size_t attention_smem(uint32_t hd, uint32_t eb = 4) { return (size_t)AT_NBUF * 2 * AT_TP * hd * eb; }
 
 void attention_init() {
-  CK(cudaFuncSetAttribute(k_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attention_smem(128)));
-  CK(cudaFuncSetAttribute(k_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attention_smem(64)));
+  CK(cudaFuncSetAttribute(k_attn<128, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attention_smem(128)));
+  CK(cudaFuncSetAttribute(k_attn<64, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attention_smem(64)));
+  CK(cudaFuncSetAttribute(k_attn<128, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          (int)attention_smem(128, 2)));
+  CK(cudaFuncSetAttribute(k_attn<64, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attention_smem(64, 2)));
 }
 
 void launch_attention(const AttnLaunch& a, cudaStream_t s) {
@@ -1572,11 +1596,19 @@ void launch_attention(const AttnLaunch& a, cudaStream_t s) {
   if (splits > AT_MAXS) fail(FZ_EINVAL, "attention: %u splits > %d", splits, AT_MAXS);
   dim3 grid(splits, a.n_kv);
   const float2* cs = reinterpret_cast<const float2*>(a.rope_cs);
-  if (a.hd == 128)
-    launch_pdl(k_attn<128>, grid, dim3(AT_THREADS), attention_smem(128), s, a.qkv, cs, a.kcache, a.vcache,
+  float *kf = static_cast<float*>(a.kcache), *vf = static_cast<float*>(a.vcache);
+  __half *kh = static_cast<__half*>(a.kcache), *vh = static_cast<__half*>(a.vcache);
+  if (a.hd == 128 && !a.kv_f16)
+    launch_pdl(k_attn<128, float>, grid, dim3(AT_THREADS), attention_smem(128), s, a.qkv, cs, kf, vf, a.partials,
+               a.n_heads, a.n_kv, a.max_ctx, a.state);
+  else if (a.hd == 64 && !a.kv_f16)
+    launch_pdl(k_attn<64, float>, grid, dim3(AT_THREADS), attention_smem(64), s, a.qkv, cs, kf, vf, a.partials,
+               a.n_heads, a.n_kv, a.max_ctx, a.state);
+  else if (a.hd == 128)
+    launch_pdl(k_attn<128, __half>, grid, dim3(AT_THREADS), attention_smem(128, 2), s, a.qkv, cs, kh, vh,
                a.partials, a.n_heads, a.n_kv, a.max_ctx, a.state);
   else if (a.hd == 64)
-    launch_pdl(k_attn<64>, grid, dim3(AT_THREADS), attention_smem(64), s, a.qkv, cs, a.kcache, a.vcache, a.partials,
+    launch_pdl(k_attn<64, __half>, grid, dim3(AT_THREADS), attention_smem(64, 2), s, a.qkv, cs, kh, vh, a.partials,
                a.n_heads, a.n_kv, a.max_ctx, a.state);
   else
     fail(FZ_EINVAL, "head_dim %u unsupported (64 or 128)", a.hd);
@@ -1618,8 +1650,13 @@ void launch_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, b
 
 void prefill_init() {
   CK(cudaFuncSetAttribute(k_qgemm, cudaFuncAttributeMaxDynamicSharedMemorySize, QG_SMEM));
-  CK(cudaFuncSetAttribute(k_attn_prefill<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, attention_smem(128)));
-  CK(cudaFuncSetAttribute(k_attn_prefill<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, attention_smem(64)));
+  CK(cudaFuncSetAttribute(k_attn_prefill<128, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          attention_smem(128)));
+  CK(cudaFuncSetAttribute(k_attn_prefill<64, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, attention_smem(64)));
+  CK(cudaFuncSetAttribute(k_attn_prefill<128, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          attention_smem(128, 2)));
+  CK(cudaFuncSetAttribute(k_attn_prefill<64, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          attention_smem(64, 2)));
 }
 
 uint64_t wpanel_elems(uint32_t rows, uint32_t K) { return (uint64_t)((rows + QG_M - 1) / QG_M) * QG_M * K; }
@@ -1666,19 +1703,32 @@ void launch_embed_rows(const DevMat& emb, const uint32_t* tokens, uint32_t T, fl
   CK(cudaGetLastError());
 }
 
-void launch_prefill_attention(const float* qkv, uint32_t ldq, const float* rope_cs, float* kc, float* vc, float* ctx,
-                              uint32_t ldc, uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t max_ctx, uint32_t pos0,
-                              uint32_t T, uint32_t* err, cudaStream_t s) {
-  const float2* cs = reinterpret_cast<const float2*>(rope_cs);
-  k_kv_append<<<dim3(T, nkv), 64, 0, s>>>(qkv, ldq, nh, nkv, hd, cs, kc, vc, max_ctx, pos0);
+template <typename KT>
+static void prefill_attention_t(const float* qkv, uint32_t ldq, const float2* cs, KT* kc, KT* vc, float* ctx,
+                                uint32_t ldc, uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t max_ctx, uint32_t pos0,
+                                uint32_t T, uint32_t* err, cudaStream_t s) {
+  k_kv_append<KT><<<dim3(T, nkv), 64, 0, s>>>(qkv, ldq, nh, nkv, hd, cs, kc, vc, max_ctx, pos0);
   CK(cudaGetLastError());
+  const size_t smem = attention_smem(hd, sizeof(KT));
   if (hd == 128)
-    k_attn_prefill<128><<<dim3(T, nkv), AT_THREADS, attention_smem(128), s>>>(qkv, ldq, cs, kc, vc, ctx, ldc, nh, nkv,
-                                                                               max_ctx, pos0, err);
+    k_attn_prefill<128, KT><<<dim3(T, nkv), AT_THREADS, smem, s>>>(qkv, ldq, cs, kc, vc, ctx, ldc, nh, nkv, max_ctx,
+                                                                   pos0, err);
   else
-    k_attn_prefill<64><<<dim3(T, nkv), AT_THREADS, attention_smem(64), s>>>(qkv, ldq, cs, kc, vc, ctx, ldc, nh, nkv,
-                                                                             max_ctx, pos0, err);
+    k_attn_prefill<64, KT><<<dim3(T, nkv), AT_THREADS, smem, s>>>(qkv, ldq, cs, kc, vc, ctx, ldc, nh, nkv, max_ctx,
+                                                                  pos0, err);
   CK(cudaGetLastError());
+}
+
+void launch_prefill_attention(const float* qkv, uint32_t ldq, const float* rope_cs, void* kc, void* vc, bool kv_f16,
+                              float* ctx, uint32_t ldc, uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t max_ctx,
+                              uint32_t pos0, uint32_t T, uint32_t* err, cudaStream_t s) {
+  const float2* cs = reinterpret_cast<const float2*>(rope_cs);
+  if (kv_f16)
+    prefill_attention_t(qkv, ldq, cs, static_cast<__half*>(kc), static_cast<__half*>(vc), ctx, ldc, nh, nkv, hd,
+                        max_ctx, pos0, T, err, s);
+  else
+    prefill_attention_t(qkv, ldq, cs, static_cast<float*>(kc), static_cast<float*>(vc), ctx, ldc, nh, nkv, hd, max_ctx,
+                        pos0, T, err, s);
 }
 
 // ---------------------------------------------------------------------------

@@ -110,14 +110,15 @@ void launch_embed(const DevMat& emb, StepState* st, float* x, cudaStream_t s);
 struct AttnLaunch {
   const float* qkv;      // [q | k | v] after bias
   const float* rope_cs;
-  float* kcache;
-  float* vcache;
+  void* kcache;          // f32, or f16 when kv_f16
+  void* vcache;
   float* ctx;            // [nh*hd]
   void* ctx_runs;        // run records of ctx (o_proj input)
   float* partials;       // attention_partial_floats(...) floats
   uint32_t n_heads, n_kv, hd, max_ctx, splits;
   StepState* state;
   uint32_t ctx_run0 = 0;  // run record index of ctx[0] in ctx_runs
+  int kv_f16 = 0;         // cache elements are f16
 };
 void launch_attention(const AttnLaunch& a, cudaStream_t s);
 uint32_t attention_splits(uint32_t n_kv);
@@ -162,8 +163,8 @@ void launch_xpanels(const float* x, uint32_t ld, uint32_t T, uint32_t K, const f
                     void* lo, cudaStream_t s);
 void launch_qgemm(const QgemmLaunch& q, cudaStream_t s);
 void launch_embed_rows(const DevMat& emb, const uint32_t* tokens, uint32_t T, float* x, uint32_t ld, cudaStream_t s);
-void launch_prefill_attention(const float* qkv, uint32_t ldq, const float* rope_cs, float* kc, float* vc, float* ctx,
-                              uint32_t ldc, uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t max_ctx, uint32_t pos0,
-                              uint32_t T, uint32_t* err, cudaStream_t s);
+void launch_prefill_attention(const float* qkv, uint32_t ldq, const float* rope_cs, void* kc, void* vc, bool kv_f16,
+                              float* ctx, uint32_t ldc, uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t max_ctx,
+                              uint32_t pos0, uint32_t T, uint32_t* err, cudaStream_t s);
 
 }  // namespace fz

@@ -267,45 +267,47 @@ __global__ void __launch_bounds__(128, 1) k_qgemm(const __grid_constant__ QgPara
 
 // KV append for a prefill chunk: rotated k and v of tokens t < T at
 // positions pos0 + t (src/model.rs:193-217, 340-352).  Grid (T, n_kv).
+template <typename KT>
 __global__ void k_kv_append(const float* __restrict__ qkv, uint32_t ldq, uint32_t nh, uint32_t nkv, uint32_t hd,
-                            const float2* __restrict__ cs, float* __restrict__ kc, float* __restrict__ vc,
+                            const float2* __restrict__ cs, KT* __restrict__ kc, KT* __restrict__ vc,
                             uint32_t max_ctx, uint32_t pos0) {
   const uint32_t t = blockIdx.x, h = blockIdx.y, half = hd / 2, pos = pos0 + t;
   const float* k = qkv + (uint64_t)t * ldq + (uint64_t)nh * hd + (uint64_t)h * hd;
   const float* v = qkv + (uint64_t)t * ldq + (uint64_t)(nh + nkv) * hd + (uint64_t)h * hd;
-  float* kd = kc + ((uint64_t)h * max_ctx + pos) * hd;
-  float* vd = vc + ((uint64_t)h * max_ctx + pos) * hd;
+  KT* kd = kc + ((uint64_t)h * max_ctx + pos) * hd;
+  KT* vd = vc + ((uint64_t)h * max_ctx + pos) * hd;
   const float2* c = cs + (uint64_t)pos * half;
   for (uint32_t i = threadIdx.x; i < half; i += blockDim.x) {
     const float a = k[i], b = k[i + half];
     const float2 cc = c[i];
-    kd[i] = __fsub_rn(__fmul_rn(a, cc.x), __fmul_rn(b, cc.y));
-    kd[i + half] = __fadd_rn(__fmul_rn(a, cc.y), __fmul_rn(b, cc.x));
-    vd[i] = v[i];
-    vd[i + half] = v[i + half];
+    kv_st(kd + i, __fsub_rn(__fmul_rn(a, cc.x), __fmul_rn(b, cc.y)));
+    kv_st(kd + i + half, __fadd_rn(__fmul_rn(a, cc.y), __fmul_rn(b, cc.x)));
+    kv_st(vd + i, v[i]);
+    kv_st(vd + i + half, v[i + half]);
   }
 }
 
 // Causal attention of prefill token t (position pos0 + t) over the cache
 // [0, pos0 + t] for the G query heads of KV head kvh (src/model.rs:371-438):
 // grid (T, n_kv), warp per head, 32-position tiles through bulk copies.
-template <int HD>
+template <int HD, typename KT>
 __global__ void __launch_bounds__(AT_THREADS) k_attn_prefill(const float* __restrict__ qkv, uint32_t ldq,
                                                               const float2* __restrict__ cs,
-                                                              const float* __restrict__ kc,
-                                                              const float* __restrict__ vc, float* __restrict__ ctx,
+                                                              const KT* __restrict__ kc,
+                                                              const KT* __restrict__ vc, float* __restrict__ ctx,
                                                               uint32_t ldc, uint32_t nh, uint32_t nkv,
                                                               uint32_t max_ctx, uint32_t pos0, uint32_t* err) {
   constexpr int DPL = HD / 32;
+  constexpr uint32_t EB = sizeof(KT);
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(16) float qs[AT_MAXG][HD];
   __shared__ __align__(8) uint64_t bar[AT_NBUF];
   const uint32_t G = nh / nkv, t = blockIdx.x, kvh = blockIdx.y;
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, half = HD / 2;
   const uint32_t pos = pos0 + t, n = pos + 1, ntiles = (n + AT_TP - 1) / AT_TP;
-  float* tiles = reinterpret_cast<float*>(smem);
-  const float* kvk = kc + (uint64_t)kvh * max_ctx * HD;
-  const float* kvv = vc + (uint64_t)kvh * max_ctx * HD;
+  KT* tiles = reinterpret_cast<KT*>(smem);
+  const KT* kvk = kc + (uint64_t)kvh * max_ctx * HD;
+  const KT* kvv = vc + (uint64_t)kvh * max_ctx * HD;
   if (tid == 0) {
     for (int b = 0; b < AT_NBUF; b++) mbar_init(&bar[b], 1);
     fence_barrier_init();
@@ -313,10 +315,10 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_prefill(const float* __rest
   const uint64_t pol = policy_evict_first();
   auto issue = [&](uint32_t j) {
     const uint32_t b = j % AT_NBUF, a = j * AT_TP, rows = min(n, a + AT_TP) - a;
-    float* kt = tiles + (size_t)b * 2 * AT_TP * HD;
-    mbar_expect_tx(&bar[b], 2 * rows * HD * 4);
-    bulk_g2s(kt, kvk + (uint64_t)a * HD, rows * HD * 4, &bar[b], pol);
-    bulk_g2s(kt + AT_TP * HD, kvv + (uint64_t)a * HD, rows * HD * 4, &bar[b], pol);
+    KT* kt = tiles + (size_t)b * 2 * AT_TP * HD;
+    mbar_expect_tx(&bar[b], 2 * rows * HD * EB);
+    bulk_g2s(kt, kvk + (uint64_t)a * HD, rows * HD * EB, &bar[b], pol);
+    bulk_g2s(kt + AT_TP * HD, kvv + (uint64_t)a * HD, rows * HD * EB, &bar[b], pol);
   };
   __syncthreads();
   if (tid == 0)
@@ -338,8 +340,8 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_prefill(const float* __rest
   bool ok = true;
   for (uint32_t j = 0; j < ntiles; j++) {
     const uint32_t b = j % AT_NBUF, tn = min(n, j * AT_TP + AT_TP) - j * AT_TP;
-    const float* kt = tiles + (size_t)b * 2 * AT_TP * HD;
-    const float* vt = kt + AT_TP * HD;
+    const KT* kt = tiles + (size_t)b * 2 * AT_TP * HD;
+    const KT* vt = kt + AT_TP * HD;
     if (!mbar_wait(&bar[b], (j / AT_NBUF) & 1)) {
       ok = false;
       break;
@@ -348,13 +350,13 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_prefill(const float* __rest
       const uint32_t tt = lane;
       float s = -INFINITY;
       if (tt < tn) {
-        const float4* kr = reinterpret_cast<const float4*>(kt + (size_t)tt * HD);
+        const KT* kr = kt + (size_t)tt * HD;
         const float4* qr = reinterpret_cast<const float4*>(qs[warp]);
         float dsum = 0.f;
 #pragma unroll 8
         for (uint32_t c = 0; c < HD / 4; c++) {
           const uint32_t cc = (c + tt) & (HD / 4 - 1);
-          const float4 k4 = kr[cc], q4 = qr[cc];
+          const float4 k4 = kv_ld4(kr, cc), q4 = qr[cc];
           dsum = fmaf(q4.x, k4.x, dsum);
           dsum = fmaf(q4.y, k4.y, dsum);
           dsum = fmaf(q4.z, k4.z, dsum);
@@ -377,9 +379,9 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_prefill(const float* __rest
       for (int d = 0; d < DPL; d++) acc[d] *= alpha;
       for (uint32_t t2 = 0; t2 < tn; t2++) {
         const float pt = __shfl_sync(0xffffffffu, pr, t2);
-        const float* vr = vt + (size_t)t2 * HD + lane * DPL;
+        const KT* vr = vt + (size_t)t2 * HD + lane * DPL;
 #pragma unroll
-        for (int d = 0; d < DPL; d++) acc[d] = fmaf(pt, vr[d], acc[d]);
+        for (int d = 0; d < DPL; d++) acc[d] = fmaf(pt, kv_ld(vr + d), acc[d]);
       }
     }
     __syncthreads();  // buffer b free

@@ -107,6 +107,14 @@ struct fz_model {
 struct fz_kv {
   fz_model* m = nullptr;
   uint32_t max_ctx = 0, len = 0, splits = 0;
+  uint32_t eb = 4;  // bytes per cached element: 4 (f32) or 2 (f16)
+  // layer li's K (or V) block [nkv_l][max_ctx][hd] of this rank
+  void* layer_k(uint32_t li, uint32_t nkv, uint32_t hd) const {
+    return k.as<uint8_t>() + (uint64_t)li * nkv * max_ctx * hd * eb;
+  }
+  void* layer_v(uint32_t li, uint32_t nkv, uint32_t hd) const {
+    return v.as<uint8_t>() + (uint64_t)li * nkv * max_ctx * hd * eb;
+  }
   DevBuf k, v, rope_cs, partials, state, forced, ids;
   cudaGraphExec_t g_full = nullptr, g_layers = nullptr;
   ~fz_kv() {
@@ -346,12 +354,11 @@ AttnLaunch layer_attention(fz_kv* kv, uint32_t li, uint32_t splits) {
   fz_model* m = kv->m;
   const fz_config& c = m->cfg;
   const uint32_t hd = c.head_dim;
-  float* kc = kv->k.as<float>() + (uint64_t)li * m->nkv_l * kv->max_ctx * hd;
-  float* vc = kv->v.as<float>() + (uint64_t)li * m->nkv_l * kv->max_ctx * hd;
-  AttnLaunch a{m->qkv.as<float>(), kv->rope_cs.as<float>(), kc, vc, m->ctx.as<float>(), m->runs_ctx.p,
-               kv->partials.as<float>(), m->nh_l, m->nkv_l, hd, kv->max_ctx, splits,
-               kv->state.as<StepState>()};
+  AttnLaunch a{m->qkv.as<float>(), kv->rope_cs.as<float>(), kv->layer_k(li, m->nkv_l, hd),
+               kv->layer_v(li, m->nkv_l, hd), m->ctx.as<float>(), m->runs_ctx.p, kv->partials.as<float>(), m->nh_l,
+               m->nkv_l, hd, kv->max_ctx, splits, kv->state.as<StepState>()};
   a.ctx_run0 = m->o_off[li] / 16;
+  a.kv_f16 = kv->eb == 2;
   return a;
 }
 
@@ -490,10 +497,9 @@ void prefill_tokens(fz_kv* kv, const uint32_t* tokens, uint32_t n, uint32_t pos0
       launch_wpanels(L.wv, L.wq.rows + L.wk.rows, m->pf_wh.p, m->pf_wl.p, s);
       gemm(H, ldq, T, PE_STORE, m->pf_qkv.as<float>(), ldq, L.bqkv);
       // rotated k / v into the cache, causal attention per token
-      float* kc = kv->k.as<float>() + (uint64_t)li * m->nkv_l * kv->max_ctx * hd;
-      float* vc = kv->v.as<float>() + (uint64_t)li * m->nkv_l * kv->max_ctx * hd;
-      launch_prefill_attention(m->pf_qkv.as<float>(), ldq, kv->rope_cs.as<float>(), kc, vc, m->pf_ctx.as<float>(), qd,
-                               m->nh_l, m->nkv_l, hd, kv->max_ctx, pos0 + c0, T, err, s);
+      launch_prefill_attention(m->pf_qkv.as<float>(), ldq, kv->rope_cs.as<float>(), kv->layer_k(li, m->nkv_l, hd),
+                               kv->layer_v(li, m->nkv_l, hd), kv->eb == 2, m->pf_ctx.as<float>(), qd, m->nh_l,
+                               m->nkv_l, hd, kv->max_ctx, pos0 + c0, T, err, s);
       // x += o_proj(ctx)
       launch_xpanels(m->pf_ctx.as<float>(), qd, T, qd, nullptr, 0.f, m->pf_xh.p, m->pf_xl.p, s);
       launch_wpanels(L.wo, 0, m->pf_wh.p, m->pf_wl.p, s);
@@ -645,6 +651,23 @@ void tp_gather_logits(fz_model* m, cudaStream_t s) {
   const size_t per = m->sl.vocab_pad / m->world;
   float* all = m->logits.as<float>();
   nccl_check(nccl().AllGather(all + (size_t)m->rank * per, all, per, ncclFloat32, m->comm, s), "ncclAllGather");
+}
+
+// IEEE binary16 -> binary32, exact (cached f16 KV elements read back).
+float half_to_float(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16, ex = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
+  uint32_t bits;
+  if (ex == 0) {
+    const float f = (float)man * 5.9604644775390625e-8f;  // man * 2^-24 (zero and subnormals)
+    return sign ? -f : f;
+  }
+  if (ex == 31)
+    bits = sign | 0x7F800000u | (man << 13);
+  else
+    bits = sign | ((ex + 112) << 23) | (man << 13);
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
 }
 
 void set_state(fz_kv* kv, uint32_t pos, uint32_t token, uint32_t n_forced) {
@@ -1114,14 +1137,16 @@ int fz_model_stream(const fz_model* m, void** stream, int* device) {
 int fz_kv_new(fz_model* m, uint32_t max_ctx, int kv_dtype, fz_kv** out) {
   return guard([&] {
     need(m && out, "null argument");
-    need(kv_dtype == FZ_KV_F32, "kv dtype %d unsupported (f32 only)", kv_dtype);
+    need(kv_dtype == FZ_KV_F32 || kv_dtype == FZ_KV_F16, "kv dtype %d unsupported (FZ_KV_F32 or FZ_KV_F16)",
+         kv_dtype);
     need(max_ctx > 0, "max_ctx must be positive");
     use_device(m);
     const fz_config& c = m->cfg;
     auto kv = std::make_unique<fz_kv>();
     kv->m = m;
     kv->max_ctx = max_ctx;
-    uint64_t per = (uint64_t)c.n_layers * m->nkv_l * max_ctx * c.head_dim * 4;  // this rank's KV heads
+    kv->eb = kv_dtype == FZ_KV_F16 ? 2 : 4;
+    uint64_t per = (uint64_t)c.n_layers * m->nkv_l * max_ctx * c.head_dim * kv->eb;  // this rank's KV heads
     kv->k.alloc(per);
     kv->v.alloc(per);
     CK(cudaMemset(kv->k.p, 0, per));
@@ -1184,11 +1209,19 @@ int fz_kv_read(const fz_kv* kv, uint32_t layer, int which_v, uint32_t n, float* 
     use_device(kv->m);
     uint32_t hd = c.head_dim;
     const uint32_t nkv = kv->m->nkv_l;  // this rank's KV heads
-    const float* base = (which_v ? kv->v : kv->k).as<float>() + (uint64_t)layer * nkv * kv->max_ctx * hd;
-    // device [kvh][pos][hd] -> host [pos][kvh*hd]
+    const uint8_t* base = static_cast<const uint8_t*>(which_v ? kv->layer_v(layer, nkv, hd) : kv->layer_k(layer, nkv, hd));
+    // device [kvh][pos][hd] -> host [pos][kvh*hd] (f16 elements widened exactly)
+    const uint32_t eb = kv->eb;
+    std::vector<uint8_t> raw((size_t)n * nkv * hd * eb);
     for (uint32_t h = 0; h < nkv; h++)
-      CK(cudaMemcpy2D(out + h * hd, (size_t)nkv * hd * 4, base + (uint64_t)h * kv->max_ctx * hd, hd * 4,
-                      hd * 4, n, cudaMemcpyDeviceToHost));
+      CK(cudaMemcpy2D(raw.data() + (size_t)h * hd * eb, (size_t)nkv * hd * eb, base + (uint64_t)h * kv->max_ctx * hd * eb,
+                      hd * eb, hd * eb, n, cudaMemcpyDeviceToHost));
+    if (eb == 4) {
+      memcpy(out, raw.data(), raw.size());
+    } else {
+      const uint16_t* r16 = reinterpret_cast<const uint16_t*>(raw.data());
+      for (size_t i = 0; i < (size_t)n * nkv * hd; i++) out[i] = half_to_float(r16[i]);
+    }
   });
 }
 
@@ -1419,7 +1452,7 @@ int fz_step_profile(fz_model* m, fz_kv* kv, uint32_t first, uint32_t reps, doubl
       for (auto& L : m->layers) {
         bytes[FZ_OP_QKV] += L.wq.gguf_bytes + L.wk.gguf_bytes + L.wv.gguf_bytes + (2 * H + qd + 2 * kd) * 4;
         bytes[FZ_OP_ROPE] += (qd + 2 * kd) * 4 + (qd + 2 * kd) * 4;
-        bytes[FZ_OP_ATTN] += 2 * (pos + 1) * kd * 4 + 2 * qd * 4;
+        bytes[FZ_OP_ATTN] += 2 * (pos + 1) * kd * kv->eb + 2 * qd * 4;
         bytes[FZ_OP_OPROJ] += L.wo.gguf_bytes + (qd + 2 * H) * 4;
         bytes[FZ_OP_GATEUP] += L.wgu.gguf_bytes + (2 * H + F) * 4;
         bytes[FZ_OP_DOWN] += L.wd.gguf_bytes + (F + 2 * H) * 4;

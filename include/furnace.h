@@ -45,8 +45,10 @@ enum {
 /* ggml tensor types the decode path computes on (src/gguf.rs:180-201). */
 enum { FZ_F32 = 0, FZ_F16 = 1, FZ_Q5_0 = 6, FZ_Q8_0 = 8, FZ_Q4_K = 12, FZ_Q6_K = 14 };
 
-/* KV cache element types.  F32 is the reference's (src/model.rs:321-327). */
-enum { FZ_KV_F32 = 0 };
+/* KV cache element types.  F32 is the reference's (src/model.rs:321-327);
+ * F16 keeps binary16 elements, rounded to nearest even when appended (the
+ * 8K-context cache of the 32B configuration: half the bytes per position). */
+enum { FZ_KV_F32 = 0, FZ_KV_F16 = 1 };
 
 typedef struct fz_file fz_file;   /* GgufFile (src/gguf.rs:297-304) */
 typedef struct fz_model fz_model; /* Model (src/model.rs:511-517), resident in HBM */
@@ -141,7 +143,8 @@ int fz_tp_unique_id(void* id, size_t n);
  * ranks' NCCL communicator (collective: every rank must call it). */
 int fz_model_load_tp(const fz_file* f, int rank, int world, const void* id, size_t n, int device, fz_model** out);
 
-/* KvCache::new (src/model.rs:330-339): max_ctx positions, f32 elements. */
+/* KvCache::new (src/model.rs:330-339): max_ctx positions of kv_dtype
+ * (FZ_KV_F32 or FZ_KV_F16) elements. */
 int fz_kv_new(fz_model* m, uint32_t max_ctx, int kv_dtype, fz_kv** out);
 void fz_kv_free(fz_kv* kv);
 /* KvCache::len (src/model.rs:324).  set_len rewinds (or restores) the

@@ -793,7 +793,34 @@ void linear(const float* x, size_t seq, const Weight& w, const std::vector<float
 struct KvCache {
   std::vector<std::vector<float>> k, v;
   size_t len = 0, max_ctx = 0, kv_dim = 0;
+  bool f16 = false;  // elements kept as IEEE binary16 (rounded to nearest even when appended)
 };
+
+// binary32 -> binary16, round to nearest even (overflow to infinity,
+// gradual underflow); the device's __float2half_rn rounding.
+uint16_t float_to_half_rne(float f) {
+  uint32_t x;
+  memcpy(&x, &f, 4);
+  const uint32_t sign = (x >> 16) & 0x8000u, ex = (x >> 23) & 0xFFu;
+  uint32_t man = x & 0x7FFFFFu;
+  if (ex == 0xFF) return (uint16_t)(sign | 0x7C00u | (man ? 0x200u : 0u));
+  const int e = (int)ex - 127 + 15;
+  if (e >= 31) return (uint16_t)(sign | 0x7C00u);
+  if (e <= 0) {
+    if (e < -10) return (uint16_t)sign;
+    man |= 0x800000u;
+    const uint32_t shift = (uint32_t)(14 - e), rem = man & ((1u << shift) - 1), halfway = 1u << (shift - 1);
+    uint32_t h = man >> shift;
+    if (rem > halfway || (rem == halfway && (h & 1u))) h++;
+    return (uint16_t)(sign | h);
+  }
+  uint32_t h = ((uint32_t)e << 10) | (man >> 13);
+  const uint32_t rem = man & 0x1FFFu;
+  if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h++;  // a carry moves to the next binade / infinity
+  return (uint16_t)(sign | h);
+}
+
+float round_to_half(float f) { return f16_to_f32(float_to_half_rne(f)); }
 
 // attention_scores_cached + softmax + attention_apply_cached
 // (src/model.rs:371-438); the uncached variants (:224-290) are the same
@@ -850,6 +877,11 @@ void layer_forward(const float* x, size_t n_new, const Layer& L, const Config& c
   rope(q.data(), n_new, nh, hd, c.rope_theta, start_pos);
   rope(k.data(), n_new, nkv, hd, c.rope_theta, start_pos);
   if (cache) {
+    if (cache->f16)
+      for (size_t i = 0; i < n_new * kd; i++) {
+        k[i] = round_to_half(k[i]);
+        v[i] = round_to_half(v[i]);
+      }
     memcpy(cache->k[li].data() + start_pos * kd, k.data(), sizeof(float) * n_new * kd);
     memcpy(cache->v[li].data() + start_pos * kd, v.data(), sizeof(float) * n_new * kd);
     size_t total = start_pos + n_new;
@@ -1154,6 +1186,8 @@ void* orc_kv_new(void* mp, size_t max_ctx) {
   return kv;
 }
 void orc_kv_free(void* kv) { delete (KvCache*)kv; }
+void orc_kv_set_f16(void* kv, int on) { ((KvCache*)kv)->f16 = on != 0; }
+uint16_t orc_float_to_half(float f) { return float_to_half_rne(f); }
 size_t orc_kv_len(void* kv) { return ((KvCache*)kv)->len; }
 void orc_kv_set_len(void* kv, size_t n) { ((KvCache*)kv)->len = n; }
 

@@ -66,6 +66,8 @@ def lib():
             "orc_model_truncate": (None, [P, U32]),
             "orc_kv_new": (P, [P, S]),
             "orc_kv_free": (None, [P]),
+            "orc_kv_set_f16": (None, [P, I]),
+            "orc_float_to_half": (C.c_uint16, [F]),
             "orc_kv_len": (S, [P]),
             "orc_kv_set_len": (None, [P, S]),
             "orc_kv_read": (I, [P, S, I, S, fp]),
@@ -117,6 +119,11 @@ def set_threads(n: int):
 
 def threads() -> int:
     return lib().orc_threads()
+
+
+def float_to_half(f: float) -> int:
+    """binary32 -> binary16 bits, round to nearest even."""
+    return lib().orc_float_to_half(f)
 
 
 def f16_to_f32(h: int) -> float:
@@ -244,8 +251,8 @@ class Model:
         lib().orc_model_truncate(self._h, n_layers)
         self.n_layers = min(self.n_layers, n_layers)
 
-    def kv_new(self, max_ctx: int) -> "KvCache":
-        return KvCache(self, max_ctx)
+    def kv_new(self, max_ctx: int, kv_dtype: int = 0) -> "KvCache":
+        return KvCache(self, max_ctx, kv_dtype)
 
     def forward_cached(self, tokens, cache: "KvCache") -> np.ndarray:
         t = np.ascontiguousarray(tokens, dtype=np.uint32)
@@ -309,10 +316,14 @@ class Model:
 class KvCache:
     """KvCache (src/model.rs:321-363)."""
 
-    def __init__(self, model: Model, max_ctx: int):
+    def __init__(self, model: Model, max_ctx: int, kv_dtype: int = 0):
+        """kv_dtype 1: elements kept as IEEE binary16, rounded to nearest even
+        when appended (the device's FZ_KV_F16 cache); 0: f32 (the reference)."""
         self.model = model
         self.max_ctx = max_ctx
         self._h = lib().orc_kv_new(model._h, max_ctx)
+        if kv_dtype:
+            lib().orc_kv_set_f16(self._h, 1)
 
     def __del__(self):
         try:

@@ -203,6 +203,42 @@ def test_forward_last_matches_oracle_uncached(tiny):
         dev.forward_last([dev.config.vocab])
 
 
+def test_f16_kv_cache_matches_oracle(tiny):
+    """FZ_KV_F16: the cache keeps binary16 elements rounded to nearest even
+    (the 32B configuration's 8K-context cache).  Against the oracle with the
+    same rounding: the cached rows, then 48 greedy steps (batched prefill of
+    a 20-token prompt, decode graph) with identical ids and logits within the
+    bar."""
+    f, dev, ref = _models(tiny)
+    ids = synth.prompt_ids(ref.vocab, 20, seed=21)
+    kd, kr = fz.KvCache(dev, 96, fz.FZ_KV_F16), ref.kv_new(96, kv_dtype=1)
+    got, am = dev.forward(ids, kd)
+    want = ref.forward_cached(ids, kr)
+    _check_logits(got, want, "f16 prefill")
+    for layer in range(ref.n_layers):
+        for which in (0, 1):
+            a, b = kd.read(layer, which, 20), kr.read(layer, which, 20)
+            # both round to binary16; the f32 inputs differ by GEMV rounding,
+            # so an element may land one binary16 step apart, a step of the
+            # largest element (2^-10 relative) bounding every element's
+            assert np.abs(a - b).max() <= 2.0 ** -10 * max(1.0, np.abs(b).max()), (layer, which)
+            assert np.mean(a == b) > 0.9, (layer, which)  # mostly bit-identical
+    tok, want_ids = am, []
+    for s in range(48):
+        want_ids.append(tok)
+        lg = ref.forward_cached([tok], kr)
+        tok = int(np.argmax(lg))
+    got_ids, got_lg = dev.decode_greedy(am, 48, kd, keep_logits=True)
+    assert got_ids.tolist() == want_ids
+    kr2 = ref.kv_new(96, kv_dtype=1)
+    ref.forward_cached(ids, kr2)
+    for s in range(47):
+        _check_logits(got_lg[s], ref.forward_cached([want_ids[s]], kr2), f"f16 step {s}")
+    with pytest.raises(fz.FurnaceError) as e:
+        fz.KvCache(dev, 8, 7)
+    assert e.value.code == fz.FZ_EINVAL
+
+
 def test_forward_rejects_bad_input(tiny):
     f, dev, _ = _models(tiny)
     kv = fz.KvCache(dev, 8)

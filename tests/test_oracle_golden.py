@@ -208,3 +208,16 @@ def test_gguf_parse_synthetic(orc):
         orc.parse_gguf_bytes(b"GGML\x03\x00\x00\x00")
     with pytest.raises(orc.OracleError):
         orc.parse_gguf_bytes(data[:40])
+
+
+def test_half_rounding_matches_numpy(orc):
+    """The f16 KV cache's rounding (binary32 -> binary16, nearest even, with
+    gradual underflow and overflow to infinity) against numpy's cast."""
+    rng = np.random.default_rng(5)
+    x = np.concatenate([rng.normal(0, 3, 20000), rng.normal(0, 1e-5, 2000),
+                        [0.0, -0.0, 65504, 65519.99, 65520, 1e30, -1e30, np.inf, -np.inf,
+                         2.9802322e-8, 2.98e-8, 5.96e-8, 6.1035156e-05, 3.0517578e-05]]).astype(np.float32)
+    mine = np.array([orc.float_to_half(float(v)) for v in x], np.uint16)
+    with np.errstate(over="ignore"):
+        ref = x.astype(np.float16).view(np.uint16)
+    assert np.array_equal(mine, ref)
