@@ -382,8 +382,9 @@ def run_ours(args, dist):
                  "note": "host wall clock of fz_model_load(_tp): GGUF bytes of this rank's share from the "
                          "page cache to the device and the repack into the chunk layout"},
         "prefill": {"tokens": args.prefill, "s": prefill_s, "tok_s": args.prefill / prefill_s,
-                    "path": "tcgen05 GEMM (fp16 hi/lo split, f32 accumulation) for all but the last prompt token"
-                    if tp == 1 and args.prefill > 8 else "decode step per token",
+                    "path": ("tcgen05 GEMM (fp16 hi/lo split, f32 accumulation) for all but the last prompt token"
+                             + (f", residual partials all-reduced over {tp} ranks (NCCL)" if tp > 1 else ""))
+                    if args.prefill > 8 else "decode step per token",
                     "note": "host wall clock of fz_forward over the prompt, including the per-layer weight "
                             "dequantization into GEMM panels"},
         "gpu_launches": launches_per_token * total_tokens, "clocks": clocks, "e2e": e2e, "roofline": roofline,

@@ -284,6 +284,7 @@ class Model:
         c = _Config()
         _check(load_library().fz_model_config(self._h, C.byref(c)))
         self.config = Config._from_c(c)
+        self.rank, self.world = 0, 1  # tensor-parallel share (load_tp)
 
     @classmethod
     def load(cls, f: GgufFile, tp: int = 1, devices=None) -> "Model":
@@ -300,7 +301,9 @@ class Model:
         h = C.c_void_p()
         buf = C.create_string_buffer(bytes(nccl_id), max(len(nccl_id), 1)) if nccl_id else None
         _check(load_library().fz_model_load_tp(f._h, rank, world, buf, len(nccl_id or b""), device, C.byref(h)))
-        return cls(h)
+        m = cls(h)
+        m.rank, m.world = rank, world
+        return m
 
     def close(self):
         if self._h:
@@ -412,8 +415,11 @@ class KvCache:
         _check(load_library().fz_kv_set_len(self._h, n))
 
     def read(self, layer: int, which_v: bool, n: int) -> np.ndarray:
-        c = self.model.config
-        out = np.zeros((n, c.n_kv_heads * c.head_dim), np.float32)
+        """Cached K (or V) rows [0, n) as [n, kv_heads * head_dim]: every KV
+        head, or this rank's under tensor parallelism."""
+        c, m = self.model.config, self.model
+        kvh = c.n_kv_heads // m.world
+        out = np.zeros((n, kvh * c.head_dim), np.float32)
         _check(load_library().fz_kv_read(self._h, layer, int(which_v), n, _fp(out)))
         return out
 

@@ -82,7 +82,12 @@ struct fz_model {
   uint64_t resident = 0, streamed = 0;
   // activations (f32) and the run records GEMVs read (see kernels.cu)
   DevBuf x, qkv, ctx, h, logits;
-  DevBuf runs_ctx, runs_h;  // attention output and ffn hidden as run records
+  DevBuf runs_h;  // ffn hidden as run records
+  // attention output as run records, one buffer per distinct o_off value:
+  // the layers sharing a buffer write the same records, so the records of
+  // o_proj's padding columns are never written and stay zero
+  std::vector<std::unique_ptr<DevBuf>> runs_ctx;
+  std::vector<uint32_t> ctx_buf;  // per layer: index into runs_ctx
   DevBuf trace;             // decode-step timeline (FURNACE_B200_TRACE=<file>)
   std::string trace_path;
   // tensor parallelism: this rank's share (world == 1: everything)
@@ -319,7 +324,7 @@ std::vector<GemvLaunch> step_gemvs(fz_kv* kv) {
     g.epilogue = EPI_STORE;
     GemvLaunch& go = gl[4 * li + 1];
     go.seg[0] = GemvSeg{L.wo, nullptr, x};
-    go.in_runs = m->runs_ctx.p;
+    go.in_runs = m->runs_ctx[m->ctx_buf[li]]->p;
     go.epilogue = resid;
     GemvLaunch& gu = gl[4 * li + 2];
     gu.seg[0] = GemvSeg{L.wgu, nullptr, nullptr};
@@ -355,14 +360,13 @@ AttnLaunch layer_attention(fz_kv* kv, uint32_t li, uint32_t splits) {
   const fz_config& c = m->cfg;
   const uint32_t hd = c.head_dim;
   AttnLaunch a{m->qkv.as<float>(), kv->rope_cs.as<float>(), kv->layer_k(li, m->nkv_l, hd),
-               kv->layer_v(li, m->nkv_l, hd), m->ctx.as<float>(), m->runs_ctx.p, kv->partials.as<float>(), m->nh_l,
+               kv->layer_v(li, m->nkv_l, hd), m->ctx.as<float>(), m->runs_ctx[m->ctx_buf[li]]->p, kv->partials.as<float>(), m->nh_l,
                m->nkv_l, hd, kv->max_ctx, splits, kv->state.as<StepState>()};
   a.ctx_run0 = m->o_off[li] / 16;
   a.kv_f16 = kv->eb == 2;
   return a;
 }
 
-// Sum of the ranks' residual-stream partials (tensor parallelism).
 // Sum of the ranks' residual-stream partials (tensor parallelism) where the
 // peer-memory exchange inside the GEMVs is unavailable (a rank could not
 // export its buffer, or FURNACE_B200_TP_ALLREDUCE=nccl): ncclAllReduce.
@@ -430,16 +434,20 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
 constexpr uint32_t PF_CHUNK = 8192;  // tokens per prefill pass (each weight is dequantized once per pass)
 constexpr uint32_t PF_MIN = 8;       // shorter prompts replay the decode step
 
+// Every GEMM's reduction width (hidden, this rank's o_proj input and FFN
+// slice) must be a multiple of 64, the k-step of the panels.
 bool prefill_supported(const fz_model* m) {
-  const fz_config& c = m->cfg;
-  return m->world == 1 && c.hidden % 64 == 0 && c.ffn % 64 == 0 && (c.n_heads * c.head_dim) % 64 == 0;
+  if (m->cfg.hidden % 64) return false;
+  for (const Layer& L : m->layers)
+    if (L.wo.cols % 64 || L.wd.cols % 64) return false;
+  return true;
 }
 
 void prefill_alloc(fz_model* m, uint32_t T) {
   if (m->pf_cap >= T) return;
   const fz_config& c = m->cfg;
   const uint32_t H = c.hidden, F = c.ffn, qd = m->qd_l, kd = m->kd_l;
-  const uint32_t maxK = std::max(std::max(H, F), qd);
+  const uint32_t maxK = std::max(std::max(H, F), std::max(qd, m->o_w));
   uint64_t wmax = 0;
   for (auto& L : m->layers) {
     wmax = std::max(wmax, wpanel_elems(L.wq.rows + L.wk.rows + L.wv.rows, H));
@@ -449,7 +457,7 @@ void prefill_alloc(fz_model* m, uint32_t T) {
   }
   m->pf_x.alloc((uint64_t)T * H * 4);
   m->pf_qkv.alloc((uint64_t)T * (qd + 2 * kd) * 4);
-  m->pf_ctx.alloc((uint64_t)T * qd * 4);
+  m->pf_ctx.alloc((uint64_t)T * std::max(qd, m->o_w) * 4);
   m->pf_h.alloc((uint64_t)T * F * 4);
   m->pf_tok.alloc((uint64_t)T * 4);
   m->pf_err.alloc(16);
@@ -471,18 +479,35 @@ void prefill_alloc(fz_model* m, uint32_t T) {
 // Tokens [0, n) at positions pos0.. through every layer, batched
 // (Model::forward_cached, src/model.rs:444-478, 579-592, without the logits):
 // x rows, the KV cache rows pos0..pos0+n, nothing else.
+//
+// Tensor parallelism: x [T, H] is replicated; each rank projects q/k/v of its
+// heads, attends over its KV heads and multiplies its o_proj columns and its
+// FFN slice, so o_proj and down leave per-rank partials of the residual
+// update.  Rank 0 adds its partial to x, the others to zeros, and one
+// all-reduce (sum) over [T, H] restores the replicated x.
 void prefill_tokens(fz_kv* kv, const uint32_t* tokens, uint32_t n, uint32_t pos0) {
   fz_model* m = kv->m;
   const fz_config& c = m->cfg;
   cudaStream_t s = m->stream;
-  const uint32_t H = c.hidden, F = c.ffn, hd = c.head_dim, qd = m->qd_l, kd = m->kd_l, ldq = qd + 2 * kd;
+  const uint32_t H = c.hidden, hd = c.head_dim, qd = m->qd_l, kd = m->kd_l, ldq = qd + 2 * kd;
+  // ctx rows are o_proj's block-aligned input: this rank's heads start at
+  // column o_off[li], the rest (a neighbour's share of a boundary block) is 0
+  const uint32_t ldc = std::max(qd, m->o_w);
   prefill_init();
   prefill_alloc(m, std::min(n, PF_CHUNK));
   float* X = m->pf_x.as<float>();
+  float* ctx = m->pf_ctx.as<float>();
   uint32_t* err = m->pf_err.as<uint32_t>();
   auto gemm = [&](uint32_t K, uint32_t N, uint32_t T, int epi, float* out, uint32_t ld, const float* bias) {
     QgemmLaunch q{m->pf_wh.p, m->pf_wl.p, m->pf_xh.p, m->pf_xl.p, K, N, T, epi, out, ld, bias, err};
     launch_qgemm(q, s);
+  };
+  // x += the [T, K] activations (panels built) times w (panels built), summed over ranks
+  auto resid = [&](uint32_t K, uint32_t T) {
+    if (m->world > 1 && m->rank != 0) CK(cudaMemsetAsync(X, 0, (size_t)T * H * 4, s));
+    gemm(K, H, T, PE_RESID, X, H, nullptr);
+    if (m->world > 1)
+      nccl_check(nccl().AllReduce(X, X, (size_t)T * H, ncclFloat32, ncclSum, m->comm, s), "ncclAllReduce");
   };
   for (uint32_t c0 = 0; c0 < n; c0 += PF_CHUNK) {
     const uint32_t T = std::min(PF_CHUNK, n - c0);
@@ -490,6 +515,7 @@ void prefill_tokens(fz_kv* kv, const uint32_t* tokens, uint32_t n, uint32_t pos0
     launch_embed_rows(m->embd, m->pf_tok.as<uint32_t>(), T, X, H, s);
     for (uint32_t li = 0; li < c.n_layers; li++) {
       Layer& L = m->layers[li];
+      const uint32_t F_l = L.wd.cols;
       // q, k, v (+ bias) of RMSNorm(x)
       launch_xpanels(X, H, T, H, L.attn_norm, c.rms_eps, m->pf_xh.p, m->pf_xl.p, s);
       launch_wpanels(L.wq, 0, m->pf_wh.p, m->pf_wl.p, s);
@@ -497,20 +523,21 @@ void prefill_tokens(fz_kv* kv, const uint32_t* tokens, uint32_t n, uint32_t pos0
       launch_wpanels(L.wv, L.wq.rows + L.wk.rows, m->pf_wh.p, m->pf_wl.p, s);
       gemm(H, ldq, T, PE_STORE, m->pf_qkv.as<float>(), ldq, L.bqkv);
       // rotated k / v into the cache, causal attention per token
+      if (L.wo.cols != qd) CK(cudaMemsetAsync(ctx, 0, (size_t)T * ldc * 4, s));
       launch_prefill_attention(m->pf_qkv.as<float>(), ldq, kv->rope_cs.as<float>(), kv->layer_k(li, m->nkv_l, hd),
-                               kv->layer_v(li, m->nkv_l, hd), kv->eb == 2, m->pf_ctx.as<float>(), qd, m->nh_l,
+                               kv->layer_v(li, m->nkv_l, hd), kv->eb == 2, ctx + m->o_off[li], ldc, m->nh_l,
                                m->nkv_l, hd, kv->max_ctx, pos0 + c0, T, err, s);
       // x += o_proj(ctx)
-      launch_xpanels(m->pf_ctx.as<float>(), qd, T, qd, nullptr, 0.f, m->pf_xh.p, m->pf_xl.p, s);
+      launch_xpanels(ctx, ldc, T, L.wo.cols, nullptr, 0.f, m->pf_xh.p, m->pf_xl.p, s);
       launch_wpanels(L.wo, 0, m->pf_wh.p, m->pf_wl.p, s);
-      gemm(qd, H, T, PE_RESID, X, H, nullptr);
+      resid(L.wo.cols, T);
       // h = swiglu(gate, up)(RMSNorm(x)); x += down(h)
       launch_xpanels(X, H, T, H, L.ffn_norm, c.rms_eps, m->pf_xh.p, m->pf_xl.p, s);
       launch_wpanels(L.wgu, 0, m->pf_wh.p, m->pf_wl.p, s);
-      gemm(H, L.wgu.rows, T, PE_SWIGLU, m->pf_h.as<float>(), F, nullptr);
-      launch_xpanels(m->pf_h.as<float>(), F, T, F, nullptr, 0.f, m->pf_xh.p, m->pf_xl.p, s);
+      gemm(H, L.wgu.rows, T, PE_SWIGLU, m->pf_h.as<float>(), F_l, nullptr);
+      launch_xpanels(m->pf_h.as<float>(), F_l, T, F_l, nullptr, 0.f, m->pf_xh.p, m->pf_xl.p, s);
       launch_wpanels(L.wd, 0, m->pf_wh.p, m->pf_wl.p, s);
-      gemm(F, H, T, PE_RESID, X, H, nullptr);
+      resid(F_l, T);
     }
   }
   uint32_t e = 0;
@@ -1014,7 +1041,17 @@ std::unique_ptr<fz_model> load_model(const fz_file* f, int rank, int world, cons
     b.alloc((uint64_t)runs_for(n) * 64);
     CK(cudaMemset(b.p, 0, b.n));  // padding records past the vector must read as zero
   };
-  runs(m->runs_ctx, m->o_w);
+  std::vector<uint32_t> offs;  // distinct o_off values, in order of first use
+  m->ctx_buf.assign(c.n_layers, 0);
+  for (uint32_t i = 0; i < c.n_layers; i++) {
+    size_t b = std::find(offs.begin(), offs.end(), m->o_off[i]) - offs.begin();
+    if (b == offs.size()) {
+      offs.push_back(m->o_off[i]);
+      m->runs_ctx.push_back(std::make_unique<DevBuf>());
+      runs(*m->runs_ctx.back(), m->o_w);
+    }
+    m->ctx_buf[i] = (uint32_t)b;
+  }
   runs(m->runs_h, F_l);
   // byte accounting (this rank)
   m->resident = total + smalls.size() * 4;

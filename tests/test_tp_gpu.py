@@ -40,7 +40,7 @@ def _rank(rank, world, port, path, n_prompt, n_new, q):
         m = fz.Model.load_tp(f, rank, world, ids[0], rank)
         prompt = synth.prompt_ids(m.config.vocab, n_prompt, seed=2)
         got_ids, got_lg = fz.generate(m, prompt, n_new, max_ctx=n_prompt + n_new, keep_logits=True)
-        q.put((rank, got_ids.tolist(), got_lg if rank == 0 else None))
+        q.put((rank, (got_ids.tolist(), got_lg if rank == 0 else None), None))
         m.close()
         dist.barrier()
     except Exception as e:  # reported to the parent, which fails the test
@@ -49,31 +49,62 @@ def _rank(rank, world, port, path, n_prompt, n_new, q):
         dist.destroy_process_group()
 
 
-def _run_tp(path, n_prompt, n_new, world=2):
-    import torch.multiprocessing as mp
+def _rank_prefill(rank, world, port, path, n_prompt, q):
+    """One forward over the prompt (batched prefill for all but the last
+    token), returning the logits and this rank's cached K/V rows."""
+    import torch.distributed as dist
 
-    from oracle import oracle
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ids = [fz.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(ids, src=0)
+        f = fz.GgufFile.open(path)
+        m = fz.Model.load_tp(f, rank, world, ids[0], rank)
+        prompt = synth.prompt_ids(m.config.vocab, n_prompt, seed=5)
+        kv = fz.KvCache(m, n_prompt + 4)
+        lg, am = m.forward(prompt, kv)
+        rows = {(li, w): kv.read(li, w, n_prompt) for li in range(m.config.n_layers) for w in (0, 1)}
+        q.put((rank, (lg, am, rows), None))
+        kv.close()
+        m.close()
+        dist.barrier()
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, repr(e), None))
+    finally:
+        dist.destroy_process_group()
+
+
+def _spawn(target, world, *args):
+    import torch.multiprocessing as mp
 
     with socket.socket() as sk:
         sk.bind(("127.0.0.1", 0))
         port = sk.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, path, n_prompt, n_new, q)) for r in range(world)]
+    procs = [ctx.Process(target=target, args=(r, world, port) + args + (q,)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
     try:
         for _ in range(world):
-            r, ids, lg = q.get(timeout=600)
-            res[r] = (ids, lg)
+            r, v, _ = q.get(timeout=600)
+            res[r] = v
     finally:
         for p in procs:
             p.join(60)
             if p.is_alive():
                 p.kill()
     for r in range(world):
-        assert isinstance(res[r][0], list), f"rank {r}: {res[r][0]}"
+        assert not isinstance(res[r], str), f"rank {r}: {res[r]}"
+    return res
+
+
+def _run_tp(path, n_prompt, n_new, world=2):
+    from oracle import oracle
+
+    res = _spawn(_rank, world, path, n_prompt, n_new)
     ref = oracle.Model(path)
     prompt = synth.prompt_ids(ref.vocab, n_prompt, seed=2)
     want_ids, want_lg, _, _ = ref.generate(prompt, n_new, keep_logits=True)
@@ -102,3 +133,33 @@ def test_tp2_greedy_tiny(tmp_path):
 def test_tp2_greedy_c1():
     """configs[0] (Q8_0, 14 heads / 2 KV heads) split over 2 GPUs, 128 steps."""
     _run_tp(synth.ensure("c1"), 32, 128)
+
+
+@pytest.mark.parametrize("over", [{}, {"hidden": 768, "n_heads": 12}], ids=["tiny", "tiny-768"])
+def test_tp2_batched_prefill(tmp_path, over):
+    """A 100-token prompt through the batched prefill on 2 ranks: each rank's
+    cached K/V rows equal the oracle's rows of its KV heads (1e-4 of the
+    largest element, as on one GPU), the prompt's logits meet the logits bar,
+    and greedy decoding after it gives the oracle's ids.  With 12 heads of 64
+    each rank's o_proj input (384 columns) widens to whole 256-element Q4_K
+    blocks in odd layers, so ctx sits at an offset inside zero padding."""
+    from oracle import oracle
+
+    path = synth.write(synth.spec("tiny", **over), str(tmp_path / "tiny.gguf"))
+    n, world = 100, 2
+    res = _spawn(_rank_prefill, world, path, n)
+    ref = oracle.Model(path)
+    prompt = synth.prompt_ids(ref.vocab, n, seed=5)
+    kr = ref.kv_new(n + 4)
+    want = ref.forward_cached(prompt, kr)
+    for r in range(world):
+        lg, am, rows = res[r]
+        _check_top5(lg, want, f"rank {r} prefill logits")
+        assert np.abs(lg - want).max() <= LOGIT_ABS, f"rank {r}: logits max-abs {np.abs(lg - want).max()}"
+        assert am == int(np.argmax(want)), f"rank {r}: argmax"
+        kvh = ref.n_kv_heads // world
+        cols = slice(r * kvh * ref.head_dim, (r + 1) * kvh * ref.head_dim)
+        for (li, w), a in rows.items():
+            b = kr.read(li, w, n)[:, cols]
+            assert np.abs(a - b).max() <= 1e-4 * max(1.0, np.abs(b).max()), (r, li, w)
+    _run_tp(path, n, 24)
