@@ -226,15 +226,17 @@ void launch_repack(uint32_t dtype, const uint8_t* raw, uint8_t* dst, uint32_t r0
 
 // ---------------------------------------------------------------------------
 // Exact dequantization of one 64-element unit of a chunked row
-// (src/quant.rs:35-39, 53-63, 78-109, 114-133).
+// (src/quant.rs:35-39, 53-63, 78-109, 114-133) into o[0..64) (o[0..32) for
+// the last unit of a row of 32 mod 64 Q8_0 / Q5_0 columns).  Inlined with
+// constant indices, so o may be a register array.
 // ---------------------------------------------------------------------------
-__device__ void dequant_unit(uint32_t dt, const uint8_t* base, uint32_t rows, uint32_t r, uint32_t cols, uint32_t u,
-                             float* o) {
+__device__ __forceinline__ void dequant_unit(uint32_t dt, const uint8_t* base, uint32_t rows, uint32_t r,
+                                             uint32_t cols, uint32_t u, float* o) {
   uint32_t c = lay_chunk_of(dt, cols, u);
   uint32_t cu0 = lay_cu0(dt, cols, c), nu = lay_cu0(dt, cols, c + 1) - cu0, lu = u - cu0;
   const uint8_t* ch = base + lay_tile_off(dt, cols, rows, r, c);
   if (dt == FZ_Q4_K) {
-    uint32_t sb = u >> 2, j64 = u & 3;
+    uint32_t j64 = u & 3;
     const uint8_t* blk = ch + 144 * (lu >> 2);
     float d = h2f(blk[0] | (blk[1] << 8)), dmin = h2f(blk[2] | (blk[3] << 8));
     const uint8_t* s = blk + 4;
@@ -255,34 +257,36 @@ __device__ void dequant_unit(uint32_t dt, const uint8_t* base, uint32_t rows, ui
     float d1 = __fmul_rn(d, scv[0]), min1 = __fmul_rn(dmin, mv[0]);
     float d2 = __fmul_rn(d, scv[1]), min2 = __fmul_rn(dmin, mv[1]);
     const uint8_t* q = blk + 16 + 32 * j64;
-    float* oa = o + 256 * sb + 64 * j64;
+#pragma unroll
     for (int l = 0; l < 32; l++) {
-      oa[l] = __fsub_rn(__fmul_rn(d1, (float)(q[l] & 0x0F)), min1);
-      oa[32 + l] = __fsub_rn(__fmul_rn(d2, (float)(q[l] >> 4)), min2);
+      o[l] = __fsub_rn(__fmul_rn(d1, (float)(q[l] & 0x0F)), min1);
+      o[32 + l] = __fsub_rn(__fmul_rn(d2, (float)(q[l] >> 4)), min2);
     }
   } else if (dt == FZ_Q6_K) {
     const uint32_t k = u & 3;
     const uint8_t* body = ch + 208 * (lu >> 2);
     const uint8_t* dp = ch + 208 * (nu >> 2) + 2 * (lu >> 2);
     float d = h2f(dp[0] | (dp[1] << 8));
-    float* ou = o + 64 * u;
+#pragma unroll
     for (uint32_t i = 0; i < 64; i++) {
       uint32_t nib = (body[32 * k + (i & 31)] >> (i < 32 ? 0 : 4)) & 15;
       uint32_t hb = (body[128 + 16 * k + (i & 15)] >> (2 * (i >> 4))) & 3;
       int q = (int)(nib | (hb << 4)) - 32;
       float sc = (float)(int8_t)body[192 + 4 * k + (i >> 4)];
-      ou[i] = __fmul_rn(__fmul_rn(d, sc), (float)q);  // (d * sc) * q, src/quant.rs:127-130
+      o[i] = __fmul_rn(__fmul_rn(d, sc), (float)q);  // (d * sc) * q, src/quant.rs:127-130
     }
   } else {
     uint32_t nb = cols / 32;
+#pragma unroll
     for (uint32_t k = 0; k < 2; k++) {
       uint32_t blk = 2 * u + k;
       if (blk >= nb) break;
-      float* ob = o + 32 * blk;
+      float* ob = o + 32 * k;
       if (dt == FZ_Q8_0) {
         const uint8_t* dp = ch + 64 * nu + 4 * lu + 2 * k;
         float d = h2f(dp[0] | (dp[1] << 8));
         const uint8_t* q = ch + 64 * lu + 32 * k;
+#pragma unroll
         for (int i = 0; i < 32; i++) ob[i] = __fmul_rn(d, (float)(int8_t)q[i]);
       } else {
         const uint8_t* qs = ch + 32 * lu + 16 * k;
@@ -290,6 +294,7 @@ __device__ void dequant_unit(uint32_t dt, const uint8_t* base, uint32_t rows, ui
         uint32_t qh = hp[0] | (hp[1] << 8) | (hp[2] << 16) | ((uint32_t)hp[3] << 24);
         const uint8_t* dp = ch + 32 * nu + round16u(8 * nu) + 4 * lu + 2 * k;
         float d = h2f(dp[0] | (dp[1] << 8));
+#pragma unroll
         for (int j = 0; j < 16; j++) {
           uint32_t hi0 = ((qh >> j) & 1) << 4, hi1 = ((qh >> (j + 16)) & 1) << 4;
           ob[j] = __fmul_rn(d, (float)((int)((qs[j] & 0x0F) | hi0) - 16));
@@ -307,7 +312,7 @@ __global__ void k_dequant(uint32_t dt, const uint8_t* __restrict__ base, uint32_
   if (idx >= (uint64_t)rows * U) return;
   uint64_t r = idx / U;
   uint32_t u = (uint32_t)(idx % U);
-  dequant_unit(dt, base, total_rows, r0 + (uint32_t)r, cols, u, out + r * cols);
+  dequant_unit(dt, base, total_rows, r0 + (uint32_t)r, cols, u, out + r * cols + 64 * u);
 }
 
 void launch_dequant(const DevMat& m, uint32_t r0, uint32_t rows, float* out, cudaStream_t s) {
@@ -1276,7 +1281,7 @@ __global__ void k_embed(uint32_t dt, const uint8_t* __restrict__ base, uint32_t 
     // the host validates ids before they reach the device; this is a guard
     if (u == 0) st->error = 1;
   }
-  if (u < (cols + 63) / 64) dequant_unit(dt, base, vocab, tok < vocab ? tok : 0, cols, u, x);
+  if (u < (cols + 63) / 64) dequant_unit(dt, base, vocab, tok < vocab ? tok : 0, cols, u, x + 64 * u);
 }
 
 void launch_embed(const DevMat& emb, StepState* st, float* x, cudaStream_t s) {

@@ -44,22 +44,37 @@ __device__ __forceinline__ void split16(float v, __half* hi, __half* lo) {
   *lo = __float2half_rn(__fmul_rn(__fsub_rn(v, __half2float(h)), QG_LO));
 }
 
+__device__ __forceinline__ uint32_t half2_bits(__half a, __half b) {
+  return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+}
+
 // W (chunk-planar) rows -> hi/lo panels at rows row0.. of a panel matrix of
-// K = m.cols columns.  One thread per (row, 64-column unit).
+// K = m.cols columns.  One thread per (row, 64-column unit), rows fastest:
+// the 8 elements of a core-matrix row are one 16-byte store, and a warp's
+// 32 rows of one core-matrix column are 512 contiguous bytes.
 __global__ void k_wpanels(DevMat m, uint32_t row0, __half* __restrict__ hi, __half* __restrict__ lo) {
   const uint32_t U = m.cols / 64;
   const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (uint64_t)m.rows * U) return;
-  const uint32_t r = (uint32_t)(idx / U), u = (uint32_t)(idx % U);
+  const uint32_t u = (uint32_t)(idx / m.rows), r = (uint32_t)(idx % m.rows);
   float v[64];
-  dequant_unit(m.dtype, m.ptr, m.rows, r, m.cols, u, v - 64 * u);
-  const uint32_t R = row0 + r, panel = (R / QG_M) * U + u;
-  __half* ph = hi + (uint64_t)panel * (QG_M * QG_KB);
-  __half* pl = lo + (uint64_t)panel * (QG_M * QG_KB);
-#pragma unroll 8
-  for (uint32_t k = 0; k < 64; k++) {
-    const uint32_t e = panel_elem(QG_M, R % QG_M, k);
-    split16(v[k], ph + e, pl + e);
+  dequant_unit(m.dtype, m.ptr, m.rows, r, m.cols, u, v);
+  const uint32_t R = row0 + r;
+  const uint64_t pbase = ((uint64_t)(R / QG_M) * U + u) * (QG_M * QG_KB);
+#pragma unroll
+  for (uint32_t kc = 0; kc < 8; kc++) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (uint32_t i = 0; i < 4; i++) {
+      __half h0, l0, h1, l1;
+      split16(v[8 * kc + 2 * i], &h0, &l0);
+      split16(v[8 * kc + 2 * i + 1], &h1, &l1);
+      h[i] = half2_bits(h0, h1);
+      l[i] = half2_bits(l0, l1);
+    }
+    const uint64_t e = pbase + panel_elem(QG_M, R % QG_M, 8 * kc);
+    *reinterpret_cast<uint4*>(hi + e) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(lo + e) = make_uint4(l[0], l[1], l[2], l[3]);
   }
 }
 
@@ -404,5 +419,5 @@ __global__ void k_embed_rows(DevMat emb, const uint32_t* __restrict__ tokens, fl
   if (u >= U) return;
   const uint32_t tok = tokens[t];
   if (tok >= emb.rows) return;  // the host validates ids
-  dequant_unit(emb.dtype, emb.ptr, emb.rows, tok, emb.cols, u, x + (uint64_t)t * ld);
+  dequant_unit(emb.dtype, emb.ptr, emb.rows, tok, emb.cols, u, x + (uint64_t)t * ld + 64 * u);
 }
