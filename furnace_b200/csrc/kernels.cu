@@ -1656,12 +1656,13 @@ void launch_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, b
 void prefill_init() {
   CK(cudaFuncSetAttribute(k_qgemm, cudaFuncAttributeMaxDynamicSharedMemorySize, QG_SMEM));
   CK(cudaFuncSetAttribute(k_attn_prefill<128, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          attention_smem(128)));
-  CK(cudaFuncSetAttribute(k_attn_prefill<64, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, attention_smem(64)));
+                          (int)ap_smem<128, float>()));
+  CK(cudaFuncSetAttribute(k_attn_prefill<64, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          (int)ap_smem<64, float>()));
   CK(cudaFuncSetAttribute(k_attn_prefill<128, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          attention_smem(128, 2)));
+                          (int)ap_smem<128, __half>()));
   CK(cudaFuncSetAttribute(k_attn_prefill<64, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          attention_smem(64, 2)));
+                          (int)ap_smem<64, __half>()));
 }
 
 uint64_t wpanel_elems(uint32_t rows, uint32_t K) { return (uint64_t)((rows + QG_M - 1) / QG_M) * QG_M * K; }
@@ -1714,13 +1715,15 @@ static void prefill_attention_t(const float* qkv, uint32_t ldq, const float2* cs
                                 uint32_t T, uint32_t* err, cudaStream_t s) {
   k_kv_append<KT><<<dim3(T, nkv), 64, 0, s>>>(qkv, ldq, nh, nkv, hd, cs, kc, vc, max_ctx, pos0);
   CK(cudaGetLastError());
-  const size_t smem = attention_smem(hd, sizeof(KT));
+  const uint32_t G = nh / nkv;
+  if (G == 0 || G > AP_ROWS || nh % nkv) fail(FZ_EINVAL, "prefill attention: %u heads over %u KV heads", nh, nkv);
+  const dim3 grid((T + AP_ROWS / G - 1) / (AP_ROWS / G), nkv);
   if (hd == 128)
-    k_attn_prefill<128, KT><<<dim3(T, nkv), AT_THREADS, smem, s>>>(qkv, ldq, cs, kc, vc, ctx, ldc, nh, nkv, max_ctx,
-                                                                   pos0, err);
+    k_attn_prefill<128, KT><<<grid, AP_THREADS, ap_smem<128, KT>(), s>>>(qkv, ldq, cs, kc, vc, ctx, ldc, nh, nkv,
+                                                                        max_ctx, pos0, T, err);
   else
-    k_attn_prefill<64, KT><<<dim3(T, nkv), AT_THREADS, smem, s>>>(qkv, ldq, cs, kc, vc, ctx, ldc, nh, nkv, max_ctx,
-                                                                  pos0, err);
+    k_attn_prefill<64, KT><<<grid, AP_THREADS, ap_smem<64, KT>(), s>>>(qkv, ldq, cs, kc, vc, ctx, ldc, nh, nkv,
+                                                                      max_ctx, pos0, T, err);
   CK(cudaGetLastError());
 }
 

@@ -302,114 +302,234 @@ __global__ void k_kv_append(const float* __restrict__ qkv, uint32_t ldq, uint32_
   }
 }
 
-// Causal attention of prefill token t (position pos0 + t) over the cache
-// [0, pos0 + t] for the G query heads of KV head kvh (src/model.rs:371-438):
-// grid (T, n_kv), warp per head, 32-position tiles through bulk copies.
+// Causal attention of a prefill chunk (src/model.rs:371-438) on the CUDA
+// cores in f32.  One CTA per (block of QB = 64 / G consecutive tokens, KV
+// head): its query rows r = i * G + h (token t0 + i, query head kvh * G + h)
+// stream the cache positions [0, pos0 + t0 + QB) in tiles of 64 through
+// shared memory once per block, each row masked to its own causal limit.
+// Scores: each thread holds a 4-row x 8-position tile and walks the 128-bit
+// columns of q and k starting at its own rotation, so the eight rows a
+// quarter-warp reads fall in distinct banks.  Online softmax per row over the
+// eight threads of a row group (shuffles), probabilities through shared
+// memory, then P V with an 8-row x (HD / 16)-dimension tile per thread.
+constexpr uint32_t AP_ROWS = 64;     // query rows per CTA
+constexpr uint32_t AP_POS = 64;      // cache positions per tile
+constexpr uint32_t AP_PST = AP_POS + 4;  // row stride of the probability tile (floats)
+constexpr uint32_t AP_THREADS = 128;
+
+// Shared memory of k_attn_prefill: q rows, one K and one V tile, and the
+// probability tile, which reuses the K tile's space when it fits (the next K
+// tile is requested only once P V is done).
 template <int HD, typename KT>
-__global__ void __launch_bounds__(AT_THREADS) k_attn_prefill(const float* __restrict__ qkv, uint32_t ldq,
+__host__ __device__ constexpr bool ap_palias() {
+  return (size_t)AP_POS * HD * sizeof(KT) >= (size_t)AP_ROWS * AP_PST * 4;
+}
+template <int HD, typename KT>
+__host__ __device__ constexpr size_t ap_smem() {
+  return (size_t)AP_ROWS * HD * 4 + 2 * (size_t)AP_POS * HD * sizeof(KT) +
+         (ap_palias<HD, KT>() ? 0 : (size_t)AP_ROWS * AP_PST * 4) + 2 * AP_ROWS * 4;
+}
+
+template <int HD, typename KT>
+__global__ void __launch_bounds__(AP_THREADS) k_attn_prefill(const float* __restrict__ qkv, uint32_t ldq,
                                                               const float2* __restrict__ cs,
                                                               const KT* __restrict__ kc,
                                                               const KT* __restrict__ vc, float* __restrict__ ctx,
                                                               uint32_t ldc, uint32_t nh, uint32_t nkv,
-                                                              uint32_t max_ctx, uint32_t pos0, uint32_t* err) {
-  constexpr int DPL = HD / 32;
+                                                              uint32_t max_ctx, uint32_t pos0, uint32_t T,
+                                                              uint32_t* err) {
+  constexpr uint32_t C4 = HD / 4;       // 4-element columns of a row
   constexpr uint32_t EB = sizeof(KT);
+  constexpr uint32_t NC = HD / 64;      // P V: 4-element columns per thread (dg, dg + 16)
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ __align__(16) float qs[AT_MAXG][HD];
-  __shared__ __align__(8) uint64_t bar[AT_NBUF];
-  const uint32_t G = nh / nkv, t = blockIdx.x, kvh = blockIdx.y;
-  const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, half = HD / 2;
-  const uint32_t pos = pos0 + t, n = pos + 1, ntiles = (n + AT_TP - 1) / AT_TP;
-  KT* tiles = reinterpret_cast<KT*>(smem);
+  float* qsm = reinterpret_cast<float*>(smem);                         // [AP_ROWS][HD]
+  KT* ksm = reinterpret_cast<KT*>(smem + (size_t)AP_ROWS * HD * 4);    // [AP_POS][HD]
+  KT* vsm = ksm + AP_POS * HD;                                         // [AP_POS][HD]
+  uint8_t* after = reinterpret_cast<uint8_t*>(vsm + AP_POS * HD);
+  float* psm = ap_palias<HD, KT>() ? reinterpret_cast<float*>(ksm) : reinterpret_cast<float*>(after);
+  float* alpha_s = reinterpret_cast<float*>(after + (ap_palias<HD, KT>() ? 0 : (size_t)AP_ROWS * AP_PST * 4));
+  float* lfin = alpha_s + AP_ROWS;
+  __shared__ __align__(8) uint64_t kbar, vbar;
+
+  const uint32_t G = nh / nkv, QB = AP_ROWS / G, kvh = blockIdx.y;
+  const uint32_t blk = gridDim.x - 1 - blockIdx.x;  // longest blocks first
+  const uint32_t t0 = blk * QB, tq = min(QB, T - t0), R = tq * G;
+  const uint32_t nmax = pos0 + t0 + tq, ntiles = (nmax + AP_POS - 1) / AP_POS;
+  const uint32_t tid = threadIdx.x;
   const KT* kvk = kc + (uint64_t)kvh * max_ctx * HD;
   const KT* kvv = vc + (uint64_t)kvh * max_ctx * HD;
+  auto issue = [&](uint64_t* bar, KT* dst, const KT* src, uint32_t j) {
+    const uint32_t a = j * AP_POS, rows = min(nmax, a + AP_POS) - a;
+    mbar_expect_tx(bar, rows * HD * EB);
+    bulk_g2s(dst, src + (uint64_t)a * HD, rows * HD * EB, bar, 0ull);
+  };
   if (tid == 0) {
-    for (int b = 0; b < AT_NBUF; b++) mbar_init(&bar[b], 1);
+    mbar_init(&kbar, 1);
+    mbar_init(&vbar, 1);
     fence_barrier_init();
   }
-  const uint64_t pol = policy_evict_first();
-  auto issue = [&](uint32_t j) {
-    const uint32_t b = j % AT_NBUF, a = j * AT_TP, rows = min(n, a + AT_TP) - a;
-    KT* kt = tiles + (size_t)b * 2 * AT_TP * HD;
-    mbar_expect_tx(&bar[b], 2 * rows * HD * EB);
-    bulk_g2s(kt, kvk + (uint64_t)a * HD, rows * HD * EB, &bar[b], pol);
-    bulk_g2s(kt + AT_TP * HD, kvv + (uint64_t)a * HD, rows * HD * EB, &bar[b], pol);
-  };
   __syncthreads();
-  if (tid == 0)
-    for (uint32_t j = 0; j < ntiles && j < (uint32_t)AT_NBUF; j++) issue(j);
-  const float2* csp = cs + (uint64_t)pos * half;
-  for (uint32_t idx = tid; idx < G * half; idx += AT_THREADS) {
-    const uint32_t h = idx / half, i = idx % half;
-    const float* x = qkv + (uint64_t)t * ldq + (uint64_t)(kvh * G + h) * HD;
-    const float a = x[i], b = x[i + half];
-    const float2 c = csp[i];
-    qs[h][i] = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
-    qs[h][i + half] = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
+  if (tid == 0) {
+    issue(&kbar, ksm, kvk, 0);
+    issue(&vbar, vsm, kvv, 0);
+  }
+  // q rows with RoPE at each token's position (src/model.rs:193-217); rows
+  // past R are zero and never written out
+  constexpr uint32_t half = HD / 2;
+  for (uint32_t idx = tid; idx < AP_ROWS * half; idx += AP_THREADS) {
+    const uint32_t r = idx / half, i = idx % half;
+    float o0 = 0.f, o1 = 0.f;
+    if (r < R) {
+      const uint32_t t = t0 + r / G, h = r % G;
+      const float* x = qkv + (uint64_t)t * ldq + (uint64_t)(kvh * G + h) * HD;
+      const float xa = x[i], xb = x[i + half];
+      const float2 c = cs[(uint64_t)(pos0 + t) * half + i];
+      o0 = __fsub_rn(__fmul_rn(xa, c.x), __fmul_rn(xb, c.y));
+      o1 = __fadd_rn(__fmul_rn(xa, c.y), __fmul_rn(xb, c.x));
+    }
+    qsm[r * HD + i] = o0;
+    qsm[r * HD + i + half] = o1;
   }
   __syncthreads();
+
+  const uint32_t rg = tid >> 3, pg = tid & 7;   // scores: rows rg*4 + i, positions pg*8 + jj
+  const uint32_t rp = tid >> 4, dg = tid & 15;  // P V: rows rp + 8k, columns dg (+ 16)
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
-  float m = -INFINITY, l = 0.f, acc[DPL];
+  float m[4], l[4];
+  uint32_t lim[4];  // last position row rg*4 + i may attend to
 #pragma unroll
-  for (int d = 0; d < DPL; d++) acc[d] = 0.f;
+  for (int i = 0; i < 4; i++) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+    lim[i] = pos0 + t0 + min((rg * 4 + i) / G, tq - 1);
+  }
+  float4 o[8][NC];
+#pragma unroll
+  for (int k = 0; k < 8; k++)
+#pragma unroll
+    for (int c = 0; c < (int)NC; c++) o[k][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+
   bool ok = true;
   for (uint32_t j = 0; j < ntiles; j++) {
-    const uint32_t b = j % AT_NBUF, tn = min(n, j * AT_TP + AT_TP) - j * AT_TP;
-    const KT* kt = tiles + (size_t)b * 2 * AT_TP * HD;
-    const KT* vt = kt + AT_TP * HD;
-    if (!mbar_wait(&bar[b], (j / AT_NBUF) & 1)) {
+    const uint32_t a = j * AP_POS, tn = min(nmax, a + AP_POS) - a;
+    if (!mbar_wait(&kbar, j & 1)) {
       ok = false;
       break;
     }
-    if (warp < G) {
-      const uint32_t tt = lane;
-      float s = -INFINITY;
-      if (tt < tn) {
-        const KT* kr = kt + (size_t)tt * HD;
-        const float4* qr = reinterpret_cast<const float4*>(qs[warp]);
-        float dsum = 0.f;
-#pragma unroll 8
-        for (uint32_t c = 0; c < HD / 4; c++) {
-          const uint32_t cc = (c + tt) & (HD / 4 - 1);
-          const float4 k4 = kv_ld4(kr, cc), q4 = qr[cc];
-          dsum = fmaf(q4.x, k4.x, dsum);
-          dsum = fmaf(q4.y, k4.y, dsum);
-          dsum = fmaf(q4.z, k4.z, dsum);
-          dsum = fmaf(q4.w, k4.w, dsum);
+    float sc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int jj = 0; jj < 8; jj++) sc[i][jj] = 0.f;
+#pragma unroll 2
+    for (uint32_t c = 0; c < C4; c++) {
+      const uint32_t cc = (c + pg) & (C4 - 1);
+      float4 q4[4], k4[8];
+#pragma unroll
+      for (int i = 0; i < 4; i++) q4[i] = reinterpret_cast<const float4*>(qsm + (rg * 4 + i) * HD)[cc];
+#pragma unroll
+      for (int jj = 0; jj < 8; jj++) k4[jj] = kv_ld4(ksm + (pg * 8 + jj) * HD, cc);
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int jj = 0; jj < 8; jj++) {
+          sc[i][jj] = fmaf(q4[i].x, k4[jj].x, sc[i][jj]);
+          sc[i][jj] = fmaf(q4[i].y, k4[jj].y, sc[i][jj]);
+          sc[i][jj] = fmaf(q4[i].z, k4[jj].z, sc[i][jj]);
+          sc[i][jj] = fmaf(q4[i].w, k4[jj].w, sc[i][jj]);
         }
-        s = __fmul_rn(dsum, scale);
+    }
+    __syncthreads();  // K tile read by every thread (its space may now hold P)
+    // causal mask, scale and the online softmax of each row
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      float mt = -INFINITY;
+#pragma unroll
+      for (int jj = 0; jj < 8; jj++) {
+        const uint32_t pp = pg * 8 + jj;
+        sc[i][jj] = (pp < tn && a + pp <= lim[i]) ? __fmul_rn(sc[i][jj], scale) : -INFINITY;
+        mt = fmaxf(mt, sc[i][jj]);
       }
-      float mt = s;
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+      const float mn = fmaxf(m[i], mt);
+      const float al = expf(m[i] - mn);
+      float ps = 0.f;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
-      const float mn = fmaxf(m, mt);
-      const float alpha = expf(m - mn);
-      const float pr = tt < tn ? expf(s - mn) : 0.f;
-      float ps = pr;
+      for (int jj = 0; jj < 8; jj++) {
+        sc[i][jj] = expf(sc[i][jj] - mn);
+        ps += sc[i][jj];
+      }
+      ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+      l[i] = fmaf(l[i], al, ps);
+      m[i] = mn;
+      float4* pr = reinterpret_cast<float4*>(psm + (rg * 4 + i) * AP_PST + pg * 8);
+      pr[0] = make_float4(sc[i][0], sc[i][1], sc[i][2], sc[i][3]);
+      pr[1] = make_float4(sc[i][4], sc[i][5], sc[i][6], sc[i][7]);
+      if (pg == 0) alpha_s[rg * 4 + i] = al;
+    }
+    __syncthreads();  // P and the rescale factors are complete
+    if (!mbar_wait(&vbar, j & 1)) {
+      ok = false;
+      break;
+    }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-      l = fmaf(l, alpha, ps);
-      m = mn;
+    for (int k = 0; k < 8; k++) {
+      const float al = alpha_s[rp + 8 * k];
 #pragma unroll
-      for (int d = 0; d < DPL; d++) acc[d] *= alpha;
-      for (uint32_t t2 = 0; t2 < tn; t2++) {
-        const float pt = __shfl_sync(0xffffffffu, pr, t2);
-        const KT* vr = vt + (size_t)t2 * HD + lane * DPL;
-#pragma unroll
-        for (int d = 0; d < DPL; d++) acc[d] = fmaf(pt, kv_ld(vr + d), acc[d]);
+      for (int c = 0; c < (int)NC; c++) {
+        o[k][c].x *= al;
+        o[k][c].y *= al;
+        o[k][c].z *= al;
+        o[k][c].w *= al;
       }
     }
-    __syncthreads();  // buffer b free
-    if (tid == 0 && j + AT_NBUF < ntiles) issue(j + AT_NBUF);
+    for (uint32_t pp = 0; pp < tn; pp++) {
+      float4 v4[NC];
+#pragma unroll
+      for (int c = 0; c < (int)NC; c++) v4[c] = kv_ld4(vsm + pp * HD, dg + 16 * c);
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const float pv = psm[(rp + 8 * k) * AP_PST + pp];
+#pragma unroll
+        for (int c = 0; c < (int)NC; c++) {
+          o[k][c].x = fmaf(pv, v4[c].x, o[k][c].x);
+          o[k][c].y = fmaf(pv, v4[c].y, o[k][c].y);
+          o[k][c].z = fmaf(pv, v4[c].z, o[k][c].z);
+          o[k][c].w = fmaf(pv, v4[c].w, o[k][c].w);
+        }
+      }
+    }
+    __syncthreads();  // P and the V tile consumed
+    if (tid == 0 && j + 1 < ntiles) {
+      // the bulk copies overwrite what this CTA's threads wrote (P) and read
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(&kbar, ksm, kvk, j + 1);
+      issue(&vbar, vsm, kvv, j + 1);
+    }
   }
   if (!ok) {
     if (tid == 0) atomicExch(err, 2u);
     return;
   }
-  if (warp < G) {
-    float* o = ctx + (uint64_t)t * ldc + (uint64_t)(kvh * G + warp) * HD + lane * DPL;
+  if (pg == 0)
 #pragma unroll
-    for (int d = 0; d < DPL; d++) o[d] = __fdiv_rn(acc[d], l);
+    for (int i = 0; i < 4; i++) lfin[rg * 4 + i] = l[i];
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const uint32_t r = rp + 8 * k;
+    if (r < R) {
+      const float lr = lfin[r];
+      float4* out = reinterpret_cast<float4*>(ctx + (uint64_t)(t0 + r / G) * ldc + (uint64_t)(kvh * G + r % G) * HD);
+#pragma unroll
+      for (int c = 0; c < (int)NC; c++)
+        out[dg + 16 * c] = make_float4(__fdiv_rn(o[k][c].x, lr), __fdiv_rn(o[k][c].y, lr), __fdiv_rn(o[k][c].z, lr),
+                                       __fdiv_rn(o[k][c].w, lr));
+    }
   }
 }
 

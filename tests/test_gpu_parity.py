@@ -188,6 +188,33 @@ def test_forward_and_kv_cache_match_oracle(tiny):
     _check_logits(got, want, "decode")
 
 
+@pytest.mark.parametrize("kv_dtype", [0, 1], ids=["f32", "f16"])
+@pytest.mark.parametrize("over", [{}, {"hidden": 1792, "n_heads": 14, "n_kv_heads": 2}], ids=["hd64-g4", "hd128-g7"])
+def test_long_prefill_at_offset_matches_oracle(tmp_path, over, kv_dtype):
+    """Two batched prefills into one cache: 150 tokens from position 0, then
+    90 more from position 150.  The causal attention streams several
+    64-position tiles per query block, the last query block of each call is
+    partial, and the second call's rows start mid-cache.  Logits of both
+    calls and every cached row against the oracle (f16 rows within one
+    binary16 step of the largest element, as above).  Head sizes 64 and 128,
+    4 and 7 query heads per KV head (16 and 9 tokens per query block)."""
+    f, dev, ref = _models(synth.write(synth.spec("tiny", **over), str(tmp_path / "m.gguf")))
+    kd, kr = fz.KvCache(dev, 256, kv_dtype), ref.kv_new(256, kv_dtype=kv_dtype)
+    n = 0
+    for count, seed in ((150, 31), (90, 32)):
+        ids = synth.prompt_ids(ref.vocab, count, seed=seed)
+        got, am = dev.forward(ids, kd)
+        want = ref.forward_cached(ids, kr)
+        _check_logits(got, want, f"prefill of {count} at {n}")
+        assert am == int(np.argmax(want))
+        n += count
+    tol = 2.0 ** -10 if kv_dtype else 1e-4
+    for layer in range(ref.n_layers):
+        for which in (0, 1):
+            a, b = kd.read(layer, which, n), kr.read(layer, which, n)
+            assert np.abs(a - b).max() <= tol * max(1.0, np.abs(b).max()), (layer, which)
+
+
 def test_forward_last_matches_oracle_uncached(tiny):
     """Model::forward_last, the reference's --no-cache path, against the
     oracle's full recompute (src/model.rs:569-575, :294-315): short prompts
