@@ -1679,7 +1679,9 @@ void launch_wpanels(const DevMat& m, uint32_t row0, void* hi, void* lo, cudaStre
 void launch_xpanels(const float* x, uint32_t ld, uint32_t T, uint32_t K, const float* w, float eps, void* hi,
                     void* lo, cudaStream_t s) {
   if (K % 64) fail(FZ_EINVAL, "prefill: width %u not a multiple of 64", K);
-  k_xpanels<<<T, 256, 0, s>>>(x, ld, K, w, eps, reinterpret_cast<__half*>(hi), reinterpret_cast<__half*>(lo));
+  if (ld % 4) fail(FZ_EINVAL, "prefill: row stride %u not a multiple of 4", ld);
+  k_xpanels<<<(T + XP_TOK - 1) / XP_TOK, 256, 0, s>>>(x, ld, T, K, w, eps, reinterpret_cast<__half*>(hi),
+                                                      reinterpret_cast<__half*>(lo));
   CK(cudaGetLastError());
 }
 
@@ -1698,7 +1700,8 @@ void launch_qgemm(const QgemmLaunch& q, cudaStream_t s) {
   p.ld = q.ld;
   p.bias = q.bias;
   p.err = q.err;
-  dim3 grid((q.N + QG_M - 1) / QG_M, (q.T + QG_N - 1) / QG_N);
+  dim3 grid((q.T + QG_N - 1) / QG_N, (q.N + QG_M - 1) / QG_M);
+  if (grid.y > 65535) fail(FZ_EINVAL, "prefill gemm: %u output rows", q.N);
   k_qgemm<<<grid, 128, QG_SMEM, s>>>(p);
   CK(cudaGetLastError());
 }

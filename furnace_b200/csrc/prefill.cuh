@@ -80,35 +80,53 @@ __global__ void k_wpanels(DevMat m, uint32_t row0, __half* __restrict__ hi, __ha
 
 // X [T, K] f32 (row stride ld) -> hi/lo token panels (P = QG_N), optionally
 // RMS-normalised per row with weight w (src/tensor.rs:164-186).  One block
-// per token; tokens T.. up to the panel padding are never written (zeroed
-// once at allocation).
-__global__ void k_xpanels(const float* __restrict__ x, uint32_t ld, uint32_t K, const float* __restrict__ w,
-                          float eps, __half* __restrict__ hi, __half* __restrict__ lo) {
-  const uint32_t t = blockIdx.x, tid = threadIdx.x;
-  const float* row = x + (uint64_t)t * ld;
-  __shared__ float red[32];
-  float inv = 1.f;
+// per 8 tokens (the 8 rows of a core matrix): warp i reduces token i's sum of
+// squares, then each thread converts 8 columns of one token into one 16-byte
+// store per panel, the block's 8 tokens of a column group being 128
+// contiguous bytes.  Tokens T.. up to the panel padding are never written
+// (zeroed once at allocation).
+constexpr uint32_t XP_TOK = 8;
+__global__ void __launch_bounds__(256) k_xpanels(const float* __restrict__ x, uint32_t ld, uint32_t T, uint32_t K,
+                                                 const float* __restrict__ w, float eps, __half* __restrict__ hi,
+                                                 __half* __restrict__ lo) {
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, tb0 = blockIdx.x * XP_TOK;
+  __shared__ float inv_s[XP_TOK];
   if (w) {
+    const uint32_t t = tb0 + warp;
     float ss = 0.f;
-    for (uint32_t k = tid; k < K; k += blockDim.x) ss = fmaf(row[k], row[k], ss);
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
-    __syncthreads();
-    if (tid < 32) {
-      float s2 = tid < blockDim.x / 32 ? red[tid] : 0.f;
-      for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-      if (tid == 0) red[0] = s2;
+    if (t < T) {
+      const float* row = x + (uint64_t)t * ld;
+      for (uint32_t k = lane; k < K; k += 32) ss = fmaf(row[k], row[k], ss);
     }
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) inv_s[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
     __syncthreads();
-    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], (float)K), eps)));
   }
-  const uint32_t U = K / 64;
-  for (uint32_t k = tid; k < K; k += blockDim.x) {
-    float v = row[k];
-    if (w) v = __fmul_rn(__fmul_rn(v, inv), w[k]);
-    const uint64_t panel = (uint64_t)(t / QG_N) * U + k / 64;
-    const uint64_t e = panel * (QG_N * QG_KB) + panel_elem(QG_N, t % QG_N, k % 64);
-    split16(v, hi + e, lo + e);
+  const uint32_t U = K / 64, nk8 = K / 8;
+  for (uint32_t idx = tid; idx < nk8 * XP_TOK; idx += blockDim.x) {
+    const uint32_t i = idx % XP_TOK, k0 = (idx / XP_TOK) * 8, t = tb0 + i;
+    if (t >= T) continue;
+    const float4* src = reinterpret_cast<const float4*>(x + (uint64_t)t * ld + k0);
+    const float4 a = src[0], b = src[1];
+    float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    if (w) {
+      const float inv = inv_s[i];
+#pragma unroll
+      for (int j = 0; j < 8; j++) v[j] = __fmul_rn(__fmul_rn(v[j], inv), w[k0 + j]);
+    }
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      __half h0, l0, h1, l1;
+      split16(v[2 * j], &h0, &l0);
+      split16(v[2 * j + 1], &h1, &l1);
+      h[j] = half2_bits(h0, h1);
+      l[j] = half2_bits(l0, l1);
+    }
+    const uint64_t panel = (uint64_t)(t / QG_N) * U + k0 / 64;
+    const uint64_t e = panel * (QG_N * QG_KB) + panel_elem(QG_N, t % QG_N, k0 % 64);
+    *reinterpret_cast<uint4*>(hi + e) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(lo + e) = make_uint4(l[0], l[1], l[2], l[3]);
   }
 }
 
@@ -174,7 +192,9 @@ __global__ void __launch_bounds__(128, 1) k_qgemm(const __grid_constant__ QgPara
   __shared__ uint32_t tmem_base;
   __shared__ volatile uint32_t fail;
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rb = blockIdx.x, tb = blockIdx.y, KB = p.K / QG_KB;
+  // token tiles fastest: the CTAs that share a weight panel run together and
+  // read it from DRAM once between them
+  const uint32_t rb = blockIdx.y, tb = blockIdx.x, KB = p.K / QG_KB;
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < QG_STAGES; s++) {
       mbar_init(&full[s], 1);
