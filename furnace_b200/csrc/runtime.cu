@@ -107,6 +107,9 @@ struct fz_model {
   uint32_t pf_cap = 0;
   DevBuf pf_x, pf_qkv, pf_ctx, pf_h, pf_tok, pf_err, pf_wh, pf_wl, pf_xh, pf_xl;
   DevBuf smp_scratch, smp_out;  // device top-k of the sampler
+  // the caches made for this model: fz_model_free releases their device
+  // memory and detaches them, so they may be freed before or after it
+  std::vector<fz_kv*> caches;
 };
 
 struct fz_kv {
@@ -122,10 +125,14 @@ struct fz_kv {
   }
   DevBuf k, v, rope_cs, partials, state, forced, ids;
   cudaGraphExec_t g_full = nullptr, g_layers = nullptr;
-  ~fz_kv() {
+  // device memory and graphs back; the handle stays valid for fz_kv_free
+  void release() {
     if (g_full) cudaGraphExecDestroy(g_full);
     if (g_layers) cudaGraphExecDestroy(g_layers);
+    g_full = g_layers = nullptr;
+    for (DevBuf* b : {&k, &v, &rope_cs, &partials, &state, &forced, &ids}) b->release();
   }
+  ~fz_kv() { release(); }
 };
 
 struct fz_weight {
@@ -1123,6 +1130,10 @@ void fz_model_free(fz_model* m) {
     cudaStreamSynchronize(m->stream);
     cudaStreamDestroy(m->stream);
   }
+  for (fz_kv* kv : m->caches) {
+    kv->release();
+    kv->m = nullptr;
+  }
   if (m->ar_p2p)
     for (int q = 0; q < m->world; q++)
       if (q != m->rank && m->ar_peers.buf[q]) cudaIpcCloseMemHandle(m->ar_peers.buf[q]);
@@ -1212,14 +1223,18 @@ int fz_kv_new(fz_model* m, uint32_t max_ctx, int kv_dtype, fz_kv** out) {
     CK(cudaMemset(kv->state.p, 0, sizeof(StepState)));
     kv->forced.alloc((uint64_t)max_ctx * 4 + 16);
     kv->ids.alloc((uint64_t)max_ctx * 4 + 16);
+    m->caches.push_back(kv.get());
     *out = kv.release();
   });
 }
 
 void fz_kv_free(fz_kv* kv) {
   if (!kv) return;
-  cudaSetDevice(kv->m->device);
-  cudaStreamSynchronize(kv->m->stream);
+  if (fz_model* m = kv->m) {  // else its model was freed first and took the device memory back
+    cudaSetDevice(m->device);
+    cudaStreamSynchronize(m->stream);
+    m->caches.erase(std::remove(m->caches.begin(), m->caches.end(), kv), m->caches.end());
+  }
   delete kv;
 }
 
@@ -1233,6 +1248,7 @@ int fz_kv_len(const fz_kv* kv, uint32_t* len) {
 int fz_kv_set_len(fz_kv* kv, uint32_t len) {
   return guard([&] {
     need(kv != nullptr, "null kv");
+    need(kv->m != nullptr, "the cache's model has been freed");
     need(len <= kv->max_ctx, "kv len %u > max_ctx %u", len, kv->max_ctx);
     kv->len = len;
   });
@@ -1241,6 +1257,7 @@ int fz_kv_set_len(fz_kv* kv, uint32_t len) {
 int fz_kv_read(const fz_kv* kv, uint32_t layer, int which_v, uint32_t n, float* out) {
   return guard([&] {
     need(kv && out, "null argument");
+    need(kv->m != nullptr, "the cache's model has been freed");
     const fz_config& c = kv->m->cfg;
     need(layer < c.n_layers && n <= kv->max_ctx, "kv read out of range");
     use_device(kv->m);

@@ -146,6 +146,9 @@ int fz_model_load_tp(const fz_file* f, int rank, int world, const void* id, size
 /* KvCache::new (src/model.rs:330-339): max_ctx positions of kv_dtype
  * (FZ_KV_F32 or FZ_KV_F16) elements. */
 int fz_kv_new(fz_model* m, uint32_t max_ctx, int kv_dtype, fz_kv** out);
+/* Either order of fz_kv_free and fz_model_free is safe: freeing the model
+ * releases its caches' device memory, and a cache handle of a freed model
+ * then accepts only fz_kv_free and fz_kv_len (the rest return FZ_EINVAL). */
 void fz_kv_free(fz_kv* kv);
 /* KvCache::len (src/model.rs:324).  set_len rewinds (or restores) the
  * filled length; positions >= len are overwritten by later forwards. */

@@ -266,6 +266,25 @@ def test_f16_kv_cache_matches_oracle(tiny):
     assert e.value.code == fz.FZ_EINVAL
 
 
+def test_cache_outlives_its_model(tiny, orc):
+    """fz_model_free before fz_kv_free (the order a garbage collector may
+    pick): the model takes the cache's device memory back, the cache handle
+    rejects use, freeing it afterwards is safe, and no CUDA error is left
+    pending for the next call."""
+    f, dev, ref = _models(tiny)
+    kd = fz.KvCache(dev, 32)
+    dev.forward(synth.prompt_ids(ref.vocab, 5, seed=4), kd)
+    dev.close()
+    with pytest.raises(fz.FurnaceError) as e:
+        kd.read(0, False, 5)
+    assert e.value.code == fz.FZ_EINVAL
+    assert kd.len == 5
+    kd.close()
+    raw = synth.random_tensor(4, 256, 12, seed=5)
+    assert np.array_equal(fz.quant.dequantize(12, raw, 1024).view(np.uint32),
+                          orc.dequantize(12, raw, 1024).view(np.uint32))
+
+
 def test_forward_rejects_bad_input(tiny):
     f, dev, _ = _models(tiny)
     kv = fz.KvCache(dev, 8)
