@@ -1,7 +1,7 @@
 """Benchmark: batch-1 greedy decode tokens/s (and achieved HBM GB/s) of the
-furnace decode loop on B200, BASELINE.json's metric.
+furnace decode loop on B200.
 
-Workload (N=1): configs[2], the Qwen2.5-7B shape in the Q4_K_M mix
+Workload (N=1): configuration C3, the Qwen2.5-7B shape in the Q4_K_M mix
 (synthetic seeded weights, same shapes/dtypes), 2048 random prompt ids
 prefilled, then greedy decode at positions 2048.. .  A "step" is STEP_TOKENS
 (16) decode tokens; --steps K times K steps (default 32 -> the config's 512

@@ -50,7 +50,7 @@ class Spec:
         return self.hidden // self.n_heads
 
     def dtype(self, kind: str, layer: int) -> int:
-        """Quantization mix per configuration."""
+        """Quantization mix per configuration (the benchmark configurations C1-C5)."""
         if self.mix == "q8_0":
             return Q8_0
         if self.mix == "q4_k_m":
@@ -81,7 +81,7 @@ class Spec:
 
 
 CONFIGS = {
-    # BASELINE.json configs[0..4]
+    # the benchmark configurations C1-C5 (Qwen2.5 0.5B, 1.5B, 7B, 32B, 72B shapes)
     "c1": Spec("qwen2.5-0.5b-q8_0", 896, 24, 14, 2, 4864, 151936, True, 4096, "q8_0"),
     "c2": Spec("qwen2.5-1.5b-q4_k_m", 1536, 28, 12, 2, 8960, 151936, True, 4096, "q4_k_m"),
     "c3": Spec("qwen2.5-7b-q4_k_m", 3584, 28, 28, 4, 18944, 152064, False, 4096, "q4_k_m"),

@@ -1,6 +1,6 @@
 """CUDA path vs the CPU oracle, through the C ABI (libfurnace_cuda.so).
 
-Bars (BASELINE north star):
+Bars:
   * dequantized blocks bit-exact;
   * GEMV outputs within 1e-4 relative error: max|gpu - oracle| <= 1e-4 * max|oracle|;
   * logits within 1e-3 max-abs, argmax and top-5 identical at every step;
@@ -348,15 +348,15 @@ def test_sampled_generate_matches_oracle(tiny, temp, top_k, top_p, pen):
 
 @pytest.mark.slow
 def test_greedy_128_steps_c1():
-    """Qwen2.5-0.5B shape, Q8_0, 32-token prompt, 128 greedy steps."""
+    """C1: Qwen2.5-0.5B shape, Q8_0, 32-token prompt, 128 greedy steps."""
     _greedy_parity(synth.ensure("c1"), 32, 128)
 
 
 @pytest.mark.slow
 @pytest.mark.parametrize("name", ["c4", "c5"])
 def test_greedy_truncated_c4_c5(name):
-    """configs[3] (Q5_0 attention, Q6_K FFN and output, 40/8 heads, hidden
-    5120) and configs[4] (Q4_K_M mix with Q5_0/Q8_0 ffn_down fallbacks,
+    """C4 (Q5_0 attention, Q6_K FFN and output, 40/8 heads, hidden
+    5120) and C5 (Q4_K_M mix with Q5_0/Q8_0 ffn_down fallbacks,
     hidden 8192), truncated to 2 layers so the CPU oracle stays fast: a
     40-token prompt (batched prefill) and 32 greedy steps."""
     _greedy_parity(synth.ensure(name, n_layers=2), 40, 32)
@@ -364,5 +364,5 @@ def test_greedy_truncated_c4_c5(name):
 
 @pytest.mark.slow
 def test_greedy_128_steps_c2():
-    """Qwen2.5-1.5B shape, Q4_K_M mix, 128-token prompt, 128 steps."""
+    """C2: Qwen2.5-1.5B shape, Q4_K_M mix, 128-token prompt, 128 steps."""
     _greedy_parity(synth.ensure("c2"), 128, 128)

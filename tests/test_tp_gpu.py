@@ -131,7 +131,7 @@ def test_tp2_greedy_tiny(tmp_path):
 
 @pytest.mark.slow
 def test_tp2_greedy_c1():
-    """configs[0] (Q8_0, 14 heads / 2 KV heads) split over 2 GPUs, 128 steps."""
+    """C1 (Q8_0, 14 heads / 2 KV heads) split over 2 GPUs, 128 steps."""
     _run_tp(synth.ensure("c1"), 32, 128)
 
 
