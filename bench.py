@@ -268,7 +268,10 @@ def run_reference(args, dist):
             "warmup": args.warmup, "ms_per_step": dt * 1000 / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": f"{spec.name} batch-1 greedy decode (CPU sample)", "context": "8+"},
+            "config": {"workload": f"{spec.name}: greedy decode tokens (batch 1), a CPU sample at context "
+                                   f"8-{8 + args.warmup + args.steps} of the {args.prefill}-token-prefill workload",
+                       "model": spec.name, "global_batch": 1, "seq_len": 8 + args.warmup + args.steps,
+                       "parallelism": f"cpu{cores}"},
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
