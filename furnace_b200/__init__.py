@@ -32,7 +32,7 @@ F32, F16, Q5_0, Q8_0, Q4_K, Q6_K = 0, 1, 6, 8, 12, 14
 BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q5_0: (32, 22), Q4_K: (256, 144), Q6_K: (256, 210)}
 TYPE_NAMES = {F32: "F32", F16: "F16", Q5_0: "Q5_0", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
 
-FZ_OK, FZ_EINVAL, FZ_EFORMAT, FZ_EIO, FZ_ECUDA, FZ_ENOMEM, FZ_ETIMEOUT = range(7)
+FZ_OK, FZ_EINVAL, FZ_EFORMAT, FZ_EIO, FZ_ECUDA, FZ_ENOMEM, FZ_ETIMEOUT, FZ_ESPACE = range(8)
 FZ_KV_F32, FZ_KV_F16 = 0, 1  # KV cache element types
 
 # Every symbol include/furnace.h declares.
@@ -44,6 +44,9 @@ EXPORTS = [
     "fz_weight_upload", "fz_weight_free", "fz_matmul_quant_dev", "fz_step_profile", "fz_model_stream",
     "fz_dequant_dev_noalloc", "fz_tp_slice_of", "fz_tp_unique_id", "fz_model_load_tp",
     "fz_sampler_new", "fz_sampler_free", "fz_sampler_draws", "fz_sample_logits", "fz_sample", "fz_generate",
+    "fz_tokenizer_from_gguf", "fz_tokenizer_new", "fz_tokenizer_free", "fz_tokenizer_vocab_size",
+    "fz_tokenizer_encode", "fz_tokenizer_decode", "fz_tokenizer_token_bytes", "fz_pretokenize", "fz_chat_template",
+    "fz_utf8_stream_new", "fz_utf8_stream_free", "fz_utf8_stream_push", "fz_utf8_stream_flush",
 ]
 
 OPS = ["embed", "qkv", "rope_append", "attention", "o_proj", "gate_up", "down", "lm_head", "finalize"]
@@ -135,6 +138,19 @@ def load_library(build_if_missing: bool = True):
         "fz_generate": (I, [P, P, P, u32p, U32, U32, u32p, U32, u32p, u32p]),
         "fz_model_stream": (I, [P, pp, C.POINTER(I)]),
         "fz_step_profile": (I, [P, P, U32, U32, C.POINTER(C.c_double), C.POINTER(C.c_double), u32p]),
+        "fz_tokenizer_from_gguf": (I, [P, pp]),
+        "fz_tokenizer_new": (I, [C.POINTER(C.c_char_p), C.POINTER(C.c_int64), S, C.POINTER(C.c_char_p), S, pp]),
+        "fz_tokenizer_free": (None, [P]),
+        "fz_tokenizer_vocab_size": (I, [P, C.POINTER(S)]),
+        "fz_tokenizer_encode": (I, [P, C.c_char_p, S, u32p, S, C.POINTER(S)]),
+        "fz_tokenizer_decode": (I, [P, u32p, S, C.c_char_p, S, C.POINTER(S)]),
+        "fz_tokenizer_token_bytes": (I, [P, U32, C.c_char_p, S, C.POINTER(S)]),
+        "fz_pretokenize": (I, [C.c_char_p, S, C.POINTER(S), S, C.POINTER(S)]),
+        "fz_chat_template": (I, [C.c_char_p, S, C.c_char_p, S, C.POINTER(S)]),
+        "fz_utf8_stream_new": (I, [pp]),
+        "fz_utf8_stream_free": (None, [P]),
+        "fz_utf8_stream_push": (I, [P, C.c_char_p, S, C.c_char_p, S, C.POINTER(S)]),
+        "fz_utf8_stream_flush": (I, [P, C.c_char_p, S, C.POINTER(S)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -534,3 +550,140 @@ def tp_slice(config: "Config", rank: int, world: int) -> dict:
     _check(load_library().fz_tp_slice_of(C.byref(c), rank, world, C.byref(out)))
     return {n: getattr(out, n) for n, _ in _TpSlice._fields_}
 
+
+
+# ---------------------------------------------------------------------------
+# tokenizer (src/tokenizer.rs) and text helpers (src/generate.rs), host side
+# ---------------------------------------------------------------------------
+def _grow(call, make, cap):
+    """Run call(buffer, cap, count_ptr) and retry once with the reported size
+    on FZ_ESPACE; returns (buffer, count)."""
+    n = C.c_size_t()
+    buf = make(cap)
+    rc = call(buf, cap, C.byref(n))
+    if rc == FZ_ESPACE:
+        cap = n.value
+        buf = make(cap)
+        rc = call(buf, cap, C.byref(n))
+    _check(rc)
+    return buf, n.value
+
+
+def _bytes_out(call, cap=256) -> bytes:
+    buf, n = _grow(call, lambda k: C.create_string_buffer(max(k, 1)), cap)
+    return buf.raw[:n]
+
+
+class Tokenizer:
+    """Byte-level BPE with the qwen2 pre-tokenizer (src/tokenizer.rs)."""
+
+    def __init__(self, handle):
+        self._h = handle
+
+    @classmethod
+    def from_gguf(cls, f: GgufFile) -> "Tokenizer":
+        """Tokenizer::from_gguf (src/tokenizer.rs:67-90)."""
+        h = C.c_void_p()
+        _check(load_library().fz_tokenizer_from_gguf(f._h, C.byref(h)))
+        return cls(h)
+
+    @classmethod
+    def new(cls, tokens, token_types, merges) -> "Tokenizer":
+        """Tokenizer::new (src/tokenizer.rs:92-138): token strings, gguf
+        token types, "left right" merges in rank order."""
+        if len(token_types) != len(tokens):
+            raise FurnaceError(FZ_EINVAL, f"{len(tokens)} tokens but {len(token_types)} token types")
+        tb = [t.encode() for t in tokens]
+        mb = [m.encode() for m in merges]
+        ta = (C.c_char_p * max(len(tb), 1))(*tb)
+        ty = (C.c_int64 * max(len(tb), 1))(*[int(x) for x in token_types])
+        ma = (C.c_char_p * max(len(mb), 1))(*mb)
+        h = C.c_void_p()
+        _check(load_library().fz_tokenizer_new(ta, ty, len(tb), ma, len(mb), C.byref(h)))
+        return cls(h)
+
+    def close(self):
+        if self._h:
+            load_library().fz_tokenizer_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __len__(self) -> int:
+        n = C.c_size_t()
+        _check(load_library().fz_tokenizer_vocab_size(self._h, C.byref(n)))
+        return n.value
+
+    def encode(self, text: str) -> list[int]:
+        """Tokenizer::encode (src/tokenizer.rs:140-149)."""
+        b = text.encode()
+        L = load_library()
+        buf, n = _grow(lambda buf, cap, np_: L.fz_tokenizer_encode(self._h, b, len(b), buf, cap, np_),
+                       lambda k: (C.c_uint32 * max(k, 1))(), len(b) + 8)
+        return list(buf[:n])
+
+    def decode(self, ids) -> str:
+        """Tokenizer::decode (src/tokenizer.rs:151-157), lossy UTF-8."""
+        a = np.ascontiguousarray(ids, dtype=np.uint32).reshape(-1)
+        L = load_library()
+        out = _bytes_out(lambda buf, cap, np_: L.fz_tokenizer_decode(self._h, _u32p(a), a.size, buf, cap, np_),
+                         4 * a.size + 16)
+        return out.decode()
+
+    def token_bytes(self, token_id: int) -> bytes:
+        """Tokenizer::token_bytes (src/tokenizer.rs:159-181)."""
+        L = load_library()
+        return _bytes_out(lambda buf, cap, np_: L.fz_tokenizer_token_bytes(self._h, token_id, buf, cap, np_), 64)
+
+
+def pretokenize(text: str) -> list[str]:
+    """The qwen2 pre-tokenizer split alone (src/tokenizer.rs:16, 215-232)."""
+    b = text.encode()
+    L = load_library()
+    buf, n = _grow(lambda buf, cap, np_: L.fz_pretokenize(b, len(b), buf, cap, np_),
+                   lambda k: (C.c_size_t * max(k, 1))(), len(b) + 1)
+    out, start = [], 0
+    for end in buf[:n]:
+        out.append(b[start:end].decode())
+        start = end
+    return out
+
+
+def chat_template(prompt: str) -> str:
+    """chat_template (src/generate.rs:13-21)."""
+    b = prompt.encode()
+    L = load_library()
+    return _bytes_out(lambda buf, cap, np_: L.fz_chat_template(b, len(b), buf, cap, np_), len(b) + 256).decode()
+
+
+class Utf8Stream:
+    """Utf8Stream (src/generate.rs:24-66): printable prefixes of a byte stream."""
+
+    def __init__(self):
+        h = C.c_void_p()
+        _check(load_library().fz_utf8_stream_new(C.byref(h)))
+        self._h = h
+
+    def push(self, data: bytes) -> str:
+        L = load_library()
+        return _bytes_out(lambda buf, cap, np_: L.fz_utf8_stream_push(self._h, data, len(data), buf, cap, np_),
+                          len(data) + 16).decode()
+
+    def flush(self) -> str:
+        L = load_library()
+        return _bytes_out(lambda buf, cap, np_: L.fz_utf8_stream_flush(self._h, buf, cap, np_), 64).decode()
+
+    def close(self):
+        if self._h:
+            load_library().fz_utf8_stream_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

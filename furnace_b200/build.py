@@ -17,7 +17,7 @@ LIB = os.path.join(OUT, "libfurnace_cuda.so")
 SYNTH = os.path.join(OUT, "libfzsynth.so")
 
 CUDA_SOURCES = ["kernels.cu", "runtime.cu", "noalloc.cu"]
-CXX_SOURCES = ["gguf.cpp", "nccl_dyn.cpp"]
+CXX_SOURCES = ["gguf.cpp", "nccl_dyn.cpp", "tokenizer.cpp"]
 HEADERS = sorted(f for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))) + [os.path.join("..", "..", "include", "furnace.h")]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -48,6 +48,7 @@ struct MetaValue {
   std::string s;
   size_t array_len = 0;
   uint32_t array_tag = 0;
+  size_t array_pos = 0;  // file offset of the first element
 };
 
 struct TensorEntry {
@@ -85,7 +86,14 @@ struct GgufFile {
   float meta_f32(const std::string& k) const;
   const std::string& meta_str(const std::string& k) const;
   size_t meta_array_len(const std::string& k) const;
+  // GgufFile::meta_array elements as strings / integers (GgufValue::as_str,
+  // as_i64, src/gguf.rs:136-163); fails on an element of another type
+  std::vector<std::string> meta_str_array(const std::string& k) const;
+  std::vector<int64_t> meta_int_array(const std::string& k) const;
 };
+
+// Whether [p, p + n) is well-formed UTF-8 (what Rust's String::from_utf8 accepts).
+bool utf8_valid(const uint8_t* p, size_t n);
 
 std::unique_ptr<GgufFile> open_gguf(const char* path);
 std::unique_ptr<GgufFile> open_gguf_bytes(const void* data, size_t n);

@@ -2,9 +2,10 @@
 // parser (src/gguf.rs:315-363): magic "GGUF", version 2 or 3, every read
 // bounds-checked, tensor dims <= 4, known ggml type ids, alignment from
 // general.alignment (default 32, power of two), data start rounded up to it,
-// and tensor data bounds checked at lookup (src/gguf.rs:412-434).  Metadata
-// arrays are validated and skipped (only their length is kept): the
-// tokenizer tables are host-side text work outside the decode path.
+// and tensor data bounds checked at lookup (src/gguf.rs:412-434), strings
+// well-formed UTF-8 (src/gguf.rs:71-75).  Metadata arrays are validated and
+// skipped at parse time; their length and the offset of their first element
+// are kept, and the tokenizer reads its tables from there.
 
 #include <cstdarg>
 #include <cstdio>
@@ -52,6 +53,7 @@ struct Reader {
     uint64_t len = get<uint64_t>();
     if (len > n - pos) fail(FZ_EFORMAT, "unexpected EOF: need %llu bytes at offset %zu", (unsigned long long)len, pos);
     const uint8_t* s = take((size_t)len);
+    if (!utf8_valid(s, (size_t)len)) fail(FZ_EFORMAT, "string is not valid UTF-8");
     return std::string((const char*)s, (size_t)len);
   }
 };
@@ -79,6 +81,7 @@ void read_value(Reader& r, uint32_t tag, MetaValue* v, int depth) {
       uint64_t cnt = r.get<uint64_t>();
       v->array_tag = et;
       v->array_len = (size_t)cnt;
+      v->array_pos = r.pos;
       if (depth > 8) fail(FZ_EFORMAT, "metadata arrays nested too deeply");
       size_t ss = scalar_size(et);
       if (ss) {
@@ -189,6 +192,71 @@ size_t GgufFile::meta_array_len(const std::string& k) const {
   auto it = meta.find(k);
   if (it != meta.end() && it->second.tag == 9) return it->second.array_len;
   fail(FZ_EFORMAT, "metadata key '%s' missing or not an array", k.c_str());
+}
+
+std::vector<std::string> GgufFile::meta_str_array(const std::string& k) const {
+  auto it = meta.find(k);
+  if (it == meta.end() || it->second.tag != 9) fail(FZ_EFORMAT, "metadata key '%s' missing or not an array", k.c_str());
+  const MetaValue& v = it->second;
+  std::vector<std::string> out;
+  if (v.array_len == 0) return out;
+  if (v.array_tag != 8) fail(FZ_EFORMAT, "metadata key '%s': element is not a string", k.c_str());
+  Reader r{base, size, v.array_pos};
+  out.reserve(v.array_len);
+  for (size_t i = 0; i < v.array_len; i++) out.push_back(r.str());
+  return out;
+}
+
+std::vector<int64_t> GgufFile::meta_int_array(const std::string& k) const {
+  auto it = meta.find(k);
+  if (it == meta.end() || it->second.tag != 9) fail(FZ_EFORMAT, "metadata key '%s' missing or not an array", k.c_str());
+  const MetaValue& v = it->second;
+  std::vector<int64_t> out;
+  if (v.array_len == 0) return out;
+  const uint32_t t = v.array_tag;
+  if (!(t <= 5 || t == 10 || t == 11)) fail(FZ_EFORMAT, "metadata key '%s': element is not an integer", k.c_str());
+  Reader r{base, size, v.array_pos};
+  out.reserve(v.array_len);
+  for (size_t i = 0; i < v.array_len; i++) {
+    MetaValue e;
+    read_value(r, t, &e, 1);
+    if (t == 10 && e.u > (uint64_t)INT64_MAX) fail(FZ_EFORMAT, "metadata key '%s': element is not an i64", k.c_str());
+    out.push_back(e.i);
+  }
+  return out;
+}
+
+// Well-formed UTF-8 per Unicode table 3-7 (no overlongs, surrogates or code
+// points above U+10FFFF).
+bool utf8_valid(const uint8_t* p, size_t n) {
+  size_t i = 0;
+  while (i < n) {
+    const uint8_t b = p[i];
+    if (b < 0x80) {
+      i++;
+      continue;
+    }
+    size_t len;
+    uint8_t lo = 0x80, hi = 0xBF;
+    if (b >= 0xC2 && b <= 0xDF) {
+      len = 2;
+    } else if (b >= 0xE0 && b <= 0xEF) {
+      len = 3;
+      if (b == 0xE0) lo = 0xA0;
+      if (b == 0xED) hi = 0x9F;
+    } else if (b >= 0xF0 && b <= 0xF4) {
+      len = 4;
+      if (b == 0xF0) lo = 0x90;
+      if (b == 0xF4) hi = 0x8F;
+    } else {
+      return false;
+    }
+    if (n - i < len || p[i + 1] < lo || p[i + 1] > hi) return false;
+    for (size_t k = 2; k < len; k++)
+      if (p[i + k] < 0x80 || p[i + k] > 0xBF) return false;
+    i += len;
+  }
+  return true;
 }
 
 std::unique_ptr<GgufFile> open_gguf(const char* path) {

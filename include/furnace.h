@@ -39,7 +39,8 @@ enum {
   FZ_EIO = 3,      /* cannot open / map the file */
   FZ_ECUDA = 4,    /* CUDA runtime or kernel error */
   FZ_ENOMEM = 5,   /* device allocation failed */
-  FZ_ETIMEOUT = 6  /* a bounded device-side wait ran out */
+  FZ_ETIMEOUT = 6, /* a bounded device-side wait ran out */
+  FZ_ESPACE = 7    /* output buffer too small: the size needed is reported, nothing was consumed */
 };
 
 /* ggml tensor types the decode path computes on (src/gguf.rs:180-201). */
@@ -208,6 +209,45 @@ int fz_sample(fz_model* m, fz_sampler* s, const uint32_t* recent, uint32_t n_rec
  * device-fed loop.  *n_out = ids written. */
 int fz_generate(fz_model* m, fz_kv* kv, fz_sampler* s, const uint32_t* prompt, uint32_t n_prompt, uint32_t max_new,
                 const uint32_t* stop_ids, uint32_t n_stop, uint32_t* ids_out, uint32_t* n_out);
+
+/* ---- Tokenizer (src/tokenizer.rs) and text helpers (src/generate.rs) -------
+ * Host code.  Text is UTF-8 (len bytes, not terminated); ill-formed input
+ * returns FZ_EINVAL.  Outputs go to caller buffers of `cap` elements: the
+ * count or size is always reported, and FZ_ESPACE means it did not fit and
+ * nothing was consumed. */
+typedef struct fz_tokenizer fz_tokenizer;
+/* Tokenizer::from_gguf (src/tokenizer.rs:67-90): tokenizer.ggml.model "gpt2",
+ * tokenizer.ggml.pre "qwen2", tokens, token_type and merges from the file. */
+int fz_tokenizer_from_gguf(const fz_file* f, fz_tokenizer** out);
+/* Tokenizer::new (src/tokenizer.rs:92-138): n token strings (in the GPT-2
+ * byte alphabet) with their gguf token types (3 control and 4 user-defined
+ * are special), n_merges "left right" rules in rank order. */
+int fz_tokenizer_new(const char* const* tokens, const int64_t* token_types, size_t n, const char* const* merges,
+                     size_t n_merges, fz_tokenizer** out);
+void fz_tokenizer_free(fz_tokenizer* t);
+int fz_tokenizer_vocab_size(const fz_tokenizer* t, size_t* n);
+/* Tokenizer::encode (src/tokenizer.rs:140-149): *n = number of ids. */
+int fz_tokenizer_encode(const fz_tokenizer* t, const char* text, size_t len, uint32_t* ids, size_t cap, size_t* n);
+/* Tokenizer::decode (src/tokenizer.rs:151-157): UTF-8, each maximal
+ * ill-formed subsequence replaced by U+FFFD (String::from_utf8_lossy). */
+int fz_tokenizer_decode(const fz_tokenizer* t, const uint32_t* ids, size_t n, char* out, size_t cap, size_t* len);
+/* Tokenizer::token_bytes (src/tokenizer.rs:159-181): raw bytes of one token,
+ * possibly a partial UTF-8 sequence. */
+int fz_tokenizer_token_bytes(const fz_tokenizer* t, uint32_t id, char* out, size_t cap, size_t* len);
+/* The qwen2 pre-tokenizer split (the pattern of src/tokenizer.rs:16, applied
+ * by encode_ordinary, :215-232) alone: ends[i] = byte offset where chunk i
+ * ends; *n = number of chunks. */
+int fz_pretokenize(const char* text, size_t len, size_t* ends, size_t cap, size_t* n);
+/* chat_template (src/generate.rs:13-21): the ChatML prompt around `prompt`. */
+int fz_chat_template(const char* prompt, size_t len, char* out, size_t cap, size_t* out_len);
+/* Utf8Stream (src/generate.rs:24-66): push token bytes, get the printable
+ * prefix (an incomplete last character is held back); flush emits the rest
+ * lossily. */
+typedef struct fz_utf8_stream fz_utf8_stream;
+int fz_utf8_stream_new(fz_utf8_stream** out);
+void fz_utf8_stream_free(fz_utf8_stream* s);
+int fz_utf8_stream_push(fz_utf8_stream* s, const void* bytes, size_t n, char* out, size_t cap, size_t* len);
+int fz_utf8_stream_flush(fz_utf8_stream* s, char* out, size_t cap, size_t* len);
 
 /* Per-op decode timings, the device counterpart of the reference's perf
  * counters (src/perf.rs:25-39, reported by `run --timings`): runs `reps`
