@@ -297,3 +297,26 @@ def test_synthetic_model_vocabulary(tmp_path):
     with pytest.raises(fz.FurnaceError) as e:
         t.encode("abc")
     assert e.value.code == fz.FZ_EINVAL
+
+
+def test_encode_matches_hf_tokenizers(trained):
+    """A third implementation of the same published algorithm: HF
+    `tokenizers` (0.22.2 here, Rust, Oniguruma regex) configured as Qwen2's
+    tokenizer.json pre-tokenizer (Split on the same pattern, isolated, then
+    ByteLevel without its own regex) over the same vocabulary, merges and
+    special tokens, without Qwen's NFC normalizer (the reference applies
+    none)."""
+    tk = pytest.importorskip("tokenizers")
+    tokens, types, merges = trained
+    hf = tk.Tokenizer(tk.models.BPE(vocab={t: i for i, t in enumerate(tokens)},
+                                    merges=[tuple(m.split(" ")) for m in merges]))
+    hf.pre_tokenizer = tk.pre_tokenizers.Sequence([
+        tk.pre_tokenizers.Split(tk.Regex(ot.QWEN2_SPLIT_PATTERN), behavior="isolated", invert=False),
+        tk.pre_tokenizers.ByteLevel(add_prefix_space=False, use_regex=False)])
+    hf.add_special_tokens([tk.AddedToken(lit, special=True, normalized=False) for lit, _ in SPECIALS])
+    ours = fz.Tokenizer.new(tokens, types, merges)
+    rng = random.Random(29)
+    pool = POOL + [s for s, _ in SPECIALS] + ["<|im_start", "|>", "<tool"]
+    for _ in range(2000):
+        s = rand_text(rng, 50, pool)
+        assert ours.encode(s) == hf.encode(s, add_special_tokens=False).ids, repr(s)
