@@ -40,11 +40,11 @@ EXPORTS = [
     "fz_last_error", "fz_version", "fz_open", "fz_open_bytes", "fz_file_free", "fz_file_info", "fz_tensor_at",
     "fz_tensor", "fz_meta_u32", "fz_meta_f32", "fz_meta_str", "fz_meta_array_len", "fz_config_from_gguf",
     "fz_model_load", "fz_model_free", "fz_model_config", "fz_model_bytes", "fz_kv_new", "fz_kv_free", "fz_kv_len",
-    "fz_kv_set_len", "fz_kv_read", "fz_forward", "fz_forward_last", "fz_decode_greedy", "fz_dequant", "fz_matmul_quant",
-    "fz_weight_upload", "fz_weight_free", "fz_matmul_quant_dev", "fz_step_profile", "fz_model_stream",
-    "fz_dequant_dev_noalloc", "fz_tp_slice_of", "fz_tp_unique_id", "fz_model_load_tp",
-    "fz_sampler_new", "fz_sampler_free", "fz_sampler_draws", "fz_sample_logits", "fz_sample", "fz_generate",
-    "fz_tokenizer_from_gguf", "fz_tokenizer_new", "fz_tokenizer_free", "fz_tokenizer_vocab_size",
+    "fz_kv_set_len", "fz_kv_reset", "fz_kv_bytes", "fz_kv_read", "fz_forward", "fz_forward_last", "fz_decode_greedy",
+    "fz_dequant", "fz_matmul_quant", "fz_gemv", "fz_weight_upload", "fz_weight_free", "fz_matmul_quant_dev",
+    "fz_step_profile", "fz_model_stream", "fz_dequant_dev_noalloc", "fz_tp_slice_of", "fz_tp_unique_id",
+    "fz_model_load_tp", "fz_sampler_new", "fz_sampler_free", "fz_sampler_draws", "fz_sample_logits", "fz_sample",
+    "fz_generate", "fz_tokenizer_from_gguf", "fz_tokenizer_new", "fz_tokenizer_free", "fz_tokenizer_vocab_size",
     "fz_tokenizer_encode", "fz_tokenizer_decode", "fz_tokenizer_token_bytes", "fz_pretokenize", "fz_chat_template",
     "fz_utf8_stream_new", "fz_utf8_stream_free", "fz_utf8_stream_push", "fz_utf8_stream_flush",
 ]
@@ -122,6 +122,9 @@ def load_library(build_if_missing: bool = True):
         "fz_forward_last": (I, [P, u32p, U32, fp, u32p]),
         "fz_decode_greedy": (I, [P, P, U32, U32, u32p, U32, u32p, fp, u32p]),
         "fz_dequant": (I, [U32, P, S, S, fp]),
+        "fz_gemv": (I, [U32, P, U32, U32, fp, fp]),
+        "fz_kv_reset": (I, [P]),
+        "fz_kv_bytes": (I, [P, C.POINTER(U64)]),
         "fz_matmul_quant": (I, [fp, U32, P, S, U32, U32, U32, fp]),
         "fz_weight_upload": (I, [U32, P, S, U32, U32, pp]),
         "fz_weight_free": (None, [P]),
@@ -430,6 +433,16 @@ class KvCache:
     def len(self, n: int):
         _check(load_library().fz_kv_set_len(self._h, n))
 
+    def reset(self):
+        """len = 0: the cache reused for a new sequence."""
+        _check(load_library().fz_kv_reset(self._h))
+
+    def bytes(self) -> int:
+        """KvCache::bytes (src/model.rs:341-343): K and V bytes of this rank."""
+        v = C.c_uint64()
+        _check(load_library().fz_kv_bytes(self._h, C.byref(v)))
+        return v.value
+
     def read(self, layer: int, which_v: bool, n: int) -> np.ndarray:
         """Cached K (or V) rows [0, n) as [n, kv_heads * head_dim]: every KV
         head, or this rank's under tensor parallelism."""
@@ -460,6 +473,15 @@ class quant:
         out = np.zeros((a.shape[0], d_out), np.float32)
         _check(load_library().fz_matmul_quant(_fp(a), a.shape[0], buf.ctypes.data, buf.size, d_out, d_in, dtype,
                                               _fp(out)))
+        return out
+
+    @staticmethod
+    def gemv(x, raw: bytes, d_out: int, d_in: int, dtype: int) -> np.ndarray:
+        """One row of quant::matmul_quant (fz_gemv): y = W x."""
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(d_in)
+        buf = np.frombuffer(bytes(raw), dtype=np.uint8)
+        out = np.zeros(d_out, np.float32)
+        _check(load_library().fz_gemv(dtype, buf.ctypes.data, d_out, d_in, _fp(x), _fp(out)))
         return out
 
 

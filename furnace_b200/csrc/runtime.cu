@@ -1254,6 +1254,16 @@ int fz_kv_set_len(fz_kv* kv, uint32_t len) {
   });
 }
 
+int fz_kv_reset(fz_kv* kv) { return fz_kv_set_len(kv, 0); }
+
+int fz_kv_bytes(const fz_kv* kv, uint64_t* bytes) {
+  return guard([&] {
+    need(kv && bytes, "null argument");
+    need(kv->m != nullptr, "the cache's model has been freed");
+    *bytes = (uint64_t)kv->k.n + kv->v.n;
+  });
+}
+
 int fz_kv_read(const fz_kv* kv, uint32_t layer, int which_v, uint32_t n, float* out) {
   return guard([&] {
     need(kv && out, "null argument");
@@ -1601,6 +1611,17 @@ int fz_matmul_quant(const float* a, uint32_t seq, const void* raw, size_t nbytes
   });
   fz_weight_free(w);
   return rc;
+}
+
+int fz_gemv(uint32_t dtype, const void* raw, uint32_t d_out, uint32_t d_in, const float* x, float* y) {
+  uint64_t nbytes = 0;
+  const int rc = guard([&] {
+    uint32_t be, bb;
+    need(block_geom(dtype, &be, &bb), "type %u is not implemented", dtype);
+    need(d_in % be == 0, "d_in %u is not a multiple of the %u-element block", d_in, be);
+    nbytes = gguf_bytes(dtype, d_out, d_in);
+  });
+  return rc ? rc : fz_matmul_quant(x, 1, raw, nbytes, d_out, d_in, dtype, y);
 }
 
 int fz_dequant(uint32_t dtype, const void* raw, size_t nbytes, size_t n, float* out) {

@@ -155,6 +155,10 @@ void fz_kv_free(fz_kv* kv);
  * filled length; positions >= len are overwritten by later forwards. */
 int fz_kv_len(const fz_kv* kv, uint32_t* len);
 int fz_kv_set_len(fz_kv* kv, uint32_t len);
+/* kv.len = 0: the cache reused for a new sequence. */
+int fz_kv_reset(fz_kv* kv);
+/* KvCache::bytes (src/model.rs:341-343): K and V bytes of this rank's cache. */
+int fz_kv_bytes(const fz_kv* kv, uint64_t* bytes);
 /* Copy layer `layer`'s cached K (which_v = 0) or V rows [0, n) to the host
  * as [n, n_kv_heads*head_dim] f32 (the reference's row layout); under tensor
  * parallelism, this rank's KV heads ([n, kv_heads*head_dim]). */
@@ -270,6 +274,9 @@ int fz_dequant(uint32_t dtype, const void* raw, size_t nbytes, size_t n, float* 
  * times the quantized weight [d_out, d_in] (raw GGUF bytes) -> [seq, d_out]. */
 int fz_matmul_quant(const float* a, uint32_t seq, const void* raw, size_t nbytes, uint32_t d_out, uint32_t d_in,
                     uint32_t dtype, float* out);
+/* One row of quant::matmul_quant: y[d_out] = W x[d_in] with W the raw GGUF
+ * blocks of a [d_out, d_in] weight (its size follows from the type). */
+int fz_gemv(uint32_t dtype, const void* raw, uint32_t d_out, uint32_t d_in, const float* x, float* y);
 
 /* ---- Device-resident variants (inputs already in HBM) --------------------- */
 /* Same as fz_matmul_quant with device pointers and a CUDA stream

@@ -96,6 +96,21 @@ def test_gemv_vs_oracle(orc, name, rows, cols):
 
 
 @pytest.mark.parametrize("name", list(TYPES))
+def test_gemv_entry_point(orc, name):
+    """fz_gemv: one row of matmul_quant, the weight's size implied by its type."""
+    dt, be, _ = TYPES[name]
+    raw = synth.random_tensor(96, 512, dt, seed=41)
+    x = np.random.default_rng(43).normal(0, 1, size=512).astype(np.float32)
+    got = fz.quant.gemv(x, raw, 96, 512, dt)
+    assert np.array_equal(got, fz.quant.matmul_quant(x, raw, 96, 512, dt)[0])
+    want = orc.matmul_quant(x.reshape(1, -1), raw, 96, 512, dt)[0]
+    assert np.abs(got - want).max() <= GEMV_REL * np.abs(want).max()
+    with pytest.raises(fz.FurnaceError) as e:
+        fz.quant.gemv(x[:be // 2], raw, 1, be // 2, dt)
+    assert e.value.code == fz.FZ_EINVAL
+
+
+@pytest.mark.parametrize("name", list(TYPES))
 @pytest.mark.parametrize("rows,cols,seq", [(130, 512, 37), (520, 3584, 300), (64, 18944, 9)])
 def test_prefill_gemm_vs_oracle(orc, name, rows, cols, seq):
     """Several input rows take the tensor-core GEMM of the batched prefill
@@ -264,6 +279,24 @@ def test_f16_kv_cache_matches_oracle(tiny):
     with pytest.raises(fz.FurnaceError) as e:
         fz.KvCache(dev, 8, 7)
     assert e.value.code == fz.FZ_EINVAL
+
+
+def test_kv_reset_and_bytes(tiny):
+    """fz_kv_reset (kv.len = 0) reuses a cache: the same prompt gives the same
+    logits again.  fz_kv_bytes is KvCache::bytes: 2 * L * n_kv * max_ctx *
+    head_dim elements of 4 (f32) or 2 (f16) bytes."""
+    f, dev, ref = _models(tiny)
+    c = dev.config
+    for kv_dtype, eb in ((fz.FZ_KV_F32, 4), (fz.FZ_KV_F16, 2)):
+        kd = fz.KvCache(dev, 64, kv_dtype)
+        assert kd.bytes() == 2 * c.n_layers * c.n_kv_heads * 64 * c.head_dim * eb
+        ids = synth.prompt_ids(ref.vocab, 12, seed=9)
+        a, am = dev.forward(ids, kd)
+        kd.reset()
+        assert kd.len == 0
+        b, bm = dev.forward(ids, kd)
+        assert np.array_equal(a, b) and am == bm and kd.len == 12
+        kd.close()
 
 
 def test_cache_outlives_its_model(tiny, orc):
