@@ -22,6 +22,27 @@ struct Error : std::runtime_error {
 
 [[noreturn]] void fail(int code, const char* fmt, ...);
 void set_last_error(const std::string& m);
+// FZ_EINVAL with the formatted message unless cond holds (argument checks).
+void need(bool cond, const char* fmt, ...);
+
+// Runs f and converts what it throws into the C ABI's status code, the
+// message going to fz_last_error().
+template <class F>
+int guard(F&& f) {
+  try {
+    f();
+    return FZ_OK;
+  } catch (const Error& e) {
+    set_last_error(e.what());
+    return e.code;
+  } catch (const std::bad_alloc&) {
+    set_last_error("host allocation failed");
+    return FZ_ENOMEM;
+  } catch (const std::exception& e) {
+    set_last_error(e.what());
+    return FZ_EINVAL;
+  }
+}
 
 // Block geometry of the ggml types on the path (src/gguf.rs:206-216).
 inline bool block_geom(uint32_t t, uint32_t* elems, uint32_t* bytes) {

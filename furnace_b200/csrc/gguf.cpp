@@ -32,6 +32,16 @@ void fail(int code, const char* fmt, ...) {
   throw Error(code, buf);
 }
 
+void need(bool cond, const char* fmt, ...) {
+  if (cond) return;
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  throw Error(FZ_EINVAL, buf);
+}
+
 namespace {
 
 struct Reader {

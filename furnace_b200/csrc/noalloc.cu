@@ -44,16 +44,6 @@ void ck(cudaError_t e, const char* what) {
   if (e != cudaSuccess) fail(FZ_ECUDA, "%s failed: %s", what, cudaGetErrorString(e));
 }
 
-void need(bool cond, const char* fmt, ...) {
-  if (cond) return;
-  char buf[512];
-  va_list ap;
-  va_start(ap, fmt);
-  vsnprintf(buf, sizeof buf, fmt, ap);
-  va_end(ap);
-  throw Error(FZ_EINVAL, buf);
-}
-
 // Address of the current device's copy of the scratch array, looked up once
 // per device (with that device current).  The first call on a device does the
 // lookup, which may load this module onto the device; make that first call

@@ -158,33 +158,6 @@ struct fz_sampler {
 
 namespace {
 
-template <class F>
-int guard(F&& f) {
-  try {
-    f();
-    return FZ_OK;
-  } catch (const Error& e) {
-    set_last_error(e.what());
-    return e.code;
-  } catch (const std::bad_alloc&) {
-    set_last_error("host allocation failed");
-    return FZ_ENOMEM;
-  } catch (const std::exception& e) {
-    set_last_error(e.what());
-    return FZ_EINVAL;
-  }
-}
-
-void need(bool cond, const char* fmt, ...) {
-  if (cond) return;
-  char buf[512];
-  va_list ap;
-  va_start(ap, fmt);
-  vsnprintf(buf, sizeof buf, fmt, ap);
-  va_end(ap);
-  throw Error(FZ_EINVAL, buf);
-}
-
 uint64_t gguf_bytes(uint32_t dtype, uint64_t rows, uint32_t cols) {
   uint32_t be, bb;
   block_geom(dtype, &be, &bb);

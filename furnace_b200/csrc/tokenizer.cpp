@@ -52,23 +52,6 @@ struct fz_utf8_stream {
 
 namespace {
 
-template <class F>
-int guard_text(F&& f) {
-  try {
-    f();
-    return FZ_OK;
-  } catch (const Error& e) {
-    set_last_error(e.what());
-    return e.code;
-  } catch (const std::bad_alloc&) {
-    set_last_error("host allocation failed");
-    return FZ_ENOMEM;
-  } catch (const std::exception& e) {
-    set_last_error(e.what());
-    return FZ_EINVAL;
-  }
-}
-
 // ---- code point classes (the pattern's \p{L}, \p{N}, \s) ----------------------
 template <size_t N>
 bool in_ranges(const uni::CpRange (&r)[N], uint32_t c) {
@@ -412,7 +395,7 @@ std::string text_arg(const char* text, size_t len) {
 extern "C" {
 
 int fz_tokenizer_from_gguf(const fz_file* f, fz_tokenizer** out) {
-  return guard_text([&] {
+  return guard([&] {
     if (!f || !out) fail(FZ_EINVAL, "null argument");
     const GgufFile& g = *f->g;
     const std::string& model = g.meta_str("tokenizer.ggml.model");
@@ -428,7 +411,7 @@ int fz_tokenizer_from_gguf(const fz_file* f, fz_tokenizer** out) {
 
 int fz_tokenizer_new(const char* const* tokens, const int64_t* token_types, size_t n, const char* const* merges,
                      size_t n_merges, fz_tokenizer** out) {
-  return guard_text([&] {
+  return guard([&] {
     if (!out || (n && (!tokens || !token_types)) || (n_merges && !merges)) fail(FZ_EINVAL, "null argument");
     std::vector<std::string> tv(n), mv(n_merges);
     for (size_t i = 0; i < n; i++) tv[i] = text_arg(tokens[i], tokens[i] ? strlen(tokens[i]) : 0);
@@ -440,14 +423,14 @@ int fz_tokenizer_new(const char* const* tokens, const int64_t* token_types, size
 void fz_tokenizer_free(fz_tokenizer* t) { delete t; }
 
 int fz_tokenizer_vocab_size(const fz_tokenizer* t, size_t* n) {
-  return guard_text([&] {
+  return guard([&] {
     if (!t || !n) fail(FZ_EINVAL, "null argument");
     *n = t->vocab.size();
   });
 }
 
 int fz_tokenizer_encode(const fz_tokenizer* t, const char* text, size_t len, uint32_t* ids, size_t cap, size_t* n) {
-  return guard_text([&] {
+  return guard([&] {
     if (!t || !n) fail(FZ_EINVAL, "null argument");
     const std::vector<uint32_t> v = encode(*t, text_arg(text, len));
     *n = v.size();
@@ -457,7 +440,7 @@ int fz_tokenizer_encode(const fz_tokenizer* t, const char* text, size_t len, uin
 }
 
 int fz_tokenizer_decode(const fz_tokenizer* t, const uint32_t* ids, size_t n, char* out, size_t cap, size_t* len) {
-  return guard_text([&] {
+  return guard([&] {
     if (!t || (n && !ids)) fail(FZ_EINVAL, "null argument");
     std::string bytes;
     for (size_t i = 0; i < n; i++) bytes += token_bytes(*t, ids[i]);
@@ -466,14 +449,14 @@ int fz_tokenizer_decode(const fz_tokenizer* t, const uint32_t* ids, size_t n, ch
 }
 
 int fz_tokenizer_token_bytes(const fz_tokenizer* t, uint32_t id, char* out, size_t cap, size_t* len) {
-  return guard_text([&] {
+  return guard([&] {
     if (!t) fail(FZ_EINVAL, "null argument");
     give(token_bytes(*t, id), out, cap, len);
   });
 }
 
 int fz_pretokenize(const char* text, size_t len, size_t* ends, size_t cap, size_t* n) {
-  return guard_text([&] {
+  return guard([&] {
     if (!n) fail(FZ_EINVAL, "null argument");
     std::vector<std::pair<size_t, size_t>> chunks;
     pretokenize(text_arg(text, len), &chunks);
@@ -484,7 +467,7 @@ int fz_pretokenize(const char* text, size_t len, size_t* ends, size_t cap, size_
 }
 
 int fz_chat_template(const char* prompt, size_t len, char* out, size_t cap, size_t* out_len) {
-  return guard_text([&] {
+  return guard([&] {
     const std::string p = text_arg(prompt, len);
     give("<|im_start|>system\nYou are Qwen, created by Alibaba Cloud. You are a helpful assistant.<|im_end|>\n"
          "<|im_start|>user\n" + p + "<|im_end|>\n<|im_start|>assistant\n",
@@ -493,7 +476,7 @@ int fz_chat_template(const char* prompt, size_t len, char* out, size_t cap, size
 }
 
 int fz_utf8_stream_new(fz_utf8_stream** out) {
-  return guard_text([&] {
+  return guard([&] {
     if (!out) fail(FZ_EINVAL, "null argument");
     *out = new fz_utf8_stream();
   });
@@ -502,7 +485,7 @@ int fz_utf8_stream_new(fz_utf8_stream** out) {
 void fz_utf8_stream_free(fz_utf8_stream* s) { delete s; }
 
 int fz_utf8_stream_push(fz_utf8_stream* s, const void* bytes, size_t n, char* out, size_t cap, size_t* len) {
-  return guard_text([&] {
+  return guard([&] {
     if (!s || (n && !bytes)) fail(FZ_EINVAL, "null argument");
     std::string buf = s->buf;
     buf.append(static_cast<const char*>(bytes), n);
@@ -530,7 +513,7 @@ int fz_utf8_stream_push(fz_utf8_stream* s, const void* bytes, size_t n, char* ou
 }
 
 int fz_utf8_stream_flush(fz_utf8_stream* s, char* out, size_t cap, size_t* len) {
-  return guard_text([&] {
+  return guard([&] {
     if (!s) fail(FZ_EINVAL, "null argument");
     give(utf8_lossy(s->buf), out, cap, len);
     s->buf.clear();
