@@ -212,6 +212,18 @@ def ncu_traffic():
     return None
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo), or "unknown"."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_baseline(path, vocab, budget_s=15.0):
     """The reference path's CPU restatement (oracle/) on all host cores: a
     short prefill, then decode tokens until ~budget_s of decode time."""
@@ -235,7 +247,7 @@ def cpu_baseline(path, vocab, budget_s=15.0):
         tok = int(lg.argmax())
         n += 1
     m.close()
-    return {"value": n / dec, "unit": "tok/s", "cores": cores, "kind": "port",
+    return {"value": n / dec, "unit": "tok/s", "cores": cores, "kind": "port", "cpu": cpu_model(),
             "sample": f"{n} greedy decode tokens after an 8-token prefill ({prefill_s:.1f} s) at context 8-{8 + n}, "
                       f"same synthetic GGUF, oracle/ C++ restatement of the reference CPU path, {cores} threads"}
 
@@ -272,7 +284,8 @@ def run_reference(args, dist):
                                    f"8-{8 + args.warmup + args.steps} of the {args.prefill}-token-prefill workload",
                        "model": spec.name, "global_batch": 1, "seq_len": 8 + args.warmup + args.steps,
                        "parallelism": f"cpu{cores}"},
-            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "cpu": cpu_model(),
+                             "sample": sample},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
