@@ -68,8 +68,16 @@ bool in_ranges(const uni::CpRange (&r)[N], uint32_t c) {
 bool is_letter(uint32_t c) { return c < 0x80 ? ((c | 0x20) - 'a') < 26u : in_ranges(uni::kLetter, c); }
 bool is_number(uint32_t c) { return c < 0x80 ? (c - '0') < 10u : in_ranges(uni::kNumber, c); }
 bool is_space(uint32_t c) { return c < 0x80 ? (c == ' ' || (c >= 9 && c <= 13)) : in_ranges(uni::kSpace, c); }
-bool is_other(uint32_t c) { return !is_space(c) && !is_letter(c) && !is_number(c); }
 bool is_nl(uint32_t c) { return c == '\r' || c == '\n'; }
+
+// The pattern's view of one code point, computed once per code point.
+enum : uint8_t { C_LETTER = 1, C_NUMBER = 2, C_SPACE = 4, C_NL = 8 };
+uint8_t classify(uint32_t c) {
+  if (is_letter(c)) return C_LETTER;
+  if (is_number(c)) return C_NUMBER;
+  if (is_space(c)) return (uint8_t)(C_SPACE | (is_nl(c) ? C_NL : 0));
+  return 0;  // other: not whitespace, letter or number
+}
 // the ASCII letter a contraction letter's case-insensitive match folds to, or 0
 uint32_t fold(uint32_t c) {
   for (const auto& f : uni::kFold)
@@ -191,9 +199,10 @@ std::string utf8_lossy(const std::string& s) {
 //   (?i:'s|'t|'re|'ve|'m|'ll|'d) | [^\r\n\p{L}\p{N}]?\p{L}+ | \p{N} |
 //   ' '?[^\s\p{L}\p{N}]+[\r\n]* | \s*[\r\n]+ | \s+(?!\S) | \s+
 // Every code point starts some alternative, so the matches tile the text.
-size_t match_at(const std::vector<uint32_t>& cp, size_t i) {
+size_t match_at(const std::vector<uint32_t>& cp, const std::vector<uint8_t>& cl, size_t i) {
   const size_t n = cp.size();
   const uint32_t c0 = cp[i];
+  const uint8_t k0 = cl[i];
   if (c0 == '\'' && i + 1 < n) {
     const uint32_t a = fold(cp[i + 1]);
     if (a == 's' || a == 't' || a == 'm' || a == 'd') return i + 2;
@@ -204,26 +213,26 @@ size_t match_at(const std::vector<uint32_t>& cp, size_t i) {
   }
   {
     size_t j = i;
-    if (!is_letter(c0) && !is_number(c0) && !is_nl(c0) && i + 1 < n && is_letter(cp[i + 1])) j = i + 1;
-    if (is_letter(cp[j])) {
-      while (j < n && is_letter(cp[j])) j++;
+    if (!(k0 & (C_LETTER | C_NUMBER | C_NL)) && i + 1 < n && (cl[i + 1] & C_LETTER)) j = i + 1;
+    if (cl[j] & C_LETTER) {
+      while (j < n && (cl[j] & C_LETTER)) j++;
       return j;
     }
   }
-  if (is_number(c0)) return i + 1;
+  if (k0 & C_NUMBER) return i + 1;
   {
     size_t j = i;
-    if (c0 == ' ' && i + 1 < n && is_other(cp[i + 1])) j = i + 1;
-    if (is_other(cp[j])) {
-      while (j < n && is_other(cp[j])) j++;
-      while (j < n && is_nl(cp[j])) j++;
+    if (c0 == ' ' && i + 1 < n && cl[i + 1] == 0) j = i + 1;
+    if (cl[j] == 0) {
+      while (j < n && cl[j] == 0) j++;
+      while (j < n && (cl[j] & C_NL)) j++;
       return j;
     }
   }
   size_t j = i;  // c0 is whitespace
-  while (j < n && is_space(cp[j])) j++;
+  while (j < n && (cl[j] & C_SPACE)) j++;
   for (size_t k = j; k > i; k--)  // \s*[\r\n]+ ends after the run's last newline
-    if (is_nl(cp[k - 1])) return k;
+    if (cl[k - 1] & C_NL) return k;
   if (j == n || j - i < 2) return j;  // \s+(?!\S) at the end of text, or \s+
   return j - 1;                       // \s+(?!\S): the last space stays for the next chunk
 }
@@ -233,17 +242,21 @@ void pretokenize(const std::string& text, std::vector<std::pair<size_t, size_t>>
   std::vector<uint32_t> cp;
   std::vector<size_t> off;
   decode_utf8(text, &cp, &off);
+  std::vector<uint8_t> cl(cp.size());
+  for (size_t i = 0; i < cp.size(); i++) cl[i] = classify(cp[i]);
   chunks->clear();
   for (size_t i = 0; i < cp.size();) {
-    const size_t j = match_at(cp, i);
+    const size_t j = match_at(cp, cl, i);
     chunks->push_back({off[i], off[j]});
     i = j;
   }
 }
 
 // ---- BPE (src/tokenizer.rs:234-285) ---------------------------------------------
-void bpe_chunk(const fz_tokenizer& t, const char* s, size_t len, std::vector<uint32_t>* ids) {
-  std::vector<uint32_t> word(len), next;
+// word / next: scratch reused across chunks
+void bpe_chunk(const fz_tokenizer& t, const char* s, size_t len, std::vector<uint32_t>* ids,
+               std::vector<uint32_t>& word, std::vector<uint32_t>& next) {
+  word.resize(len);
   for (size_t i = 0; i < len; i++) word[i] = t.byte_sym[(uint8_t)s[i]];
   while (word.size() > 1) {
     // the adjacent pair of lowest rank (the first such pair on ties)
@@ -281,7 +294,8 @@ void bpe_chunk(const fz_tokenizer& t, const char* s, size_t len, std::vector<uin
 void encode_ordinary(const fz_tokenizer& t, const std::string& text, std::vector<uint32_t>* ids) {
   std::vector<std::pair<size_t, size_t>> chunks;
   pretokenize(text, &chunks);
-  for (const auto& c : chunks) bpe_chunk(t, text.data() + c.first, c.second - c.first, ids);
+  std::vector<uint32_t> word, next;
+  for (const auto& c : chunks) bpe_chunk(t, text.data() + c.first, c.second - c.first, ids, word, next);
 }
 
 std::vector<uint32_t> encode(const fz_tokenizer& t, const std::string& text) {
