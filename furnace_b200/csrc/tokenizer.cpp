@@ -300,14 +300,23 @@ void encode_ordinary(const fz_tokenizer& t, const std::string& text, std::vector
 
 std::vector<uint32_t> encode(const fz_tokenizer& t, const std::string& text) {
   std::vector<uint32_t> ids;
+  // next occurrence of each special literal at or after the last search
+  // position (npos: none left), searched again only once pos passes it
+  std::vector<size_t> next(t.specials.size(), 0);
+  std::vector<bool> searched(t.specials.size(), false);
   size_t pos = 0;
   while (pos < text.size()) {
     // leftmost special literal; the longest one at equal starts (specials are
     // sorted longest first and only a strictly earlier start replaces one)
     size_t start = std::string::npos, lit_len = 0;
     uint32_t id = 0;
-    for (const auto& sp : t.specials) {
-      const size_t f = text.find(sp.first, pos);
+    for (size_t k = 0; k < t.specials.size(); k++) {
+      const auto& sp = t.specials[k];
+      if (!searched[k] || (next[k] != std::string::npos && next[k] < pos)) {
+        next[k] = text.find(sp.first, pos);
+        searched[k] = true;
+      }
+      const size_t f = next[k];
       if (f != std::string::npos && (start == std::string::npos || f < start)) {
         start = f;
         lit_len = sp.first.size();
