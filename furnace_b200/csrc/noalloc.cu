@@ -86,15 +86,22 @@ extern "C" int fz_dequant_dev_noalloc(uint32_t dtype, const void* raw_dev, size_
         k = t;
         break;
       }
-    DevMat m;
-    m.dtype = dtype;
-    m.rows = (uint32_t)(nblk / k);
-    m.cols = (uint32_t)(k * be);
-    m.stride = dev_row_stride(dtype, m.cols);
-    const uint64_t lay_bytes = (uint64_t)m.rows * m.stride;
+    // the scratch bound is checked on the 64-bit row count, before anything
+    // is narrowed to the layout's 32-bit row index
+    const uint64_t rows64 = nblk / k;
+    const uint32_t cols = (uint32_t)(k * be);
+    const uint64_t stride = dev_row_stride(dtype, cols);  // < 2^12: rows64 * stride cannot wrap below
+    need(rows64 <= kScratchBytes, "fz_dequant_dev_noalloc: %zu blocks exceed the %zu-byte scratch", (size_t)nblk,
+         kScratchBytes);
+    const uint64_t lay_bytes = rows64 * stride;
     need(lay_bytes <= kScratchBytes,
          "fz_dequant_dev_noalloc: %zu blocks need %llu bytes of scratch, the limit is %zu (fz_dequant has none)",
          (size_t)nblk, (unsigned long long)lay_bytes, kScratchBytes);
+    DevMat m;
+    m.dtype = dtype;
+    m.rows = (uint32_t)rows64;
+    m.cols = cols;
+    m.stride = stride;
     if (!m.rows) return FZ_OK;
     uint8_t* lay = scratch_for_current_device();
     // padding inside the layout starts at zero, as in fz_dequant's buffer

@@ -551,6 +551,29 @@ void matmul_q8_0(const float* a, size_t seq, const uint8_t* raw, size_t d_out, s
 void matmul_blocks(const float* a, size_t seq, const uint8_t* raw, size_t d_out, size_t d_in,
                    size_t be, size_t bb, BlockFn fn, float* out) {
   size_t row_bytes = d_in / be * bb;
+  if (seq > 1) {
+    // Prefill: the reference re-dequantizes each block for every activation
+    // row (src/tensor.rs:114-135 calling src/quant.rs:214-226).  The
+    // dequantized values do not depend on the row, so each weight row is
+    // decoded once here and every activation row runs the same per-block
+    // `acc += dot(...)` sequence over it: identical results, less work.
+    size_t chunks = (d_out + 63) / 64;
+    pool().parallel_for(chunks, [&](size_t c) {
+      std::vector<float> wrow(d_in);
+      size_t o0 = c * 64, o1 = std::min(d_out, o0 + 64);
+      for (size_t o = o0; o < o1; o++) {
+        const uint8_t* row = raw + o * row_bytes;
+        for (size_t b = 0; b < d_in / be; b++) fn(row + b * bb, wrow.data() + b * be);
+        for (size_t s = 0; s < seq; s++) {
+          const float* arow = a + s * d_in;
+          float acc = 0.0f;
+          for (size_t b = 0; b < d_in / be; b++) acc += dot8(arow + b * be, wrow.data() + b * be, be);
+          out[s * d_out + o] = acc;
+        }
+      }
+    });
+    return;
+  }
   matmul_with(a, seq, d_out, d_in, out, [&](size_t o, const float* arow) {
     const uint8_t* row = raw + o * row_bytes;
     float buf[256];
@@ -830,7 +853,12 @@ void attention(const float* q, size_t n_new, const float* kc, const float* vc, s
   size_t kv_dim = nkv * hd, group = nh / nkv;
   float scale = 1.0f / sqrtf((float)hd);
   std::vector<float> probs(nh * n_new * total);
-  for (size_t h = 0; h < nh; h++) {
+  memset(out, 0, sizeof(float) * n_new * nh * hd);
+  // Heads are independent: one task per head, each running the reference's
+  // per-head loops unchanged (scores, softmax row by row, then p * v).  A
+  // masked entry's probability is exactly 0 (exp(-inf)); its p * v term
+  // (+0 or -0 for finite v) leaves the sum unchanged, so it is skipped.
+  pool().parallel_for(nh, [&](size_t h) {
     size_t kv = h / group;
     for (size_t s = 0; s < n_new; s++) {
       const float* qh = q + s * nh * hd + h * hd;
@@ -846,21 +874,18 @@ void attention(const float* q, size_t n_new, const float* kc, const float* vc, s
         }
       }
     }
-  }
-  softmax(probs.data(), nh * n_new, total);
-  memset(out, 0, sizeof(float) * n_new * nh * hd);
-  for (size_t h = 0; h < nh; h++) {
-    size_t kv = h / group;
+    softmax(probs.data() + h * n_new * total, n_new, total);
     for (size_t s = 0; s < n_new; s++) {
       const float* row = probs.data() + (h * n_new + s) * total;
       float* oh = out + s * nh * hd + h * hd;
-      for (size_t t = 0; t < total; t++) {
+      const size_t lim = std::min(total, start_pos + s + 1);
+      for (size_t t = 0; t < lim; t++) {
         float p = row[t];
         const float* vh = vc + t * kv_dim + kv * hd;
         for (size_t d = 0; d < hd; d++) oh[d] += p * vh[d];
       }
     }
-  }
+  });
 }
 
 // layer_forward_cached (src/model.rs:444-478).  With cache == nullptr this is
