@@ -125,11 +125,15 @@ struct fz_kv {
   }
   DevBuf k, v, rope_cs, partials, state, forced, ids;
   cudaGraphExec_t g_full = nullptr, g_layers = nullptr;
+  StepKernel *mk_full = nullptr, *mk_layers = nullptr;  // persistent step kernels of the graphs
   // device memory and graphs back; the handle stays valid for fz_kv_free
   void release() {
     if (g_full) cudaGraphExecDestroy(g_full);
     if (g_layers) cudaGraphExecDestroy(g_layers);
     g_full = g_layers = nullptr;
+    step_kernel_free(mk_full);
+    step_kernel_free(mk_layers);
+    mk_full = mk_layers = nullptr;
     for (DevBuf* b : {&k, &v, &rope_cs, &partials, &state, &forced, &ids}) b->release();
   }
   ~fz_kv() { release(); }
@@ -410,6 +414,86 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
   H(FZ_OP_FINALIZE, false);
 }
 
+// The step as one persistent kernel (kernels.cu: step.cuh): the phases of
+// every layer and lm_head with their arrival counters.  Counter block of
+// layer l: 16 l + {0: q|k|v written, 1: attention merges, 2: o_proj, 3:
+// gate/up, 4: down, 8 + g: attention splits of KV head g}.
+bool step_kernel_enabled(const fz_model* m) {
+  if (m->world > 1) return false;  // the tensor-parallel exchange runs on the per-kernel path
+  const char* e = getenv("FURNACE_B200_STEP");
+  return e && e[0] == '1';
+}
+
+StepKernel* build_step_kernel(fz_kv* kv, bool with_logits) {
+  fz_model* m = kv->m;
+  const fz_config& c = m->cfg;
+  const std::vector<GemvLaunch> gl = step_gemvs(kv);
+  const uint32_t grid = step_grid(), S = step_splits(m->nkv_l), L = c.n_layers;
+  auto base = [](uint32_t l) { return 16 * l; };
+  std::vector<StepPhaseDesc> ph;
+  for (uint32_t l = 0; l < L; l++) {
+    StepPhaseDesc q, a, o, u, d;
+    q.g = gl[4 * l];
+    if (l) {
+      q.wait_ctr = base(l - 1) + 4;
+      q.wait_target = grid;
+    }
+    q.arrive_ctr = base(l);
+    a.kind = 1;
+    a.a = layer_attention(kv, l, S);
+    a.wait_ctr = base(l);
+    a.wait_target = grid;
+    a.arrive_ctr = base(l) + 1;
+    a.att_ctr0 = base(l) + 8;
+    o.g = gl[4 * l + 1];
+    o.wait_ctr = base(l) + 1;
+    o.wait_target = m->nkv_l * S;  // every attention CTA arrives after merging its share
+    o.arrive_ctr = base(l) + 2;
+    u.g = gl[4 * l + 2];
+    u.wait_ctr = base(l) + 2;
+    u.wait_target = grid;
+    u.arrive_ctr = base(l) + 3;
+    d.g = gl[4 * l + 3];
+    d.wait_ctr = base(l) + 3;
+    d.wait_target = grid;
+    d.arrive_ctr = base(l) + 4;
+    for (StepPhaseDesc* x : {&q, &a, &o, &u, &d}) ph.push_back(*x);
+  }
+  if (with_logits) {
+    StepPhaseDesc lm;
+    lm.g = gl[4 * L];
+    lm.wait_ctr = base(L - 1) + 4;
+    lm.wait_target = grid;
+    lm.arrive_ctr = 16 * L + 1;
+    ph.push_back(lm);
+  }
+  StepGlobals g{};
+  g.qkv = m->qkv.as<float>();
+  g.rope_cs = kv->rope_cs.as<float>();
+  g.partials = kv->partials.as<float>();
+  g.ctx = m->ctx.as<float>();
+  g.nh = m->nh_l;
+  g.nkv = m->nkv_l;
+  g.hd = c.head_dim;
+  g.max_ctx = kv->max_ctx;
+  g.splits = S;
+  g.kv_f16 = kv->eb == 2;
+  g.st = kv->state.as<StepState>();
+  g.eps = c.rms_eps;
+  g.nsync = 16 * L + 2;
+  g.done_ctr = 16 * L;
+  return step_kernel_build(ph, g);
+}
+
+// One step through the persistent kernel: embed, the step kernel, finalize.
+void record_step_mk(fz_kv* kv, bool with_logits, cudaStream_t s) {
+  fz_model* m = kv->m;
+  StepState* st = kv->state.as<StepState>();
+  launch_embed(m->embd, st, m->x.as<float>(), s);
+  launch_step_kernel(with_logits ? kv->mk_full : kv->mk_layers, s);
+  launch_finalize(st, kv->forced.as<uint32_t>(), kv->ids.as<uint32_t>(), with_logits, s);
+}
+
 // ---- batched prefill on the tensor cores ------------------------------------
 constexpr uint32_t PF_CHUNK = 8192;  // tokens per prefill pass (each weight is dequantized once per pass)
 constexpr uint32_t PF_MIN = 8;       // shorter prompts replay the decode step
@@ -448,11 +532,13 @@ void prefill_alloc(fz_model* m, uint32_t T) {
   m->pf_xl.alloc(xe * 2);
   // padding rows of the panels are read by the MMAs and dropped by the
   // epilogue: start them finite
-  CK(cudaMemset(m->pf_wh.p, 0, m->pf_wh.n));
-  CK(cudaMemset(m->pf_wl.p, 0, m->pf_wl.n));
-  CK(cudaMemset(m->pf_xh.p, 0, m->pf_xh.n));
-  CK(cudaMemset(m->pf_xl.p, 0, m->pf_xl.n));
-  CK(cudaMemset(m->pf_err.p, 0, 16));
+  // on the model's stream: it does not wait for the legacy default stream,
+  // so a cudaMemset there could still be running when the panels are written
+  CK(cudaMemsetAsync(m->pf_wh.p, 0, m->pf_wh.n, m->stream));
+  CK(cudaMemsetAsync(m->pf_wl.p, 0, m->pf_wl.n, m->stream));
+  CK(cudaMemsetAsync(m->pf_xh.p, 0, m->pf_xh.n, m->stream));
+  CK(cudaMemsetAsync(m->pf_xl.p, 0, m->pf_xl.n, m->stream));
+  CK(cudaMemsetAsync(m->pf_err.p, 0, 16, m->stream));
   m->pf_cap = T;
 }
 
@@ -633,11 +719,19 @@ uint32_t sample_device(fz_model* m, fz_sampler* s, const uint32_t* recent, uint3
 void build_graphs(fz_kv* kv) {
   if (kv->g_full) return;
   cudaStream_t s = kv->m->stream;
+  const bool mk = step_kernel_enabled(kv->m);
+  if (mk) {
+    kv->mk_full = build_step_kernel(kv, true);
+    kv->mk_layers = build_step_kernel(kv, false);
+  }
   for (int variant = 0; variant < 2; variant++) {
     cudaGraph_t g;
     CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
     try {
-      record_step(kv, variant == 0, s);
+      if (mk)
+        record_step_mk(kv, variant == 0, s);
+      else
+        record_step(kv, variant == 0, s);
     } catch (...) {
       cudaStreamEndCapture(s, &g);
       if (g) cudaGraphDestroy(g);
@@ -693,11 +787,114 @@ void check_state(fz_kv* kv) {
   CK(cudaStreamSynchronize(kv->m->stream));
   // codes 1-2: token >= vocab, position >= max_ctx; 3-5 and 7: a bounded
   // device wait (input records, ring slot, KV tile; residual exchange) ran out
+  if (st.error && kv->mk_full) {
+    // a step kernel that stopped early leaves its arrival counters behind:
+    // rebuild the graphs and step kernels (fresh counters) on the next use
+    if (kv->g_full) cudaGraphExecDestroy(kv->g_full);
+    if (kv->g_layers) cudaGraphExecDestroy(kv->g_layers);
+    kv->g_full = kv->g_layers = nullptr;
+    step_kernel_free(kv->mk_full);
+    step_kernel_free(kv->mk_layers);
+    kv->mk_full = kv->mk_layers = nullptr;
+  }
   if (st.error >= 3) fail(FZ_ETIMEOUT, "a bounded device wait ran out (code %u)", st.error);
   if (st.error) fail(FZ_EINVAL, "device step rejected its input (code %u)", st.error);
 }
 
 void use_device(const fz_model* m) { CK(cudaSetDevice(m->device)); }
+
+// Algorithmic bytes of one decode step at position pos, per op kind:
+// GGUF weight bytes, the KV rows read, the vectors read and written.
+void step_bytes(const fz_model* m, const fz_kv* kv, uint64_t pos, double* bytes) {
+  const fz_config& c = m->cfg;
+  uint64_t H = c.hidden, F = m->sl.ffn_n, qd = m->qd_l, kd = m->kd_l;  // this rank's widths
+  bytes[FZ_OP_EMBED] += m->embd.gguf_bytes / c.vocab + H * 4;
+  for (auto& L : m->layers) {
+    bytes[FZ_OP_QKV] += L.wq.gguf_bytes + L.wk.gguf_bytes + L.wv.gguf_bytes + (2 * H + qd + 2 * kd) * 4;
+    bytes[FZ_OP_ROPE] += (qd + 2 * kd) * 4 + (qd + 2 * kd) * 4;
+    bytes[FZ_OP_ATTN] += 2 * (pos + 1) * kd * kv->eb + 2 * qd * 4;
+    bytes[FZ_OP_OPROJ] += L.wo.gguf_bytes + (qd + 2 * H) * 4;
+    bytes[FZ_OP_GATEUP] += L.wgu.gguf_bytes + (2 * H + F) * 4;
+    bytes[FZ_OP_DOWN] += L.wd.gguf_bytes + (F + 2 * H) * 4;
+  }
+  bytes[FZ_OP_LMHEAD] += m->lm_head.gguf_bytes + (2 * H + (uint64_t)c.vocab) * 4;
+}
+
+// fz_step_profile on the captured step (persistent kernel): the step kernel
+// records %globaltimer per CTA and phase; an op's time is the span from the
+// end of the previous phase (the last CTA to finish it) to the end of its own
+// phase, so the ops of a token add up to the kernel's span.  The rest of the
+// token period (embedding, step bookkeeping, launch gaps, from CUDA events
+// around the replays) is reported under FZ_OP_EMBED.
+void step_profile_graph(fz_model* m, fz_kv* kv, uint32_t first, uint32_t reps, double* ms, double* bytes,
+                        uint32_t* launches) {
+  for (int k = 0; k < FZ_OP_COUNT; k++) ms[k] = bytes[k] = launches[k] = 0;
+  if (!reps) return;
+  cudaStream_t s = m->stream;
+  build_graphs(kv);
+  const uint32_t nph = step_kernel_phases(kv->mk_full), grid = step_grid(), L = m->cfg.n_layers;
+  const uint64_t cap = (uint64_t)reps * nph * grid + 64;
+  DevBuf tb(cap * sizeof(TraceRec));
+  trace_install(tb.as<TraceRec>(), (uint32_t)cap);
+  struct Restore {
+    fz_model* m;
+    ~Restore() {
+      try {
+        if (m->trace.p)
+          trace_install(m->trace.as<TraceRec>(), (uint32_t)(m->trace.n / sizeof(TraceRec)));
+        else
+          trace_install(nullptr, 0);
+      } catch (...) {
+      }
+    }
+  } restore{m};
+  cudaEvent_t e0, e1;
+  CK(cudaEventCreate(&e0));
+  CK(cudaEventCreate(&e1));
+  CK(cudaMemcpyAsync(kv->forced.p, &first, 4, cudaMemcpyHostToDevice, s));
+  set_state(kv, kv->len, first, 1);
+  CK(cudaEventRecord(e0, s));
+  for (uint32_t r = 0; r < reps; r++) CK(cudaGraphLaunch(kv->g_full, s));
+  CK(cudaEventRecord(e1, s));
+  CK(cudaStreamSynchronize(s));
+  float total = 0;
+  CK(cudaEventElapsedTime(&total, e0, e1));
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  check_state(kv);
+  const uint32_t n = std::min<uint32_t>(trace_count(), (uint32_t)cap);
+  std::vector<TraceRec> rec(n);
+  if (n) CK(cudaMemcpy(rec.data(), tb.p, (size_t)n * sizeof(TraceRec), cudaMemcpyDeviceToHost));
+  need(n == (uint64_t)reps * nph * grid, "step trace: %u records, expected %llu", n,
+       (unsigned long long)reps * nph * grid);
+  // records of token r are [r * nph * grid, (r + 1) * nph * grid): kernel
+  // boundaries order the tokens; inside one, aux is the phase index
+  double span_ms = 0;
+  for (uint32_t r = 0; r < reps; r++) {
+    std::vector<uint64_t> t0(nph, ~0ull), t4(nph, 0);
+    for (uint64_t i = (uint64_t)r * nph * grid; i < (uint64_t)(r + 1) * nph * grid; i++) {
+      const TraceRec& x = rec[i];
+      need(x.aux < nph, "step trace: bad phase index");
+      t0[x.aux] = std::min(t0[x.aux], x.t[0]);
+      t4[x.aux] = std::max(t4[x.aux], x.t[4]);
+    }
+    uint64_t prev = t0[0];
+    for (uint32_t k = 0; k < nph; k++) {
+      static const int kLayerOps[5] = {FZ_OP_QKV, FZ_OP_ATTN, FZ_OP_OPROJ, FZ_OP_GATEUP, FZ_OP_DOWN};
+      const int op = k == L * 5 ? FZ_OP_LMHEAD : kLayerOps[k % 5];
+      const uint64_t end = std::max(t4[k], prev);
+      ms[op] += (double)(end - prev) * 1e-6;
+      launches[op] += 1;
+      prev = end;
+    }
+    span_ms += (double)(prev - t0[0]) * 1e-6;
+  }
+  ms[FZ_OP_EMBED] = std::max(0.0, (double)total - span_ms);
+  launches[FZ_OP_EMBED] = reps;
+  launches[FZ_OP_FINALIZE] = reps;
+  for (uint32_t r = 0; r < reps; r++) step_bytes(m, kv, kv->len + r, bytes);
+  kv->len += reps;
+}
 
 }  // namespace
 
@@ -816,9 +1013,10 @@ void tp_p2p_setup(fz_model* m) {
   need(W <= (uint32_t)AR_MAX_RANKS, "tensor parallelism over %u ranks > %d", W, AR_MAX_RANKS);
   need(m->cfg.hidden % 4 == 0, "hidden %u not a multiple of 4", m->cfg.hidden);
   m->ar_buf.alloc(ar_buffer_bytes(m->cfg.hidden, W));
-  CK(cudaMemset(m->ar_buf.p, 0, m->ar_buf.n));
+  CK(cudaMemsetAsync(m->ar_buf.p, 0, m->ar_buf.n, m->stream));
   m->ar_base.alloc(16);
-  CK(cudaMemset(m->ar_base.p, 0, m->ar_base.n));
+  CK(cudaMemsetAsync(m->ar_base.p, 0, m->ar_base.n, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
   // every rank takes part in the exchange (the same collective steps on all
   // ranks); a rank that cannot export marks its handle invalid
   static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
@@ -948,7 +1146,7 @@ std::unique_ptr<fz_model> load_model(const fz_file* f, int rank, int world, cons
   }
   if (!share_embd) order.push_back({&m->lm_head, reserve(m->lm_head)});
   m->weights.alloc(total);
-  CK(cudaMemset(m->weights.p, 0, total));
+  CK(cudaMemsetAsync(m->weights.p, 0, total, m->stream));  // the uploads below run on m->stream
   uint8_t* base = m->weights.as<uint8_t>();
   for (auto& o : order) o.first->ptr = base + o.second;
   uint64_t max_raw = 0;
@@ -1016,10 +1214,10 @@ std::unique_ptr<fz_model> load_model(const fz_file* f, int rank, int world, cons
   m->ctx.alloc(qd_l * 4);
   m->h.alloc(F_l * 4);
   m->logits.alloc((uint64_t)sl.vocab_pad * 4);
-  CK(cudaMemset(m->logits.p, 0, m->logits.n));
+  CK(cudaMemsetAsync(m->logits.p, 0, m->logits.n, m->stream));
   auto runs = [&](DevBuf& b, uint32_t n) {
     b.alloc((uint64_t)runs_for(n) * 64);
-    CK(cudaMemset(b.p, 0, b.n));  // padding records past the vector must read as zero
+    CK(cudaMemsetAsync(b.p, 0, b.n, m->stream));  // padding records past the vector must read as zero
   };
   std::vector<uint32_t> offs;  // distinct o_off values, in order of first use
   m->ctx_buf.assign(c.n_layers, 0);
@@ -1170,8 +1368,9 @@ int fz_kv_new(fz_model* m, uint32_t max_ctx, int kv_dtype, fz_kv** out) {
     uint64_t per = (uint64_t)c.n_layers * m->nkv_l * max_ctx * c.head_dim * kv->eb;  // this rank's KV heads
     kv->k.alloc(per);
     kv->v.alloc(per);
-    CK(cudaMemset(kv->k.p, 0, per));
-    CK(cudaMemset(kv->v.p, 0, per));
+    // every user of the cache runs on the model's stream
+    CK(cudaMemsetAsync(kv->k.p, 0, per, m->stream));
+    CK(cudaMemsetAsync(kv->v.p, 0, per, m->stream));
     // RoPE factors with the reference's arithmetic (src/model.rs:207-210):
     // freq = theta^(-2i/hd), angle = pos * freq, (sin, cos) via libm.
     uint32_t half = c.head_dim / 2;
@@ -1191,9 +1390,9 @@ int fz_kv_new(fz_model* m, uint32_t max_ctx, int kv_dtype, fz_kv** out) {
     kv->partials.alloc(attention_partial_floats(m->nh_l, m->nkv_l, c.head_dim, kv->splits) * 4);
     // the split-padding entries of the accumulator block are never written
     // and must read as zero (they are weighted by 0 in the merge)
-    CK(cudaMemset(kv->partials.p, 0, kv->partials.n));
+    CK(cudaMemsetAsync(kv->partials.p, 0, kv->partials.n, m->stream));
     kv->state.alloc(sizeof(StepState));
-    CK(cudaMemset(kv->state.p, 0, sizeof(StepState)));
+    CK(cudaMemsetAsync(kv->state.p, 0, sizeof(StepState), m->stream));
     kv->forced.alloc((uint64_t)max_ctx * 4 + 16);
     kv->ids.alloc((uint64_t)max_ctx * 4 + 16);
     m->caches.push_back(kv.get());
@@ -1244,6 +1443,7 @@ int fz_kv_read(const fz_kv* kv, uint32_t layer, int which_v, uint32_t n, float* 
     const fz_config& c = kv->m->cfg;
     need(layer < c.n_layers && n <= kv->max_ctx, "kv read out of range");
     use_device(kv->m);
+    CK(cudaStreamSynchronize(kv->m->stream));  // the copies below run on the legacy stream
     uint32_t hd = c.head_dim;
     const uint32_t nkv = kv->m->nkv_l;  // this rank's KV heads
     const uint8_t* base = static_cast<const uint8_t*>(which_v ? kv->layer_v(layer, nkv, hd) : kv->layer_k(layer, nkv, hd));
@@ -1448,6 +1648,10 @@ int fz_step_profile(fz_model* m, fz_kv* kv, uint32_t first, uint32_t reps, doubl
     need((uint64_t)kv->len + reps <= kv->max_ctx, "context overflow: %u + %u > max_ctx %u", kv->len, reps, kv->max_ctx);
     use_device(m);
     cudaStream_t s = m->stream;
+    if (step_kernel_enabled(m)) {
+      step_profile_graph(m, kv, first, reps, ms, bytes, launches);
+      return;
+    }
     struct Hook : OpHook {
       std::vector<cudaEvent_t> ev;
       std::vector<int> ops;
@@ -1480,22 +1684,7 @@ int fz_step_profile(fz_model* m, fz_kv* kv, uint32_t first, uint32_t reps, doubl
       launches[hook.ops[i]] += 1;
     }
     check_state(kv);
-    // algorithmic bytes per op kind
-    const fz_config& c = m->cfg;
-    uint64_t H = c.hidden, F = m->sl.ffn_n, qd = m->qd_l, kd = m->kd_l;  // this rank's widths
-    for (uint32_t r = 0; r < reps; r++) {
-      uint64_t pos = kv->len + r;
-      bytes[FZ_OP_EMBED] += m->embd.gguf_bytes / c.vocab + H * 4;
-      for (auto& L : m->layers) {
-        bytes[FZ_OP_QKV] += L.wq.gguf_bytes + L.wk.gguf_bytes + L.wv.gguf_bytes + (2 * H + qd + 2 * kd) * 4;
-        bytes[FZ_OP_ROPE] += (qd + 2 * kd) * 4 + (qd + 2 * kd) * 4;
-        bytes[FZ_OP_ATTN] += 2 * (pos + 1) * kd * kv->eb + 2 * qd * 4;
-        bytes[FZ_OP_OPROJ] += L.wo.gguf_bytes + (qd + 2 * H) * 4;
-        bytes[FZ_OP_GATEUP] += L.wgu.gguf_bytes + (2 * H + F) * 4;
-        bytes[FZ_OP_DOWN] += L.wd.gguf_bytes + (F + 2 * H) * 4;
-      }
-      bytes[FZ_OP_LMHEAD] += m->lm_head.gguf_bytes + (2 * H + (uint64_t)c.vocab) * 4;
-    }
+    for (uint32_t r = 0; r < reps; r++) step_bytes(m, kv, kv->len + r, bytes);
     kv->len += reps;
   });
 }
