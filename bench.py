@@ -56,7 +56,8 @@ def parse():
     ap.add_argument("--config", default=CONFIG)
     ap.add_argument("--prefill", type=int, default=PREFILL)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel group size (divides --gpus)")
+    ap.add_argument("--tp", type=int, default=None,
+                    help="tensor-parallel group size (divides --gpus); default: the largest the model allows")
     ap.add_argument("--kv", default="f32", choices=["f32", "f16"],
                     help="KV cache elements (f32: the reference's; f16: the 32B config's 8K-context cache)")
     ap.add_argument("--layers", type=int, default=None,
@@ -224,22 +225,19 @@ def cpu_model() -> str:
     return "unknown"
 
 
-def cpu_baseline(path, vocab, budget_s=15.0):
-    """The reference path's CPU restatement (oracle/) on all host cores: a
-    short prefill, then decode tokens until ~budget_s of decode time."""
-    from furnace_b200 import synth
+def cpu_baseline(path, vocab, context, budget_s=15.0):
+    """The reference path's CPU restatement (oracle/) on all host cores,
+    decoding at the GPU arm's positions: the cache holds `context` positions
+    (seeded synthetic rows; a decode step's cost does not depend on the
+    cached values), then greedy decode tokens until ~budget_s of decode time."""
     from oracle import oracle
 
     cores = os.cpu_count() or 1
     oracle.set_threads(cores)
     m = oracle.Model(path)
-    ids = synth.prompt_ids(vocab, 8, seed=1)
-    kv = m.kv_new(64)
-    t0 = time.perf_counter()
-    lg = m.forward_cached(ids, kv)
-    prefill_s = time.perf_counter() - t0
-    n, dec = 0, 0.0
-    tok = int(lg.argmax())
+    kv = m.kv_new(context + 64)
+    kv.fill_synthetic(context, seed=1)
+    n, dec, tok = 0, 0.0, 1
     while n < 32 and (dec < budget_s or n < 2):
         t0 = time.perf_counter()
         lg = m.forward_cached([tok], kv)
@@ -248,12 +246,14 @@ def cpu_baseline(path, vocab, budget_s=15.0):
         n += 1
     m.close()
     return {"value": n / dec, "unit": "tok/s", "cores": cores, "kind": "port", "cpu": cpu_model(),
-            "sample": f"{n} greedy decode tokens after an 8-token prefill ({prefill_s:.1f} s) at context 8-{8 + n}, "
-                      f"same synthetic GGUF, oracle/ C++ restatement of the reference CPU path, {cores} threads"}
+            "sample": f"{n} greedy decode tokens at positions {context}-{context + n - 1} (context filled with "
+                      f"seeded synthetic K/V rows), same synthetic GGUF, oracle/ C++ restatement of the reference "
+                      f"CPU path, {cores} threads"}
 
 
 def run_reference(args, dist):
-    """--impl reference: the reference's CPU path (restated) on host cores."""
+    """--impl reference: the reference's CPU path (restated) on host cores, at
+    the GPU arm's context: positions prefill.. of the same model."""
     from furnace_b200 import synth
     from oracle import oracle
 
@@ -264,9 +264,9 @@ def run_reference(args, dist):
     cores = os.cpu_count() or 1
     oracle.set_threads(cores)
     m = oracle.Model(path)
-    ids = synth.prompt_ids(spec.vocab, 8, seed=1)
-    kv = m.kv_new(16 + args.warmup + args.steps)
-    tok = int(m.forward_cached(ids, kv).argmax())
+    kv = m.kv_new(args.prefill + args.warmup + args.steps + 16)
+    kv.fill_synthetic(args.prefill, seed=1)
+    tok = 1
     for _ in range(args.warmup):
         tok = int(m.forward_cached([tok], kv).argmax())
     t0 = time.perf_counter()
@@ -274,25 +274,40 @@ def run_reference(args, dist):
         tok = int(m.forward_cached([tok], kv).argmax())
     dt = time.perf_counter() - t0
     v = args.steps / dt
-    sample = (f"one greedy decode token per step (a sample of the {STEP_TOKENS}-token step) after an 8-token prefill, "
-              f"oracle/ C++ restatement of the reference CPU path (Rust toolchain absent), {cores} threads")
+    p0 = args.prefill + args.warmup
+    sample = (f"one greedy decode token per step (a sample of the {STEP_TOKENS}-token step) at positions "
+              f"{p0}-{p0 + args.steps - 1}, the {args.prefill}-position context filled with seeded synthetic K/V "
+              f"rows, oracle/ C++ restatement of the reference CPU path (Rust toolchain absent), {cores} threads")
     line = {"metric": "decode_tok_per_s", "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt * 1000 / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": f"{spec.name}: greedy decode tokens (batch 1), a CPU sample at context "
-                                   f"8-{8 + args.warmup + args.steps} of the {args.prefill}-token-prefill workload",
-                       "model": spec.name, "global_batch": 1, "seq_len": 8 + args.warmup + args.steps,
-                       "parallelism": f"cpu{cores}"},
+            "config": workload_config(spec, args, args.steps * STEP_TOKENS, f"cpu{cores}", 1),
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "cpu": cpu_model(),
                              "sample": sample},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args, dist):
-    import numpy as np
+def workload_config(spec, args, total_tokens, parallelism, groups):
+    """The workload both arms report (same keys and values but parallelism)."""
+    return {"workload": f"{spec.name}: {args.prefill}-token context, then greedy decode (batch 1) at positions "
+                        f"{args.prefill}..", "model": spec.name, "global_batch": groups,
+            "seq_len": args.prefill + total_tokens, "parallelism": parallelism,
+            "l2": "inputs larger than L2: the weights streamed per token exceed 126 MB", "kv": args.kv}
 
+
+def default_tp(world: int, spec) -> int:
+    """The largest tensor-parallel degree <= world that divides world and the
+    query and KV head counts: one group over every GPU when the model allows
+    it (strong scaling), else groups of that size side by side."""
+    for t in range(world, 0, -1):
+        if world % t == 0 and spec.n_heads % t == 0 and spec.n_kv_heads % t == 0:
+            return t
+    return 1
+
+
+def run_ours(args, dist):
     import furnace_b200 as fz
     from furnace_b200 import synth
 
@@ -306,7 +321,7 @@ def run_ours(args, dist):
     cud.set_device(dev)
     f = fz.GgufFile.open(path)
     # tensor-parallel groups of `tp` consecutive ranks (see the module docstring)
-    tp = max(1, min(args.tp, dist.world))
+    tp = default_tp(dist.world, spec) if args.tp is None else max(1, min(args.tp, dist.world))
     if dist.world % tp or spec.n_heads % tp or spec.n_kv_heads % tp:
         raise SystemExit(f"--tp {tp} must divide --gpus {dist.world} and the head counts")
     groups = dist.world // tp
@@ -349,6 +364,7 @@ def run_ours(args, dist):
     clocks = sampler.stop()
     ms = dist.max(ms)
     tok_s = total_tokens * groups / (ms / 1000.0)
+    ms_tok = ms / total_tokens
     # ---- e2e: public API, one call per step, host buffers ---------------
     kv.len = base
     dist.barrier()
@@ -361,39 +377,39 @@ def run_ours(args, dist):
     e2e = {"value": total_tokens * groups / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 + 32,
            "d2h_bytes_per_step": 4 * (T + 1) + 32,
            "note": "fz_decode_greedy per step; h2d = seed token + step state, d2h = ids + status"}
-    # ---- per-op timing of one step's kernels (roofline of the GEMV) -----
-    kv.len = base
+    # ---- where a token's time goes, and its algorithmic bytes ------------
+    # step kernel (FURNACE_B200_STEP=1): per-op spans from the kernel's own
+    # %globaltimer trace inside the captured step; per-kernel path: CUDA
+    # events around each launch outside the graph (serialised: shares only)
+    kv.len = base + total_tokens // 2  # mid-decode position, as the timed region's mean
     prof = model.step_profile(first, T, kv)
-    gemv_ops = ["qkv", "o_proj", "gate_up", "down", "lm_head"]
-    g_ms = sum(prof[o][0] for o in gemv_ops)
-    g_b = sum(prof[o][1] for o in gemv_ops)
-    g_n = sum(prof[o][2] for o in gemv_ops)
+    in_graph = os.environ.get("FURNACE_B200_STEP", "") == "1" and tp == 1
+    bytes_tok = sum(v[1] for v in prof.values()) / T  # weights, KV rows read, vectors
     peak, peak_src = measured_peaks()
-    achieved = (g_b / g_n) / (g_ms / g_n / 1000.0) / 1e9
+    achieved = bytes_tok / (ms_tok / 1000.0) / 1e9
+    prof_ms = sum(v[0] for v in prof.values())
+    ops = {o: {"ms_per_token": prof[o][0] / T, "share": prof[o][0] / prof_ms if prof_ms else None,
+               "gbs": (prof[o][1] / (prof[o][0] / 1000.0) / 1e9) if prof[o][0] else None} for o in prof}
     traffic = ncu_traffic()
-    roofline = {"kernel": "k_gemv (all GEMV launches of a decode step)", "bound": "hbm", "achieved": achieved,
-                "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_src} hbm_gbs",
-                "bytes_per_launch": g_b / g_n, "avg_launch_us": g_ms / g_n * 1000,
+    kernel = ("k_step (persistent decode step: every GEMV, attention and lm_head of a token in one launch)"
+              if in_graph else "decode step (per-kernel path: 6 launches per layer + lm_head)")
+    roofline = {"kernel": kernel, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_source": f"{peak_src} hbm_gbs (burst copy)",
+                "bytes_per_launch": bytes_tok, "launch_us": ms_tok * 1000.0,
+                "how": "algorithmic bytes of one token (GGUF weight bytes of every matrix, the KV rows read at the "
+                       "timed region's mean position, vectors) / the device-timed ms per token of the timed region",
                 "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
                 "traffic_source": traffic.get("source") if traffic else None}
-    step_ms_sum = sum(v[0] for v in prof.values())
-    ops = {o: {"ms_per_token": prof[o][0] / T, "share": prof[o][0] / step_ms_sum,
-               "gbs": (prof[o][1] / (prof[o][0] / 1000.0) / 1e9) if prof[o][0] else None} for o in prof}
     hbm = per_tok * tok_s / groups / 1e9  # this rank's weight bytes per token x the group's token rate
-    launches_per_token = 6 * cfg.n_layers + 3
     out = {
         "metric": "decode_tok_per_s", "value": tok_s, "unit": "tok/s", "n_gpus": dist.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "strong" if groups == 1 else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{spec.name}: {args.prefill}-token prefill then {total_tokens} greedy decode tokens "
-                               f"(batch 1), {T} tokens per step", "model": spec.name, "global_batch": groups,
-                   "seq_len": args.prefill + total_tokens,
-                   "parallelism": f"tp{tp}" + (f"x{groups}" if groups > 1 else ""),
-                   "l2": "inputs larger than L2: %.2f GB of weights streamed per token" % (per_tok / 1e9),
-                   "kv": args.kv},
+        "config": workload_config(spec, args, total_tokens, f"tp{tp}" + (f"x{groups}" if groups > 1 else ""),
+                                  groups),
         "hbm_gbs_per_gpu": hbm, "hbm_frac_of_8tbs": hbm / 8000.0, "hbm_frac_of_measured": hbm / peak,
-        "bytes_per_token": per_tok, "ms_per_token": ms / total_tokens, "prefill_s": prefill_s,
+        "bytes_per_token": per_tok, "ms_per_token": ms_tok, "prefill_s": prefill_s,
         "load": {"s": load_s, "gb": resident / 1e9,
                  "note": "host wall clock of fz_model_load(_tp): GGUF bytes of this rank's share from the "
                          "page cache to the device and the repack into the chunk layout"},
@@ -403,11 +419,12 @@ def run_ours(args, dist):
                     if args.prefill > 8 else "decode step per token",
                     "note": "host wall clock of fz_forward over the prompt, including the per-layer weight "
                             "dequantization into GEMM panels"},
-        "gpu_launches": launches_per_token * total_tokens, "clocks": clocks, "e2e": e2e, "roofline": roofline,
-        "ops": ops,
+        "gpu_launches": (3 if in_graph else 6 * cfg.n_layers + 3) * total_tokens, "clocks": clocks, "e2e": e2e,
+        "roofline": roofline,
+        "ops": ops, "ops_timing": "in-graph %globaltimer spans" if in_graph else "CUDA events per launch, serialised",
     }
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(path, cfg.vocab)
+        out["cpu_baseline"] = cpu_baseline(path, cfg.vocab, base)
     if dist.rank == 0:
         print(json.dumps(out), flush=True)
     kv.close()

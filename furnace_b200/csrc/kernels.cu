@@ -1683,7 +1683,10 @@ struct StepKernel {
   size_t smem = 0;
 };
 
-constexpr uint32_t MK_STAGE_MAX = 48 * 1024;  // bytes of one ring stage at most
+#ifndef MK_STAGE_KB
+#define MK_STAGE_KB 48
+#endif
+constexpr uint32_t MK_STAGE_MAX = MK_STAGE_KB * 1024;  // bytes of one ring stage at most
 
 uint32_t step_grid() { return (uint32_t)num_sms(); }
 uint32_t step_splits(uint32_t n_kv) {
@@ -1758,7 +1761,7 @@ StepKernel* step_kernel_build(const std::vector<StepPhaseDesc>& d, const StepGlo
         const uint32_t n = s.cta_end - s.cta_begin, units = s.rows / s.align;
         m.max_rows = std::max(m.max_rows, s.align * ((units + n - 1) / n) + s.align);
       }
-      m.rs = std::min<uint32_t>(GV_ROWS, MK_STAGE_MAX / tmax);
+      m.rs = std::min<uint32_t>(MK_ROWS, MK_STAGE_MAX / tmax);
       if (m.rs == 0) fail(FZ_EINVAL, "step kernel: a %u-byte row tile exceeds a ring stage", tmax);
       acc = std::max(acc, m.max_rows);
     } else {
@@ -1851,20 +1854,22 @@ void prefill_init() {
 uint64_t wpanel_elems(uint32_t rows, uint32_t K) { return (uint64_t)((rows + QG_M - 1) / QG_M) * QG_M * K; }
 uint64_t xpanel_elems(uint32_t T, uint32_t K) { return (uint64_t)((T + QG_N - 1) / QG_N) * QG_N * K; }
 
-void launch_wpanels(const DevMat& m, uint32_t row0, void* hi, void* lo, cudaStream_t s) {
+void launch_wpanels(const DevMat& m, uint32_t row0, int8_t* rexp, void* hi, void* lo, cudaStream_t s) {
   if (m.cols % 64) fail(FZ_EINVAL, "prefill: %u columns not a multiple of 64", m.cols);
+  k_rowexp<<<(m.rows * 32 + 255) / 256, 256, 0, s>>>(m, row0, rexp);
+  CK(cudaGetLastError());
   const uint64_t n = (uint64_t)m.rows * (m.cols / 64);
-  k_wpanels<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(m, row0, reinterpret_cast<__half*>(hi),
+  k_wpanels<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(m, row0, rexp, reinterpret_cast<__half*>(hi),
                                                         reinterpret_cast<__half*>(lo));
   CK(cudaGetLastError());
 }
 
 void launch_xpanels(const float* x, uint32_t ld, uint32_t T, uint32_t K, const float* w, float eps, void* hi,
-                    void* lo, cudaStream_t s) {
+                    void* lo, int8_t* texp, cudaStream_t s) {
   if (K % 64) fail(FZ_EINVAL, "prefill: width %u not a multiple of 64", K);
   if (ld % 4) fail(FZ_EINVAL, "prefill: row stride %u not a multiple of 4", ld);
   k_xpanels<<<(T + XP_TOK - 1) / XP_TOK, 256, 0, s>>>(x, ld, T, K, w, eps, reinterpret_cast<__half*>(hi),
-                                                      reinterpret_cast<__half*>(lo));
+                                                      reinterpret_cast<__half*>(lo), texp);
   CK(cudaGetLastError());
 }
 
@@ -1883,6 +1888,9 @@ void launch_qgemm(const QgemmLaunch& q, cudaStream_t s) {
   p.ld = q.ld;
   p.bias = q.bias;
   p.err = q.err;
+  p.rexp = q.rexp;
+  p.texp = q.texp;
+  if (!q.rexp || !q.texp) fail(FZ_EINVAL, "prefill gemm: missing row / token exponents");
   dim3 grid((q.T + QG_N - 1) / QG_N, (q.N + QG_M - 1) / QG_M);
   if (grid.y > 65535) fail(FZ_EINVAL, "prefill gemm: %u output rows", q.N);
   k_qgemm<<<grid, 128, QG_SMEM, s>>>(p);

@@ -183,6 +183,7 @@ enum PrefillEpilogue : int { PE_STORE = 0, PE_RESID = 1, PE_SWIGLU = 2 };
 struct QgemmLaunch {
   const void *ahi, *alo;  // weight panels (launch_wpanels)
   const void *bhi, *blo;  // token panels (launch_xpanels)
+  const int8_t *rexp, *texp;  // their power-of-two row / token exponents
   uint32_t K, N, T;
   int epi;                // PE_*: out[t*ld + r] (+ bias[r]); += ; SwiGLU into out[t*ld + r/2]
   float* out;
@@ -193,9 +194,10 @@ struct QgemmLaunch {
 void prefill_init();
 uint64_t wpanel_elems(uint32_t rows, uint32_t K);  // fp16 elements of one weight panel set
 uint64_t xpanel_elems(uint32_t T, uint32_t K);
-void launch_wpanels(const DevMat& m, uint32_t row0, void* hi, void* lo, cudaStream_t s);
+// rexp: one int8 exponent per panel row (rows padded to 128, padding zero)
+void launch_wpanels(const DevMat& m, uint32_t row0, int8_t* rexp, void* hi, void* lo, cudaStream_t s);
 void launch_xpanels(const float* x, uint32_t ld, uint32_t T, uint32_t K, const float* w, float eps, void* hi,
-                    void* lo, cudaStream_t s);
+                    void* lo, int8_t* texp, cudaStream_t s);
 void launch_qgemm(const QgemmLaunch& q, cudaStream_t s);
 void launch_embed_rows(const DevMat& emb, const uint32_t* tokens, uint32_t T, float* x, uint32_t ld, cudaStream_t s);
 void launch_prefill_attention(const float* qkv, uint32_t ldq, const float* rope_cs, void* kc, void* vc, bool kv_f16,

@@ -30,6 +30,12 @@ const NcclApi& nccl() {
     api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(sym("ncclAllReduce"));
     api.AllGather = reinterpret_cast<decltype(api.AllGather)>(sym("ncclAllGather"));
     api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(sym("ncclGetErrorString"));
+    // optional: a communicator that does not block its caller (init can time out)
+    api.CommInitRankConfig = reinterpret_cast<decltype(api.CommInitRankConfig)>(dlsym(h, "ncclCommInitRankConfig"));
+    api.CommGetAsyncError = reinterpret_cast<decltype(api.CommGetAsyncError)>(dlsym(h, "ncclCommGetAsyncError"));
+    api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(dlsym(h, "ncclCommAbort"));
+    if (!api.CommInitRankConfig || !api.CommGetAsyncError || !api.CommAbort)
+      api.CommInitRankConfig = nullptr;
   });
   if (err) fail(FZ_ECUDA, "%s", err);
   return api;

@@ -38,6 +38,37 @@ __host__ __device__ __forceinline__ uint32_t panel_elem(uint32_t P, uint32_t rr,
   return ((k >> 3) * (P >> 3) + (rr >> 3)) * 64 + (rr & 7) * 8 + (k & 7);  // in fp16 elements
 }
 
+// Power-of-two scaling of the fp16 split: every weight row and every token
+// row is multiplied by 2^e before the split, with e chosen from the row's
+// largest magnitude so that it lands in [2^13, 2^14): no element overflows
+// fp16 (|x| > 65504 would become inf) and small rows keep the split's full
+// precision instead of falling into fp16 subnormals.  The GEMM epilogue
+// multiplies by 2^-(e_row + e_token).  Power-of-two scaling is exact.
+__device__ __forceinline__ int pow2_exp(float amax) {
+  if (!(amax > 0.f) || !isfinite(amax)) return 0;
+  int ex;
+  frexpf(amax, &ex);  // amax in [2^(ex-1), 2^ex)
+  return min(max(14 - ex, -100), 100);
+}
+__device__ __forceinline__ float exp2i(int e) { return __int_as_float((127 + e) << 23); }  // e in [-126, 127]
+
+// Row exponents of weight rows [0, m.rows), stored at rexp[row0 + r]: one
+// warp per row dequantizes it (dequant_unit) and takes the largest magnitude.
+__global__ void k_rowexp(DevMat m, uint32_t row0, int8_t* __restrict__ rexp) {
+  const uint32_t row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (row >= m.rows) return;  // warp-uniform
+  float amax = 0.f;
+  for (uint32_t u = lane; u < m.cols / 64; u += 32) {
+    float v[64];
+    dequant_unit(m.dtype, m.ptr, m.rows, row, m.cols, u, v);
+#pragma unroll
+    for (int i = 0; i < 64; i++) amax = fmaxf(amax, fabsf(v[i]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (lane == 0) rexp[row0 + row] = (int8_t)pow2_exp(amax);
+}
+
 __device__ __forceinline__ void split16(float v, __half* hi, __half* lo) {
   const __half h = __float2half_rn(v);
   *hi = h;
@@ -52,7 +83,8 @@ __device__ __forceinline__ uint32_t half2_bits(__half a, __half b) {
 // K = m.cols columns.  One thread per (row, 64-column unit), rows fastest:
 // the 8 elements of a core-matrix row are one 16-byte store, and a warp's
 // 32 rows of one core-matrix column are 512 contiguous bytes.
-__global__ void k_wpanels(DevMat m, uint32_t row0, __half* __restrict__ hi, __half* __restrict__ lo) {
+__global__ void k_wpanels(DevMat m, uint32_t row0, const int8_t* __restrict__ rexp, __half* __restrict__ hi,
+                          __half* __restrict__ lo) {
   const uint32_t U = m.cols / 64;
   const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (uint64_t)m.rows * U) return;
@@ -60,6 +92,9 @@ __global__ void k_wpanels(DevMat m, uint32_t row0, __half* __restrict__ hi, __ha
   float v[64];
   dequant_unit(m.dtype, m.ptr, m.rows, r, m.cols, u, v);
   const uint32_t R = row0 + r;
+  const float sc = exp2i(rexp[R]);
+#pragma unroll
+  for (int i = 0; i < 64; i++) v[i] = __fmul_rn(v[i], sc);
   const uint64_t pbase = ((uint64_t)(R / QG_M) * U + u) * (QG_M * QG_KB);
 #pragma unroll
   for (uint32_t kc = 0; kc < 8; kc++) {
@@ -88,18 +123,33 @@ __global__ void k_wpanels(DevMat m, uint32_t row0, __half* __restrict__ hi, __ha
 constexpr uint32_t XP_TOK = 8;
 __global__ void __launch_bounds__(256) k_xpanels(const float* __restrict__ x, uint32_t ld, uint32_t T, uint32_t K,
                                                  const float* __restrict__ w, float eps, __half* __restrict__ hi,
-                                                 __half* __restrict__ lo) {
+                                                 __half* __restrict__ lo, int8_t* __restrict__ texp) {
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, tb0 = blockIdx.x * XP_TOK;
-  __shared__ float inv_s[XP_TOK];
-  if (w) {
+  __shared__ float inv_s[XP_TOK], sc_s[XP_TOK];
+  {
+    // warp i: token tb0 + i's sum of squares (RMSNorm) and largest |x * w|
     const uint32_t t = tb0 + warp;
-    float ss = 0.f;
+    float ss = 0.f, amax = 0.f;
     if (t < T) {
       const float* row = x + (uint64_t)t * ld;
-      for (uint32_t k = lane; k < K; k += 32) ss = fmaf(row[k], row[k], ss);
+      for (uint32_t k = lane; k < K; k += 32) {
+        const float v = row[k];
+        ss = fmaf(v, v, ss);
+        amax = fmaxf(amax, fabsf(w ? v * w[k] : v));
+      }
     }
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) inv_s[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
+    for (int o = 16; o > 0; o >>= 1) {
+      ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    }
+    if (lane == 0) {
+      const float inv = w ? __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps))) : 1.0f;
+      // the normalised values are (x * inv) * w: at most inv * amax up to rounding
+      const int e = pow2_exp(inv * amax * 1.0001f);
+      inv_s[warp] = inv;
+      sc_s[warp] = exp2i(e);
+      if (t < T) texp[t] = (int8_t)e;
+    }
     __syncthreads();
   }
   const uint32_t U = K / 64, nk8 = K / 8;
@@ -114,6 +164,9 @@ __global__ void __launch_bounds__(256) k_xpanels(const float* __restrict__ x, ui
 #pragma unroll
       for (int j = 0; j < 8; j++) v[j] = __fmul_rn(__fmul_rn(v[j], inv), w[k0 + j]);
     }
+    const float sc = sc_s[i];
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = __fmul_rn(v[j], sc);
     uint32_t h[4], l[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
@@ -179,6 +232,8 @@ struct QgParams {
   uint32_t ld;
   const float* bias;  // STORE: + bias[r]
   uint32_t* err;      // set nonzero if a bounded wait ran out
+  const int8_t* rexp;  // power-of-two exponents of the weight rows [Np] and
+  const int8_t* texp;  //   of the token rows [T] applied before the fp16 split
 };
 
 // Y^T tile [128 weight rows x 256 tokens] of one CTA.  Warp 0 lane 0 copies
@@ -268,6 +323,7 @@ __global__ void __launch_bounds__(128, 1) k_qgemm(const __grid_constant__ QgPara
   if (!ok && threadIdx.x == 0) atomicExch(p.err, 1u);
   tc_fence_after();
   const uint32_t r = rb * QG_M + warp * 32 + lane;
+  const float rsc = exp2i(-(int)p.rexp[r]);  // rows past N are zero-padded: their exponent is 0
   if (ok) {
     const uint32_t lanebase = (warp * 32) << 16;
     for (uint32_t c = 0; c < QG_N; c += 8) {
@@ -277,7 +333,9 @@ __global__ void __launch_bounds__(128, 1) k_qgemm(const __grid_constant__ QgPara
 #pragma unroll
       for (int j = 0; j < 8; j++) {
         const uint32_t t = tb * QG_N + c + j;
-        const float y = __fadd_rn(a1[j], __fmul_rn(a2[j], 1.0f / QG_LO));
+        // undo the row and token scaling (exact powers of two)
+        const float y = __fmul_rn(__fmul_rn(__fadd_rn(a1[j], __fmul_rn(a2[j], 1.0f / QG_LO)), rsc),
+                                  exp2i(-(int)p.texp[min(t, p.T - 1)]));
         if (p.epi == QE_SWIGLU) {
           // rows interleave gate (even) / up (odd): h = silu(g) * u (src/tensor.rs:213-227)
           const float other = __shfl_xor_sync(0xffffffffu, y, 1);

@@ -4,6 +4,9 @@
 
 #include <cuda_runtime.h>
 
+#include <chrono>
+#include <thread>
+
 #include <algorithm>
 #include <cmath>
 #include <cstdarg>
@@ -106,6 +109,7 @@ struct fz_model {
   // fp16 hi/lo panels of one weight and of one activation matrix
   uint32_t pf_cap = 0;
   DevBuf pf_x, pf_qkv, pf_ctx, pf_h, pf_tok, pf_err, pf_wh, pf_wl, pf_xh, pf_xl;
+  DevBuf pf_rexp, pf_texp;  // power-of-two exponents of the panel rows / token rows
   DevBuf smp_scratch, smp_out;  // device top-k of the sampler
   // the caches made for this model: fz_model_free releases their device
   // memory and detaches them, so they may be freed before or after it
@@ -208,6 +212,45 @@ fz_tp_slice tp_slice(const fz_config& c, int r, int T) {
 }
 
 void nccl_check(ncclResult_t r, const char* what) {
+  if (r != ncclSuccess) fail(FZ_ECUDA, "%s failed: %s", what, nccl().GetErrorString(r));
+}
+
+// Seconds a communicator call may make no progress (a peer that never joins,
+// or stops taking part) before the communicator is aborted and the call
+// fails with FZ_ETIMEOUT: FURNACE_B200_NCCL_TIMEOUT_S, default 300.
+double nccl_timeout_s() {
+  const char* e = getenv("FURNACE_B200_NCCL_TIMEOUT_S");
+  const double v = e ? atof(e) : 0.0;
+  return v > 0 ? v : 300.0;
+}
+
+// The result of a call on a (possibly non-blocking) communicator: while it
+// reports ncclInProgress, poll ncclCommGetAsyncError; past the time limit,
+// ncclCommAbort it (*comm becomes null) and fail with FZ_ETIMEOUT.
+void nccl_comm_check(ncclComm_t* comm, ncclResult_t r, const char* what) {
+  if (r == ncclInProgress && nccl().CommGetAsyncError) {
+    const auto t0 = std::chrono::steady_clock::now();
+    const double lim = nccl_timeout_s();
+    for (;;) {
+      ncclResult_t st = ncclSuccess;
+      const ncclResult_t q = nccl().CommGetAsyncError(*comm, &st);
+      if (q != ncclSuccess) {
+        r = q;
+        break;
+      }
+      if (st != ncclInProgress) {
+        r = st;
+        break;
+      }
+      if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > lim) {
+        nccl().CommAbort(*comm);
+        *comm = nullptr;
+        fail(FZ_ETIMEOUT, "%s: no progress within %.0f s (a peer did not take part); communicator aborted", what,
+             lim);
+      }
+      std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+  }
   if (r != ncclSuccess) fail(FZ_ECUDA, "%s failed: %s", what, nccl().GetErrorString(r));
 }
 
@@ -356,7 +399,8 @@ AttnLaunch layer_attention(fz_kv* kv, uint32_t li, uint32_t splits) {
 // export its buffer, or FURNACE_B200_TP_ALLREDUCE=nccl): ncclAllReduce.
 void tp_allreduce_x(fz_model* m, cudaStream_t s) {
   if (m->world == 1 || m->ar_p2p) return;
-  nccl_check(nccl().AllReduce(m->x.p, m->x.p, m->cfg.hidden, ncclFloat32, ncclSum, m->comm, s), "ncclAllReduce");
+  nccl_comm_check(&m->comm, nccl().AllReduce(m->x.p, m->x.p, m->cfg.hidden, ncclFloat32, ncclSum, m->comm, s),
+                  "ncclAllReduce");
 }
 
 // One step as separate kernels (programmatic dependent launches): the path
@@ -403,7 +447,7 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
     // greedy pick over all ranks' vocabulary slices: max of the packed
     // (logit, index) keys, which prefers the first index on ties
     if (m->world > 1)
-      nccl_check(nccl().AllReduce(&st->argmax_key, &st->argmax_key, 1, ncclUint64, ncclMax, m->comm, s),
+      nccl_comm_check(&m->comm, nccl().AllReduce(&st->argmax_key, &st->argmax_key, 1, ncclUint64, ncclMax, m->comm, s),
                  "ncclAllReduce");
     H(FZ_OP_LMHEAD, false);
   }
@@ -512,12 +556,13 @@ void prefill_alloc(fz_model* m, uint32_t T) {
   const fz_config& c = m->cfg;
   const uint32_t H = c.hidden, F = c.ffn, qd = m->qd_l, kd = m->kd_l;
   const uint32_t maxK = std::max(std::max(H, F), std::max(qd, m->o_w));
-  uint64_t wmax = 0;
+  uint64_t wmax = 0, rmax = 0;
   for (auto& L : m->layers) {
     wmax = std::max(wmax, wpanel_elems(L.wq.rows + L.wk.rows + L.wv.rows, H));
     wmax = std::max(wmax, wpanel_elems(L.wo.rows, L.wo.cols));
     wmax = std::max(wmax, wpanel_elems(L.wgu.rows, H));
     wmax = std::max(wmax, wpanel_elems(L.wd.rows, L.wd.cols));
+    rmax = std::max<uint64_t>(rmax, std::max({L.wq.rows + L.wk.rows + L.wv.rows, L.wo.rows, L.wgu.rows, L.wd.rows}));
   }
   m->pf_x.alloc((uint64_t)T * H * 4);
   m->pf_qkv.alloc((uint64_t)T * (qd + 2 * kd) * 4);
@@ -539,6 +584,10 @@ void prefill_alloc(fz_model* m, uint32_t T) {
   CK(cudaMemsetAsync(m->pf_xh.p, 0, m->pf_xh.n, m->stream));
   CK(cudaMemsetAsync(m->pf_xl.p, 0, m->pf_xl.n, m->stream));
   CK(cudaMemsetAsync(m->pf_err.p, 0, 16, m->stream));
+  m->pf_rexp.alloc((rmax + 127) / 128 * 128);
+  m->pf_texp.alloc(T + 16);
+  CK(cudaMemsetAsync(m->pf_rexp.p, 0, m->pf_rexp.n, m->stream));
+  CK(cudaMemsetAsync(m->pf_texp.p, 0, m->pf_texp.n, m->stream));
   m->pf_cap = T;
 }
 
@@ -565,7 +614,8 @@ void prefill_tokens(fz_kv* kv, const uint32_t* tokens, uint32_t n, uint32_t pos0
   float* ctx = m->pf_ctx.as<float>();
   uint32_t* err = m->pf_err.as<uint32_t>();
   auto gemm = [&](uint32_t K, uint32_t N, uint32_t T, int epi, float* out, uint32_t ld, const float* bias) {
-    QgemmLaunch q{m->pf_wh.p, m->pf_wl.p, m->pf_xh.p, m->pf_xl.p, K, N, T, epi, out, ld, bias, err};
+    QgemmLaunch q{m->pf_wh.p, m->pf_wl.p, m->pf_xh.p, m->pf_xl.p, m->pf_rexp.as<int8_t>(), m->pf_texp.as<int8_t>(),
+                  K, N, T, epi, out, ld, bias, err};
     launch_qgemm(q, s);
   };
   // x += the [T, K] activations (panels built) times w (panels built), summed over ranks
@@ -573,7 +623,8 @@ void prefill_tokens(fz_kv* kv, const uint32_t* tokens, uint32_t n, uint32_t pos0
     if (m->world > 1 && m->rank != 0) CK(cudaMemsetAsync(X, 0, (size_t)T * H * 4, s));
     gemm(K, H, T, PE_RESID, X, H, nullptr);
     if (m->world > 1)
-      nccl_check(nccl().AllReduce(X, X, (size_t)T * H, ncclFloat32, ncclSum, m->comm, s), "ncclAllReduce");
+      nccl_comm_check(&m->comm, nccl().AllReduce(X, X, (size_t)T * H, ncclFloat32, ncclSum, m->comm, s),
+                      "ncclAllReduce");
   };
   for (uint32_t c0 = 0; c0 < n; c0 += PF_CHUNK) {
     const uint32_t T = std::min(PF_CHUNK, n - c0);
@@ -583,10 +634,10 @@ void prefill_tokens(fz_kv* kv, const uint32_t* tokens, uint32_t n, uint32_t pos0
       Layer& L = m->layers[li];
       const uint32_t F_l = L.wd.cols;
       // q, k, v (+ bias) of RMSNorm(x)
-      launch_xpanels(X, H, T, H, L.attn_norm, c.rms_eps, m->pf_xh.p, m->pf_xl.p, s);
-      launch_wpanels(L.wq, 0, m->pf_wh.p, m->pf_wl.p, s);
-      launch_wpanels(L.wk, L.wq.rows, m->pf_wh.p, m->pf_wl.p, s);
-      launch_wpanels(L.wv, L.wq.rows + L.wk.rows, m->pf_wh.p, m->pf_wl.p, s);
+      launch_xpanels(X, H, T, H, L.attn_norm, c.rms_eps, m->pf_xh.p, m->pf_xl.p, m->pf_texp.as<int8_t>(), s);
+      launch_wpanels(L.wq, 0, m->pf_rexp.as<int8_t>(), m->pf_wh.p, m->pf_wl.p, s);
+      launch_wpanels(L.wk, L.wq.rows, m->pf_rexp.as<int8_t>(), m->pf_wh.p, m->pf_wl.p, s);
+      launch_wpanels(L.wv, L.wq.rows + L.wk.rows, m->pf_rexp.as<int8_t>(), m->pf_wh.p, m->pf_wl.p, s);
       gemm(H, ldq, T, PE_STORE, m->pf_qkv.as<float>(), ldq, L.bqkv);
       // rotated k / v into the cache, causal attention per token
       if (L.wo.cols != qd) CK(cudaMemsetAsync(ctx, 0, (size_t)T * ldc * 4, s));
@@ -594,15 +645,15 @@ void prefill_tokens(fz_kv* kv, const uint32_t* tokens, uint32_t n, uint32_t pos0
                                kv->layer_v(li, m->nkv_l, hd), kv->eb == 2, ctx + m->o_off[li], ldc, m->nh_l,
                                m->nkv_l, hd, kv->max_ctx, pos0 + c0, T, err, s);
       // x += o_proj(ctx)
-      launch_xpanels(ctx, ldc, T, L.wo.cols, nullptr, 0.f, m->pf_xh.p, m->pf_xl.p, s);
-      launch_wpanels(L.wo, 0, m->pf_wh.p, m->pf_wl.p, s);
+      launch_xpanels(ctx, ldc, T, L.wo.cols, nullptr, 0.f, m->pf_xh.p, m->pf_xl.p, m->pf_texp.as<int8_t>(), s);
+      launch_wpanels(L.wo, 0, m->pf_rexp.as<int8_t>(), m->pf_wh.p, m->pf_wl.p, s);
       resid(L.wo.cols, T);
       // h = swiglu(gate, up)(RMSNorm(x)); x += down(h)
-      launch_xpanels(X, H, T, H, L.ffn_norm, c.rms_eps, m->pf_xh.p, m->pf_xl.p, s);
-      launch_wpanels(L.wgu, 0, m->pf_wh.p, m->pf_wl.p, s);
+      launch_xpanels(X, H, T, H, L.ffn_norm, c.rms_eps, m->pf_xh.p, m->pf_xl.p, m->pf_texp.as<int8_t>(), s);
+      launch_wpanels(L.wgu, 0, m->pf_rexp.as<int8_t>(), m->pf_wh.p, m->pf_wl.p, s);
       gemm(H, L.wgu.rows, T, PE_SWIGLU, m->pf_h.as<float>(), F_l, nullptr);
-      launch_xpanels(m->pf_h.as<float>(), F_l, T, F_l, nullptr, 0.f, m->pf_xh.p, m->pf_xl.p, s);
-      launch_wpanels(L.wd, 0, m->pf_wh.p, m->pf_wl.p, s);
+      launch_xpanels(m->pf_h.as<float>(), F_l, T, F_l, nullptr, 0.f, m->pf_xh.p, m->pf_xl.p, m->pf_texp.as<int8_t>(), s);
+      launch_wpanels(L.wd, 0, m->pf_rexp.as<int8_t>(), m->pf_wh.p, m->pf_wl.p, s);
       resid(F_l, T);
     }
   }
@@ -751,7 +802,8 @@ void tp_gather_logits(fz_model* m, cudaStream_t s) {
   if (m->world == 1) return;
   const size_t per = m->sl.vocab_pad / m->world;
   float* all = m->logits.as<float>();
-  nccl_check(nccl().AllGather(all + (size_t)m->rank * per, all, per, ncclFloat32, m->comm, s), "ncclAllGather");
+  nccl_comm_check(&m->comm, nccl().AllGather(all + (size_t)m->rank * per, all, per, ncclFloat32, m->comm, s),
+                  "ncclAllGather");
 }
 
 // IEEE binary16 -> binary32, exact (cached f16 KV elements read back).
@@ -833,7 +885,7 @@ void step_profile_graph(fz_model* m, fz_kv* kv, uint32_t first, uint32_t reps, d
   cudaStream_t s = m->stream;
   build_graphs(kv);
   const uint32_t nph = step_kernel_phases(kv->mk_full), grid = step_grid(), L = m->cfg.n_layers;
-  const uint64_t cap = (uint64_t)reps * nph * grid + 64;
+  const uint64_t cap = 2ull * reps * nph * grid + 64;  // consumer and producer records
   DevBuf tb(cap * sizeof(TraceRec));
   trace_install(tb.as<TraceRec>(), (uint32_t)cap);
   struct Restore {
@@ -865,15 +917,20 @@ void step_profile_graph(fz_model* m, fz_kv* kv, uint32_t first, uint32_t reps, d
   const uint32_t n = std::min<uint32_t>(trace_count(), (uint32_t)cap);
   std::vector<TraceRec> rec(n);
   if (n) CK(cudaMemcpy(rec.data(), tb.p, (size_t)n * sizeof(TraceRec), cudaMemcpyDeviceToHost));
-  need(n == (uint64_t)reps * nph * grid, "step trace: %u records, expected %llu", n,
+  // consumer records (tags TR_STEP + 0..4; the producer's are TR_STEP + 8):
+  // nph * grid per token, tokens in launch order (kernel boundaries order
+  // them); inside one token, aux is the phase index
+  std::vector<const TraceRec*> cons;
+  cons.reserve(n);
+  for (uint32_t i = 0; i < n; i++)
+    if (rec[i].tag >= TR_STEP && rec[i].tag < TR_STEP + 8) cons.push_back(&rec[i]);
+  need(cons.size() == (uint64_t)reps * nph * grid, "step trace: %zu records, expected %llu", cons.size(),
        (unsigned long long)reps * nph * grid);
-  // records of token r are [r * nph * grid, (r + 1) * nph * grid): kernel
-  // boundaries order the tokens; inside one, aux is the phase index
   double span_ms = 0;
   for (uint32_t r = 0; r < reps; r++) {
     std::vector<uint64_t> t0(nph, ~0ull), t4(nph, 0);
     for (uint64_t i = (uint64_t)r * nph * grid; i < (uint64_t)(r + 1) * nph * grid; i++) {
-      const TraceRec& x = rec[i];
+      const TraceRec& x = *cons[i];
       need(x.aux < nph, "step trace: bad phase index");
       t0[x.aux] = std::min(t0[x.aux], x.t[0]);
       t4[x.aux] = std::max(t4[x.aux], x.t[4]);
@@ -1028,7 +1085,7 @@ void tp_p2p_setup(fz_model* m) {
   mine[64] = ok ? 1 : 0;
   DevBuf d(72ull * W);
   CK(cudaMemcpy(d.as<uint8_t>() + 72ull * m->rank, mine.data(), 72, cudaMemcpyHostToDevice));
-  nccl_check(nccl().AllGather(d.as<uint8_t>() + 72ull * m->rank, d.p, 72, ncclUint8, m->comm, m->stream),
+  nccl_comm_check(&m->comm, nccl().AllGather(d.as<uint8_t>() + 72ull * m->rank, d.p, 72, ncclUint8, m->comm, m->stream),
              "ncclAllGather");
   CK(cudaStreamSynchronize(m->stream));
   CK(cudaMemcpy(all.data(), d.p, all.size(), cudaMemcpyDeviceToHost));
@@ -1240,7 +1297,15 @@ std::unique_ptr<fz_model> load_model(const fz_file* f, int rank, int world, cons
   m->streamed = per_tok;
   if (world > 1) {
     need(id != nullptr, "tensor parallelism needs an NCCL id");
-    nccl_check(nccl().CommInitRank(&m->comm, world, *id, rank), "ncclCommInitRank");
+    if (nccl().CommInitRankConfig) {
+      // non-blocking: a peer that never joins ends in FZ_ETIMEOUT, not a hang
+      ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+      cfg.blocking = 0;
+      nccl_comm_check(&m->comm, nccl().CommInitRankConfig(&m->comm, world, *id, rank, &cfg),
+                      "ncclCommInitRankConfig");
+    } else {
+      nccl_check(nccl().CommInitRank(&m->comm, world, *id, rank), "ncclCommInitRank");
+    }
     tp_p2p_setup(m.get());
   }
   // optional timeline of every decode-step kernel's CTAs, written to the named
@@ -1728,11 +1793,12 @@ int fz_matmul_quant_dev(const fz_weight* w, const float* a_dev, uint32_t seq, fl
       const uint32_t rows = w->m.rows, cols = w->m.cols;
       DevBuf wh(wpanel_elems(rows, cols) * 2), wl(wpanel_elems(rows, cols) * 2);
       DevBuf xh(xpanel_elems(seq, cols) * 2), xl(xpanel_elems(seq, cols) * 2), err(16);
-      for (DevBuf* b : {&wh, &wl, &xh, &xl, &err}) CK(cudaMemsetAsync(b->p, 0, b->n, s));
-      launch_wpanels(w->m, 0, wh.p, wl.p, s);
-      launch_xpanels(a_dev, cols, seq, cols, nullptr, 0.f, xh.p, xl.p, s);
-      launch_qgemm(QgemmLaunch{wh.p, wl.p, xh.p, xl.p, cols, rows, seq, PE_STORE, out_dev, rows, nullptr,
-                               err.as<uint32_t>()},
+      DevBuf rexp((rows + 127) / 128 * 128), texp(seq + 16);
+      for (DevBuf* b : {&wh, &wl, &xh, &xl, &err, &rexp, &texp}) CK(cudaMemsetAsync(b->p, 0, b->n, s));
+      launch_wpanels(w->m, 0, rexp.as<int8_t>(), wh.p, wl.p, s);
+      launch_xpanels(a_dev, cols, seq, cols, nullptr, 0.f, xh.p, xl.p, texp.as<int8_t>(), s);
+      launch_qgemm(QgemmLaunch{wh.p, wl.p, xh.p, xl.p, rexp.as<int8_t>(), texp.as<int8_t>(), cols, rows, seq,
+                               PE_STORE, out_dev, rows, nullptr, err.as<uint32_t>()},
                    s);
       uint32_t e = 0;
       CK(cudaMemcpyAsync(&e, err.p, 4, cudaMemcpyDeviceToHost, s));

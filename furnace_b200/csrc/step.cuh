@@ -38,6 +38,13 @@
 constexpr int MK_THREADS = 512;
 constexpr int MK_CWARPS = 15;
 constexpr int MK_NT = MK_CWARPS * 32;
+#ifndef MK_RPW
+#define MK_RPW 2  // rows per consumer warp and ring stage
+#endif
+constexpr int MK_ROWS = MK_CWARPS * MK_RPW;
+#ifndef MK_NOINLINE
+#define MK_NOINLINE
+#endif
 constexpr uint32_t MK_NSLOT = 8;   // stages in flight at most
 constexpr uint32_t MK_NREC = 4;    // record chunks in flight (long inputs)
 constexpr long long MK_SPIN_NS = 1000000000ll;
@@ -154,29 +161,142 @@ struct MkProd {
   const uint32_t* err;
   uint64_t pol;
   uint32_t n = 0, rel = 0, head = 0;  // stages issued, stages known released, ring head
-  uint32_t soff[MK_NSLOT], ssz[MK_NSLOT];
-  bool ok = true;
+  // byte ranges of the stages in flight by slot, kept in registers: every
+  // index below is a compile-time constant after unrolling
+  uint32_t soff[MK_NSLOT], send[MK_NSLOT], live = 0;
+  uint64_t waited = 0;  // ns spent waiting for ring space (timeline trace)
+  bool ok = true, reserve_ok = true;
 
   // Room for a stage of `bytes`: its slot and its byte range free.
   __device__ bool reserve(uint32_t bytes, uint32_t ring_bytes, uint32_t* off) {
-    *off = ring_alloc(head, bytes, ring_bytes);
+    const uint32_t o = ring_alloc(head, bytes, ring_bytes), e = o + bytes;
     for (;;) {
       bool clash = n - rel >= MK_NSLOT;
-      for (uint32_t j = rel; j < n && !clash; j++) {
-        const uint32_t s = soff[j % MK_NSLOT], e = s + ssz[j % MK_NSLOT];
-        clash = *off < e && s < *off + bytes;
-      }
+#pragma unroll
+      for (uint32_t j = 0; j < MK_NSLOT; j++) clash |= ((live >> j) & 1) && o < send[j] && soff[j] < e;
       if (!clash) break;
-      if (!mk_mbar_wait(&empty[rel % MK_NSLOT], (rel / MK_NSLOT) & 1, err)) return false;
+      const uint64_t tw = gtimer();
+      const bool got = mk_mbar_wait(&empty[rel % MK_NSLOT], (rel / MK_NSLOT) & 1, err);
+      waited += gtimer() - tw;
+      if (!got) return reserve_ok = false;
+      live &= ~(1u << (rel % MK_NSLOT));
       rel++;
     }
-    soff[n % MK_NSLOT] = *off;
-    ssz[n % MK_NSLOT] = bytes;
+    const uint32_t sl = n % MK_NSLOT;
+#pragma unroll
+    for (uint32_t j = 0; j < MK_NSLOT; j++)
+      if (j == sl) {
+        soff[j] = o;
+        send[j] = e;
+      }
+    live |= 1u << sl;
+    *off = o;
     return true;
   }
 };
 
-__device__ void mk_producer(const MkParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty, MkPhase* desc,
+// One stage of the producer's walk: up to two copies (attention: K and V)
+// into one ring range of `size` bytes.
+struct MkStage {
+  const uint8_t* src[2];
+  uint32_t nb[2], off1, size;
+};
+
+// Walks this CTA's stages of phases [k, kend) in consumption order.  The
+// producer runs one walker that issues the copies and a second one ahead of
+// it that only prefetches into L2 (cp.async.bulk.prefetch.L2), so more bytes
+// are requested from HBM than the ring can hold.
+struct MkWalk {
+  uint32_t k = 0, c = 0, ra = 0, a = 0, t1 = 0;
+  uint32_t sk = 0;  // phase of the stage returned last
+  bool open = false;
+  bool fetches = false;  // the copying walk refills a descriptor buffer as it leaves a phase
+  StageIter it;
+  const uint8_t *kb = nullptr, *vb = nullptr;
+
+  __device__ void leave(const MkParams& p, MkPhase* desc, uint64_t* dbar) {
+    if (fetches && k + 2 < p.nph) {
+      // phase k's descriptor is not read again: its buffer takes phase k + 2
+      fence_proxy_async_smem();
+      mbar_expect_tx(&dbar[k & 1], sizeof(MkPhase));
+      bulk_g2s(&desc[k & 1], &p.ph[k + 2], sizeof(MkPhase), &dbar[k & 1], 0ull);
+    }
+    k++;
+    open = false;
+  }
+
+  // 1: *st is the next stage; 0: phase kend reached; -1: phase k's
+  // descriptor has not landed yet (only when !block); -2: a wait ran out.
+  __device__ int next(const MkParams& p, MkPhase* desc, uint64_t* dbar, uint32_t kend, bool block, uint32_t pos,
+                      MkStage* st) {
+    for (;;) {
+      if (k >= kend) return 0;
+      const MkPhase& ph = desc[k & 1];
+      if (!open) {
+        if (block) {
+          if (!mk_mbar_wait(&dbar[k & 1], (k >> 1) & 1, &p.st->error)) return -2;
+        } else if (!mbar_try(&dbar[k & 1], (k >> 1) & 1)) {
+          return -1;
+        }
+        open = true;
+        if (ph.kind == MK_GEMV) {
+          it.init(ph.seg, ph.nseg, blockIdx.x);
+          c = 0;
+          ra = it.r0;
+        } else {
+          uint32_t g, t0;
+          a = t1 = 0;
+          if (pos < p.max_ctx && mk_att_range(p, pos, &g, &t0, &t1)) {
+            const uint32_t rowb = p.hd * (p.kv_f16 ? 2u : 4u);
+            kb = static_cast<const uint8_t*>(ph.kc) + (uint64_t)g * p.max_ctx * rowb;
+            vb = static_cast<const uint8_t*>(ph.vc) + (uint64_t)g * p.max_ctx * rowb;
+            a = t0;
+          }
+        }
+      }
+      // the walk leaves a phase as soon as its last stage is handed out, so
+      // the phase's descriptor is not read again after that
+      sk = k;
+      if (ph.kind == MK_GEMV) {
+        if (c < it.nch) {
+          ChunkInfo ci;
+          chunk_info(it, c, &ci);
+          const uint32_t nr = min(ra + ph.rs, it.r1) - ra;
+          st->src[0] = ci.plane + (uint64_t)ra * ci.tb;
+          st->nb[0] = nr * ci.tb;
+          st->src[1] = nullptr;
+          st->nb[1] = 0;
+          st->off1 = 0;
+          st->size = st->nb[0];
+          ra += ph.rs;
+          if (ra >= it.r1) {
+            ra = it.r0;
+            c++;
+          }
+          if (c >= it.nch) leave(p, desc, dbar);
+          return 1;
+        }
+      } else if (a < t1) {
+        // rows below pos are final; row pos is this step's and is patched in
+        const uint32_t rowb = p.hd * (p.kv_f16 ? 2u : 4u);
+        const uint32_t e = min(min(t1, a + AT_TP), pos), rows = e > a ? e - a : 0;
+        st->src[0] = kb + (uint64_t)a * rowb;
+        st->src[1] = vb + (uint64_t)a * rowb;
+        st->nb[0] = st->nb[1] = rows * rowb;
+        st->off1 = AT_TP * rowb;
+        st->size = mk_kv_stage(p);
+        a += AT_TP;
+        if (a >= t1) leave(p, desc, dbar);
+        return 1;
+      }
+      leave(p, desc, dbar);  // a phase without stages for this CTA
+    }
+  }
+};
+
+constexpr uint32_t MK_PF_AHEAD = 128 * 1024;  // bytes requested ahead of the ring's copies
+
+MK_NOINLINE __device__ void mk_producer(const MkParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty, MkPhase* desc,
                             uint64_t* dbar) {
   MkProd pr;
   pr.ring = ring;
@@ -191,68 +311,56 @@ __device__ void mk_producer(const MkParams& p, uint8_t* ring, uint64_t* full, ui
   };
   fetch_desc(0);
   if (p.nph > 1) fetch_desc(1);
-  uint32_t k = 0;
-  for (; k < p.nph && pr.ok; k++) {
-    if (!mk_mbar_wait(&dbar[k & 1], (k >> 1) & 1, pr.err)) {
+  MkWalk w, pf;
+  w.fetches = true;
+  uint64_t copied = 0, prefetched = 0;
+  MkStage st, sp;
+  Tracer tr;  // per phase: t[0] first copy issued, t[1] last, t[2] ns waiting for ring space
+  uint32_t tk = ~0u;
+  uint64_t w0 = 0;
+  for (;;) {
+    const int r = w.next(p, desc, dbar, p.nph, true, pos, &st);
+    if (r == 1 && w.sk != tk) {
+      if (tr.r) tr.r->t[2] = pr.waited - w0;
+      tr = Tracer();
+      tr.begin(TR_STEP + 8, w.sk);
+      tk = w.sk;
+      w0 = pr.waited;
+    }
+    if (r == 0) break;
+    if (r < 0) {
       pr.ok = false;
       break;
     }
-    const MkPhase& ph = desc[k & 1];
-    if (ph.kind == MK_GEMV) {
-      StageIter it;
-      it.init(ph.seg, ph.nseg, blockIdx.x);
-      for (uint32_t c = 0; c < it.nch && pr.ok; c++) {
-        ChunkInfo ci;
-        chunk_info(it, c, &ci);
-        for (uint32_t ra = it.r0; ra < it.r1; ra += ph.rs) {
-          const uint32_t bytes = (min(ra + ph.rs, it.r1) - ra) * ci.tb;
-          uint32_t off;
-          if (!pr.reserve(bytes, p.ring_bytes, &off)) {
-            pr.ok = false;
-            break;
-          }
-          uint64_t* fb = &full[pr.n % MK_NSLOT];
-          mbar_expect_tx(fb, bytes);
-          bulk_g2s(ring + off, ci.plane + (uint64_t)ra * ci.tb, bytes, fb, pr.pol);
-          pr.n++;
-        }
-      }
-    } else {
-      uint32_t g, t0, t1;
-      if (pos < p.max_ctx && mk_att_range(p, pos, &g, &t0, &t1)) {
-        const uint32_t rowb = p.hd * (p.kv_f16 ? 2u : 4u), sb = mk_kv_stage(p);
-        const uint8_t* kb = static_cast<const uint8_t*>(ph.kc) + (uint64_t)g * p.max_ctx * rowb;
-        const uint8_t* vb = static_cast<const uint8_t*>(ph.vc) + (uint64_t)g * p.max_ctx * rowb;
-        for (uint32_t a = t0; a < t1; a += AT_TP) {
-          uint32_t off;
-          if (!pr.reserve(sb, p.ring_bytes, &off)) {
-            pr.ok = false;
-            break;
-          }
-          // rows below pos are final; row pos is this step's and is patched in
-          const uint32_t e = min(min(t1, a + AT_TP), pos), rows = e > a ? e - a : 0;
-          uint64_t* fb = &full[pr.n % MK_NSLOT];
-          mbar_expect_tx(fb, 2 * rows * rowb);
-          if (rows) {
-            bulk_g2s(ring + off, kb + (uint64_t)a * rowb, rows * rowb, fb, pr.pol);
-            bulk_g2s(ring + off + AT_TP * rowb, vb + (uint64_t)a * rowb, rows * rowb, fb, pr.pol);
-          }
-          pr.n++;
-        }
-      }
+    uint32_t off;
+    if (!pr.reserve(st.size, p.ring_bytes, &off)) break;
+    uint64_t* fb = &full[pr.n % MK_NSLOT];
+    mbar_expect_tx(fb, st.nb[0] + st.nb[1]);
+    if (st.nb[0]) bulk_g2s(ring + off, st.src[0], st.nb[0], fb, pr.pol);
+    if (st.nb[1]) bulk_g2s(ring + off + st.off1, st.src[1], st.nb[1], fb, pr.pol);
+    pr.n++;
+    copied += st.size;
+    tr.mark(1);
+    // keep the L2 prefetch walk MK_PF_AHEAD bytes in front, at most into the
+    // phase after the one being copied (whose descriptor is resident)
+    if (prefetched < copied) {
+      pf = w;
+      pf.fetches = false;
+      prefetched = copied;
     }
-    // this phase's descriptor has been read: reuse its buffer two phases on
-    if (k + 2 < p.nph) {
-      fence_proxy_async_smem();
-      fetch_desc(k + 2);
+    while (prefetched < copied + MK_PF_AHEAD) {
+      const int q = pf.next(p, desc, dbar, min(p.nph, w.k + 2), false, pos, &sp);
+      if (q <= 0) break;
+      if (sp.nb[0]) bulk_prefetch(sp.src[0], sp.nb[0]);
+      if (sp.nb[1]) bulk_prefetch(sp.src[1], sp.nb[1]);
+      prefetched += sp.size;
     }
   }
-  if (!pr.ok) {
+  if (tr.r) tr.r->t[2] = pr.waited - w0;
+  if (!pr.ok || !pr.reserve_ok) {
     atomicCAS(&p.st->error, 0u, 4u);
-    // stopped in phase k (or k - 1 after finishing it): the copies of
-    // descriptors up to k + 1 may still be in flight
-    const uint32_t k0 = k > 0 && k >= p.nph ? k - 1 : k;
-    for (uint32_t j = k0; j < k0 + 2 && j < p.nph; j++) mbar_wait(&dbar[j & 1], (j >> 1) & 1);
+    // descriptors up to two phases past the walk may still be in flight
+    for (uint32_t j = w.k; j < w.k + 2 && j < p.nph; j++) mbar_wait(&dbar[j & 1], (j >> 1) & 1);
     // the copies already issued land in this CTA's shared memory: wait for
     // them (bounded) before this thread, possibly the CTA's last, exits
     for (uint32_t j = pr.n > MK_NSLOT ? pr.n - MK_NSLOT : 0; j < pr.n; j++)
@@ -269,9 +377,17 @@ struct MkCons {
   const uint32_t* err;
   uint32_t n = 0, head = 0;  // stages consumed, ring head (mirrors the producer)
   // the next stage: wait until it has landed; returns its bytes in the ring
+  uint64_t waited = 0;  // ns this thread spent waiting for stages (timeline trace)
   __device__ const uint8_t* acquire(uint32_t bytes, uint32_t ring_bytes) {
     const uint32_t off = ring_alloc(head, bytes, ring_bytes);
-    if (!mk_mbar_wait(&full[n % MK_NSLOT], (n / MK_NSLOT) & 1, err)) return nullptr;
+    uint64_t* b = &full[n % MK_NSLOT];
+    const uint32_t par = (n / MK_NSLOT) & 1;
+    if (!mbar_try(b, par)) {
+      const uint64_t t = gtimer();
+      const bool ok = mk_mbar_wait(b, par, err);
+      waited += gtimer() - t;
+      if (!ok) return nullptr;
+    }
     return ring + off;
   }
   // every consumer warp calls this once per stage
@@ -328,20 +444,20 @@ __device__ bool mk_gemv_body(const MkParams& p, const MkPhase& ph, const StageIt
       const uint8_t* tile = cs.acquire(nr * tb, p.ring_bytes);
       if (!tile) return false;
       const uint32_t last = nr - 1;
-      float v[GV_RPW];
+      float v[MK_RPW];
 #pragma unroll
-      for (int j = 0; j < GV_RPW; j++) {
-        const uint32_t r = min(warp + GV_CWARPS * j, last);
+      for (int j = 0; j < MK_RPW; j++) {
+        const uint32_t r = min(warp + MK_CWARPS * j, last);
         v[j] = lane_on * unit_dot<DT>(tile + r * tb, lu, nu, xr);
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-        for (int j = 0; j < GV_RPW; j++) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
+        for (int j = 0; j < MK_RPW; j++) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
       if (lane == 0) {
 #pragma unroll
-        for (int j = 0; j < GV_RPW; j++) {
-          const uint32_t r = warp + GV_CWARPS * j;
+        for (int j = 0; j < MK_RPW; j++) {
+          const uint32_t r = warp + MK_CWARPS * j;
           if (r <= last) acc[ra + r - it.r0] += v[j];
         }
       }
@@ -502,7 +618,7 @@ __device__ bool mk_gemv(const MkParams& p, const MkPhase& ph, MkCons& cs, uint8_
 
 // Attention of one layer: this CTA's split, then its share of the merge.
 template <int HD, typename KT>
-__device__ bool mk_attn(const MkParams& p, const MkPhase& ph, MkCons& cs, uint8_t* scratch, volatile uint32_t* flag,
+MK_NOINLINE __device__ bool mk_attn(const MkParams& p, const MkPhase& ph, MkCons& cs, uint8_t* scratch, volatile uint32_t* flag,
                         Tracer& tr) {
   constexpr int DPL = HD / 32;
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -795,6 +911,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(const __grid_constant__ 
     mk_csync();
     if (tid == 0) {
       tr.mark(4);
+      if (tr.r) tr.r->t[5] = cs.waited;  // cumulative ns warp 0 waited for stages
       // every consumer thread is done with this descriptor: refill its buffer
       if (ok && k + 2 < p.nph) {
         fence_proxy_async_smem();

@@ -1225,6 +1225,17 @@ int orc_kv_read(void* kvp, size_t li, int which_v, size_t n, float* out) {
   return 0;
 }
 
+// Overwrite layer `li`'s cached K (or V) rows [0, n) from [n, kv_dim] (the
+// timed CPU baseline fills a long context with synthetic rows: the cost of
+// a decode step does not depend on the cached values).
+int orc_kv_write(void* kvp, size_t li, int which_v, size_t n, const float* in) {
+  KvCache* kv = (KvCache*)kvp;
+  if (li >= kv->k.size() || n > kv->max_ctx) { set_err("kv write out of range"); return 1; }
+  auto& dst = which_v ? kv->v[li] : kv->k[li];
+  memcpy(dst.data(), in, sizeof(float) * n * kv->kv_dim);
+  return 0;
+}
+
 int orc_forward_cached(void* mp, void* kv, const uint32_t* toks, size_t n, float* logits) {
   if (n == 0) { set_err("forward with no tokens"); return 1; }
   return forward_cached(*(Model*)mp, toks, n, (KvCache*)kv, logits) ? 0 : 1;

@@ -71,6 +71,7 @@ def lib():
             "orc_kv_len": (S, [P]),
             "orc_kv_set_len": (None, [P, S]),
             "orc_kv_read": (I, [P, S, I, S, fp]),
+            "orc_kv_write": (I, [P, S, I, S, fp]),
             "orc_forward_cached": (I, [P, P, u32p, S, fp]),
             "orc_forward_last": (I, [P, u32p, S, fp]),
             "orc_embed": (I, [P, u32p, S, fp]),
@@ -346,6 +347,19 @@ class KvCache:
         if lib().orc_kv_read(self._h, layer, int(which_v), n, _fp(out)) != 0:
             raise OracleError(_err())
         return out
+
+    def fill_synthetic(self, n: int, seed: int = 0, scale: float = 1.0):
+        """Rows [0, n) of every layer's K and V set to seeded N(0, scale^2)
+        values and len = n: a long context for timing decode steps (their
+        cost does not depend on the cached values)."""
+        kvd = self.model.n_kv_heads * self.model.head_dim
+        rng = np.random.default_rng(seed)
+        for layer in range(self.model.n_layers):
+            for which in (0, 1):
+                rows = np.ascontiguousarray((rng.standard_normal((n, kvd)) * scale).astype(np.float32))
+                if lib().orc_kv_write(self._h, layer, which, n, _fp(rows)) != 0:
+                    raise OracleError(_err())
+        self.len = n
 
 
 class Sampler:

@@ -124,6 +124,30 @@ def test_prefill_gemm_vs_oracle(orc, name, rows, cols, seq):
     assert err <= GEMV_REL, err
 
 
+@pytest.mark.parametrize("scale", [1e5, 1e-6, 3e4], ids=["1e5", "1e-6", "mixed"])
+@pytest.mark.parametrize("name", ["Q4_K", "Q6_K"])
+def test_prefill_gemm_extreme_magnitudes(orc, name, scale):
+    """The GEMM's fp16 hi/lo split scales every token row and weight row by a
+    power of two first: activations around 1e5 (fp16 overflows at 65504) and
+    around 1e-6 (fp16 subnormals) keep the GEMV bar.  "mixed" gives every
+    token row its own magnitude, 1e-6 .. 3e4."""
+    dt = TYPES[name][0]
+    rows, cols, seq = 160, 512, 40
+    raw = synth.random_tensor(rows, cols, dt, seed=77)
+    rng = np.random.default_rng(5)
+    x = rng.normal(0, 1, size=(seq, cols))
+    if scale == 3e4:
+        x *= np.logspace(-6, np.log10(3e4), seq)[:, None]
+    else:
+        x *= scale
+    x = x.astype(np.float32)
+    want = orc.matmul_quant(x, raw, rows, cols, dt)
+    got = fz.quant.matmul_quant(x, raw, rows, cols, dt)
+    assert np.all(np.isfinite(got))
+    err = np.abs(got - want).max(axis=1) / np.abs(want).max(axis=1)  # per token row
+    assert err.max() <= GEMV_REL, err.max()
+
+
 def test_fused_q8_matmul_reference_case():
     """src/quant.rs:331-357 on the device."""
     raw = b""
@@ -432,3 +456,34 @@ def test_greedy_c3_full_depth_512_prompt_32_steps():
     layer included, at a size the oracle's prefill finishes in a few
     minutes."""
     _greedy_parity(synth.ensure("c3"), 512, 32, seed=6)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name,n_prompt,n_new", [("c1", 32, 128), ("c2", 128, 128)])
+def test_quantized_path_meets_the_bars_against_f32_mode(name, n_prompt, n_new):
+    """The reference's `--f32` mode (Model::load(use_f32), src/model.rs:110-117;
+    CLI flag src/main.rs:62-65) dequantizes every matrix to f32 at load and
+    takes one 8-lane dot over each whole row (tensor::matmul,
+    src/tensor.rs:74-80) instead of a dot per block summed block by block
+    (src/quant.rs:218-225).  The weights are the same numbers either way (the
+    dequantization is exact), so only the grouping of the f32 sums differs.
+    The device path (exact in-kernel dequantization, f32 accumulation) meets
+    the north star's bars against the oracle's f32 mode too: identical greedy
+    ids, logits within 1e-3 with the same argmax and top-5 at every step."""
+    from oracle import oracle
+
+    path = synth.ensure(name)
+    f = fz.GgufFile.open(path)
+    dev = fz.Model.load(f)
+    ref = oracle.Model(path, use_f32=True)
+    ids = synth.prompt_ids(ref.vocab, n_prompt, seed=9)
+    want_ids, want_lg, _, _ = ref.generate(ids, n_new, keep_logits=True)
+    got_ids, got_lg = fz.generate(dev, ids, n_new, max_ctx=n_prompt + n_new, keep_logits=True)
+    assert got_ids.tolist() == want_ids.tolist()
+    worst, ties = 0.0, []
+    for s in range(len(want_ids)):
+        worst = max(worst, _check_logits(got_lg[s], want_lg[s], f"step {s}", ties))
+    print(f"\n{name} vs the f32 mode: {len(want_ids)} steps, worst logit error {worst:.2e}, near ties {ties}")
+    dev.close()
+    ref.close()
+
