@@ -502,7 +502,7 @@ struct GvParams {
   uint32_t slots, slot_bytes, max_rows, pf_ahead;
   GvNext next;
   uint32_t idx_base;     // EPI_LOGITS: global index of row 0
-  uint32_t chunked_rec;  // in_runs stream per K-chunk through two buffers (long inputs)
+  uint32_t chunked_rec;  // in_runs stream per K-chunk through GV_NREC buffers (long inputs)
   // tensor-parallel exchange through peer memory (GemvLaunch::ar_*)
   ArPeers ar_peers;
   uint32_t ar_w, ar_rank, ar_k, ar_h;
@@ -511,6 +511,7 @@ struct GvParams {
   float* x_out;          // ar_pull: this CTA's slice of the summed x goes here
 };
 constexpr uint32_t GV_CREC = 32 * 256;  // run records of one chunk (<= 32 units)
+constexpr uint32_t GV_NREC = 4;         // chunk record buffers of a long input (copies in flight)
 
 // This CTA's row range within its segment: whole multiples of seg.align rows
 // (pairs for gate/up, 16-row runs where the epilogue writes run records).
@@ -729,8 +730,8 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
 // thread; the chunked-record mode of long inputs.
 __device__ __forceinline__ bool gv_issue_records(const GvParams& p, const ChunkInfo& ci, uint32_t c, uint8_t* crec,
                                                  uint64_t* recbar, uint64_t* recfree) {
-  const uint32_t b = c & 1;
-  if (c >= 2 && !mbar_wait(&recfree[b], ((c - 2) >> 1) & 1)) return false;
+  const uint32_t b = c % GV_NREC;
+  if (c >= GV_NREC && !mbar_wait(&recfree[b], ((c - GV_NREC) / GV_NREC) & 1)) return false;
   asm volatile("fence.proxy.async;" ::: "memory");
   mbar_expect_tx(&recbar[b], ci.nu * 256);
   bulk_g2s(crec + b * GV_CREC, reinterpret_cast<const uint8_t*>(p.in_runs) + 256ull * ci.cu0, ci.nu * 256,
@@ -753,8 +754,8 @@ __device__ bool gv_consume(const GvParams& p, const StageIter& it, const ChunkIn
     const float lane_on = lane < nu ? 1.f : 0.f;
     const XRun* rb = rec;
     if (p.chunked_rec) {
-      if (!mbar_wait(&recbar[c & 1], (c >> 1) & 1)) return false;
-      rb = reinterpret_cast<const XRun*>(reinterpret_cast<const uint8_t*>(rec) + (c & 1) * GV_CREC) -
+      if (!mbar_wait(&recbar[c % GV_NREC], (c / GV_NREC) & 1)) return false;
+      rb = reinterpret_cast<const XRun*>(reinterpret_cast<const uint8_t*>(rec) + (c % GV_NREC) * GV_CREC) -
            4 * chunks[c].cu0;
     }
     XRun xr[4];
@@ -762,10 +763,10 @@ __device__ bool gv_consume(const GvParams& p, const StageIter& it, const ChunkIn
     for (uint32_t j = 0; j < 4; j++) xr[j] = load_run(rb, chunks[c].cu0 + lu, j);
     if (p.chunked_rec) {
       __syncwarp();
-      if (lane == 0) mbar_arrive(&recfree[c & 1]);
-      if (threadIdx.x == 0 && c + 2 < it.nch &&
-          !gv_issue_records(p, chunks[c + 2], c + 2, reinterpret_cast<uint8_t*>(const_cast<XRun*>(rec)), recbar,
-                            recfree))
+      if (lane == 0) mbar_arrive(&recfree[c % GV_NREC]);
+      if (threadIdx.x == 0 && c + GV_NREC < it.nch &&
+          !gv_issue_records(p, chunks[c + GV_NREC], c + GV_NREC, reinterpret_cast<uint8_t*>(const_cast<XRun*>(rec)),
+                            recbar, recfree))
         return false;
     }
     for (uint32_t ra = it.r0; ra < it.r1; ra += GV_ROWS) {
@@ -864,9 +865,9 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
   const uint32_t NX = runs_for_dev(p.cols);
   uint8_t* ring = smem;
   XRun* rec = reinterpret_cast<XRun*>(ring + (size_t)p.slots * p.slot_bytes);
-  float* acc = p.chunked_rec ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(rec) + 2 * GV_CREC)
+  float* acc = p.chunked_rec ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(rec) + GV_NREC * GV_CREC)
                              : reinterpret_cast<float*>(rec + NX);
-  __shared__ __align__(8) uint64_t crecbar[2], crecfree[2];
+  __shared__ __align__(8) uint64_t crecbar[GV_NREC], crecfree[GV_NREC];
   __shared__ float red[GV_CWARPS];
   __shared__ unsigned long long kred[GV_CWARPS];
   __shared__ ChunkInfo chunks[GV_MAX_CH];
@@ -881,7 +882,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
       mbar_init(&empty[s], GV_CWARPS);
     }
     mbar_init(&recbar, 1);
-    for (int b = 0; b < 2; b++) {
+    for (uint32_t b = 0; b < GV_NREC; b++) {
       mbar_init(&crecbar[b], 1);
       mbar_init(&crecfree[b], GV_CWARPS);
     }
@@ -974,9 +975,9 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
   pdl_wait();  // the predecessor's output (this GEMV's input) is complete
   if (ctid == 0) tr.mark(1);
   if (p.in_runs && p.chunked_rec) {
-    // records of a long input stream per chunk (gv_consume): the first two
+    // records of a long input stream per chunk (gv_consume): the first GV_NREC
     if (ctid == 0 && it.n_stages)
-      for (uint32_t c = 0; c < 2 && c < it.nch; c++)
+      for (uint32_t c = 0; c < GV_NREC && c < it.nch; c++)
         gv_issue_records(p, chunks[c], c, reinterpret_cast<uint8_t*>(rec), crecbar, crecfree);
   } else if (p.in_runs) {
     // records written by the producing kernel: one bulk copy
@@ -1256,7 +1257,7 @@ void launch_gemv(const GemvLaunch& g, cudaStream_t st) {
   if (g.in_runs && fixed + 2 * slot > GV_SMEM) {
     // a long record input (ffn hidden of the large configs): stream it
     p.chunked_rec = 1;
-    fixed = 2 * GV_CREC + 4 * max_rows + 128;
+    fixed = GV_NREC * GV_CREC + 4 * max_rows + 128;
   }
   if (fixed + 2 * slot > GV_SMEM) fail(FZ_EINVAL, "gemv: %u rows per block exceed shared memory", max_rows);
   uint32_t slots = std::min<uint32_t>(GV_MAX_SLOTS, (GV_SMEM - fixed) / slot);

@@ -163,3 +163,32 @@ def test_tp2_batched_prefill(tmp_path, over):
             b = kr.read(li, w, n)[:, cols]
             assert np.abs(a - b).max() <= 1e-4 * max(1.0, np.abs(b).max()), (r, li, w)
     _run_tp(path, n, 24)
+
+
+def _need(n):
+    if _ngpus() < n:
+        pytest.skip(f"needs {n} GPUs")
+
+
+@pytest.mark.slow
+def test_tp4_greedy_c3_truncated():
+    """C3 at TP4 (the benchmarked 7B shape, 2 of its 28 layers at full
+    width): 7 query heads and 1 KV head per rank; each rank's o_proj input
+    is 896 columns, 3.5 Q4_K super-blocks, so neighbours share a boundary
+    block; the FFN's 74 super-blocks split 18/19/18/19 (fz_tp_slice_of cuts
+    on 256-element boundaries).  A 40-token prompt (batched prefill), then 64
+    greedy steps against the oracle."""
+    _need(4)
+    _run_tp(synth.ensure("c3", n_layers=2), 40, 64, world=4)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name", ["c4", "c5"])
+def test_tp8_greedy_truncated_c4_c5(name):
+    """TP8 on the 32B and 72B shapes (2 layers at full width): C4's FFN of
+    108 super-blocks splits 13/14 alternately; C5's FFN of 29568 (not a
+    multiple of 256, so ffn_down is Q8_0 / Q5_0 in 32-element blocks) splits
+    into slices of 3584/3840 elements and a last one of 3712 (14.5 units of
+    256).  40-token prompt, 64 greedy steps."""
+    _need(8)
+    _run_tp(synth.ensure(name, n_layers=2), 40, 64, world=8)
