@@ -378,12 +378,11 @@ def run_ours(args, dist):
            "d2h_bytes_per_step": 4 * (T + 1) + 32,
            "note": "fz_decode_greedy per step; h2d = seed token + step state, d2h = ids + status"}
     # ---- where a token's time goes, and its algorithmic bytes ------------
-    # step kernel (FURNACE_B200_STEP=1): per-op spans from the kernel's own
-    # %globaltimer trace inside the captured step; per-kernel path: CUDA
-    # events around each launch outside the graph (serialised: shares only)
-    kv.len = base + total_tokens // 2  # mid-decode position, as the timed region's mean
+    # fz_step_profile: CUDA events around each launch outside the graph
+    # (serialised, so only the shares are meaningful); the bytes are the
+    # algorithmic bytes of every op at the timed region's mean position
+    kv.len = base + total_tokens // 2
     prof = model.step_profile(first, T, kv)
-    in_graph = os.environ.get("FURNACE_B200_STEP", "") == "1" and tp == 1
     bytes_tok = sum(v[1] for v in prof.values()) / T  # weights, KV rows read, vectors
     peak, peak_src = measured_peaks()
     achieved = bytes_tok / (ms_tok / 1000.0) / 1e9
@@ -391,9 +390,7 @@ def run_ours(args, dist):
     ops = {o: {"ms_per_token": prof[o][0] / T, "share": prof[o][0] / prof_ms if prof_ms else None,
                "gbs": (prof[o][1] / (prof[o][0] / 1000.0) / 1e9) if prof[o][0] else None} for o in prof}
     traffic = ncu_traffic()
-    kernel = ("k_step (persistent decode step: every GEMV, attention and lm_head of a token in one launch)"
-              if in_graph else "decode step (per-kernel path: 6 launches per layer + lm_head)")
-    roofline = {"kernel": kernel, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+    roofline = {"kernel": "decode step (k_gemv x4, k_attn, k_attn_combine per layer; lm_head k_gemv)", "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": f"{peak_src} hbm_gbs (burst copy)",
                 "bytes_per_launch": bytes_tok, "launch_us": ms_tok * 1000.0,
                 "how": "algorithmic bytes of one token (GGUF weight bytes of every matrix, the KV rows read at the "
@@ -419,9 +416,9 @@ def run_ours(args, dist):
                     if args.prefill > 8 else "decode step per token",
                     "note": "host wall clock of fz_forward over the prompt, including the per-layer weight "
                             "dequantization into GEMM panels"},
-        "gpu_launches": (3 if in_graph else 6 * cfg.n_layers + 3) * total_tokens, "clocks": clocks, "e2e": e2e,
+        "gpu_launches": (6 * cfg.n_layers + 3) * total_tokens, "clocks": clocks, "e2e": e2e,
         "roofline": roofline,
-        "ops": ops, "ops_timing": "in-graph %globaltimer spans" if in_graph else "CUDA events per launch, serialised",
+        "ops": ops, "ops_timing": "CUDA events per launch outside the graph, serialised: shares only",
     }
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(path, cfg.vocab, base)

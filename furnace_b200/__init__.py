@@ -98,6 +98,7 @@ def load_library(build_if_missing: bool = True):
     sig = {
         "fz_last_error": (C.c_char_p, []),
         "fz_version": (C.c_char_p, []),
+        "fz_selftest_exchange_timeout": (I, [I, U32]),
         "fz_open": (I, [C.c_char_p, pp]),
         "fz_open_bytes": (I, [P, S, pp]),
         "fz_file_free": (None, [P]),

@@ -25,6 +25,7 @@
 #include <cuda_fp16.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <algorithm>
 #include <memory>
@@ -459,7 +460,10 @@ uint32_t runs_for(uint32_t cols) { return runs_for_dev(cols); }
 // GEMV
 // ---------------------------------------------------------------------------
 constexpr int GV_CWARPS = 15;                      // consumer warps (16 warps per block with the producer)
-constexpr int GV_RPW = 2;                          // rows per consumer warp per stage
+#ifndef GV_RPW_DEF
+#define GV_RPW_DEF 2
+#endif
+constexpr int GV_RPW = GV_RPW_DEF;                 // rows per consumer warp per stage
 constexpr int GV_ROWS = GV_CWARPS * GV_RPW;        // rows per stage
 constexpr int GV_THREADS = (GV_CWARPS + 1) * 32;   // + one producer warp
 constexpr int GV_NT = GV_CWARPS * 32;              // consumer threads
@@ -509,6 +513,7 @@ struct GvParams {
   const uint32_t* ar_base;
   int ar_push, ar_pull;
   float* x_out;          // ar_pull: this CTA's slice of the summed x goes here
+  uint64_t ar_spin_ns;   // ar_pull: time limit of the wait for a peer's word
 };
 constexpr uint32_t GV_CREC = 32 * 256;  // run records of one chunk (<= 32 units)
 constexpr uint32_t GV_NREC = 4;         // chunk record buffers of a long input (copies in flight)
@@ -817,8 +822,9 @@ __device__ bool gv_consume(const GvParams& p, const StageIter& it, const ChunkIn
 // each rank sends only after it read e).  epoch = *ar_base + k + 1, where
 // ar_base advances by the step's exchange count at every step's end and k
 // numbers the exchanges inside the step; all ranks run the same steps.  A
-// word that does not arrive within 2 s sets error 7.
-constexpr long long AR_SPIN_NS = 2000000000ll;
+// word that does not arrive within the wait limit (GvParams::ar_spin_ns:
+// FURNACE_B200_WAIT_MS, default 2 s) sets error 7.
+constexpr uint64_t AR_SPIN_NS = 2000000000ull;
 
 uint64_t ar_buffer_bytes(uint32_t H, uint32_t W) { return 2ull * W * H * 8; }
 
@@ -845,7 +851,7 @@ __device__ __forceinline__ bool ar_pull4(const GvParams& p, uint32_t e, uint32_t
     if (a.y != e || a.w != e || b.y != e || b.w != e) {
       const uint64_t t0 = gtimer();
       while (a.y != e || a.w != e || b.y != e || b.w != e) {
-        if (gtimer() - t0 > (uint64_t)AR_SPIN_NS) return false;
+        if (gtimer() - t0 > p.ar_spin_ns) return false;
         a = ld_volatile_u4(w);
         b = ld_volatile_u4(w + 1);
       }
@@ -1244,6 +1250,9 @@ void launch_gemv(const GemvLaunch& g, cudaStream_t st) {
     p.ar_push = g.ar_push;
     p.ar_pull = g.ar_pull;
     p.x_out = const_cast<float*>(g.x);
+    p.ar_spin_ns = g.ar_spin_ns ? g.ar_spin_ns : AR_SPIN_NS;
+    if (const char* e = getenv("FURNACE_B200_WAIT_MS"))
+      if (atof(e) > 0) p.ar_spin_ns = (uint64_t)(atof(e) * 1e6);
   }
   uint32_t max_rows = 0, slot = 0;
   for (int i = 0; i < g.nseg; i++) {
@@ -1649,190 +1658,6 @@ __global__ void k_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_
 void launch_finalize(StepState* st, const uint32_t* forced, uint32_t* ids_out, bool has_logits, cudaStream_t s,
                      uint32_t* ar_base, uint32_t ar_step) {
   launch_pdl(k_finalize, dim3(1), dim3(1), 0, s, st, forced, ids_out, has_logits ? 1 : 0, ar_base, ar_step);
-}
-
-// ---------------------------------------------------------------------------
-// The decode step as one persistent kernel
-// ---------------------------------------------------------------------------
-enum MkKind : int { MK_GEMV = 0, MK_ATTN = 1 };
-enum MkIn : int { MK_IN_NORM = 0, MK_IN_RUNS = 1, MK_IN_RUNS_CHUNKED = 2 };
-
-// One phase of the step (device copy of a StepPhaseDesc, CTA shares resolved;
-// a multiple of 16 bytes: it is bulk-copied into shared memory).
-struct alignas(16) MkPhase {
-  int kind, nseg, epilogue, in_kind;
-  GvSeg seg[3];
-  uint32_t cols, rs, max_rows, idx_base;  // rs: rows per ring stage
-  const float* x;
-  const float* norm_w;
-  const XRun* in_runs;
-  XRun* out_runs;  // SWIGLU: h records; attention: ctx records
-  void* kc;
-  void* vc;
-  uint32_t ctx_run0;
-  uint32_t wait_ctr, wait_target, arrive_ctr, att_ctr0;
-};
-
-static_assert(sizeof(MkPhase) % 16 == 0, "phase descriptor");
-
-#include "step.cuh"
-
-struct StepKernel {
-  MkPhase* d_ph = nullptr;
-  uint32_t* d_sync = nullptr;
-  MkParams p{};
-  size_t smem = 0;
-};
-
-#ifndef MK_STAGE_KB
-#define MK_STAGE_KB 48
-#endif
-constexpr uint32_t MK_STAGE_MAX = MK_STAGE_KB * 1024;  // bytes of one ring stage at most
-
-uint32_t step_grid() { return (uint32_t)num_sms(); }
-uint32_t step_splits(uint32_t n_kv) {
-  const uint32_t s = step_grid() / n_kv;
-  return s < 1 ? 1 : s > AT_MAXS ? AT_MAXS : s;
-}
-
-void step_kernel_free(StepKernel* k) {
-  if (!k) return;
-  if (k->d_ph) cudaFree(k->d_ph);
-  if (k->d_sync) cudaFree(k->d_sync);
-  delete k;
-}
-
-StepKernel* step_kernel_build(const std::vector<StepPhaseDesc>& d, const StepGlobals& gl) {
-  std::unique_ptr<StepKernel, void (*)(StepKernel*)> k(new StepKernel, step_kernel_free);
-  std::vector<MkPhase> ph(d.size());
-  const uint32_t G = gl.nh / gl.nkv, Spad = (gl.splits + 3) & ~3u, eb = gl.kv_f16 ? 2u : 4u;
-  if (G == 0 || G > (uint32_t)AT_MAXG || gl.nh % gl.nkv) fail(FZ_EINVAL, "step kernel: GQA group %u unsupported", G);
-  if (gl.hd != 64 && gl.hd != 128) fail(FZ_EINVAL, "step kernel: head_dim %u unsupported", gl.hd);
-  if (gl.nkv * gl.splits > step_grid()) fail(FZ_EINVAL, "step kernel: %u attention CTAs", gl.nkv * gl.splits);
-  // records region: the largest resident input, two streamed chunks, and
-  // the attention scratch (queries, new k/v, per-warp partials; the merge)
-  uint32_t rec = 2 * GV_CREC, acc = 0;
-  rec = std::max(rec, (uint32_t)(MK_NREC * GV_CREC));
-  rec = std::max(rec, (AT_MAXG * gl.hd + 2 * gl.hd + 2 * MK_CWARPS + MK_CWARPS * gl.hd) * 4);
-  // the merge: each split's share of the group's 16-element runs spans at
-  // most two heads, and its values and weights fit the scratch
-  const uint32_t R = G * gl.hd / 16, share = 16 * ((R + gl.splits - 1) / gl.splits);
-  if (share > gl.hd) fail(FZ_EINVAL, "step kernel: %u splits too few for %u heads per KV head", gl.splits, G);
-  rec = std::max(rec, (share + 2 * Spad) * 4);
-  for (size_t i = 0; i < d.size(); i++) {
-    MkPhase& m = ph[i];
-    memset(&m, 0, sizeof m);
-    m.kind = d[i].kind;
-    m.wait_ctr = d[i].wait_ctr;
-    m.wait_target = d[i].wait_target;
-    m.arrive_ctr = d[i].arrive_ctr;
-    m.att_ctr0 = d[i].att_ctr0;
-    if (std::max({m.wait_ctr, m.arrive_ctr, m.att_ctr0 + gl.nkv}) > gl.nsync)
-      fail(FZ_EINVAL, "step kernel: counter index out of range");
-    if (m.kind == MK_GEMV) {
-      const GemvLaunch& g = d[i].g;
-      const uint32_t cols = g.seg[0].w.cols;
-      for (int j = 0; j < g.nseg; j++)
-        if (g.seg[j].w.cols != cols) fail(FZ_EINVAL, "step kernel: segments disagree on input width");
-      if (lay_nch(cols) > GV_MAX_CH || cols % 32) fail(FZ_EINVAL, "step kernel: input width %u unsupported", cols);
-      if (g.ar_push || g.ar_pull) fail(FZ_EINVAL, "step kernel: tensor-parallel exchange not supported");
-      fill_segs(g, m.seg);
-      m.nseg = g.nseg;
-      m.cols = cols;
-      m.epilogue = g.epilogue;
-      m.x = g.x;
-      m.norm_w = g.norm_w;
-      m.in_runs = reinterpret_cast<const XRun*>(g.in_runs);
-      m.out_runs = reinterpret_cast<XRun*>(g.out_runs);
-      m.idx_base = g.idx_base;
-      const uint32_t nx = runs_for(cols) * 64;
-      if (g.in_runs) {
-        m.in_kind = nx > 2 * GV_CREC ? MK_IN_RUNS_CHUNKED : MK_IN_RUNS;
-        if (m.in_kind == MK_IN_RUNS) rec = std::max(rec, nx);
-      } else {
-        if (!g.x || !g.norm_w) fail(FZ_EINVAL, "step kernel: an f32 input must be RMS-normalised");
-        if (cols / 4 > 8u * MK_NT) fail(FZ_EINVAL, "step kernel: input width %u too large", cols);
-        m.in_kind = MK_IN_NORM;
-        rec = std::max(rec, nx);
-      }
-      uint32_t tmax = 0;
-      for (int j = 0; j < g.nseg; j++) {
-        const GvSeg& s = m.seg[j];
-        tmax = std::max(tmax, lay_max_chunk_bytes(s.dtype, s.cols));
-        const uint32_t n = s.cta_end - s.cta_begin, units = s.rows / s.align;
-        m.max_rows = std::max(m.max_rows, s.align * ((units + n - 1) / n) + s.align);
-      }
-      m.rs = std::min<uint32_t>(MK_ROWS, MK_STAGE_MAX / tmax);
-      if (m.rs == 0) fail(FZ_EINVAL, "step kernel: a %u-byte row tile exceeds a ring stage", tmax);
-      acc = std::max(acc, m.max_rows);
-    } else {
-      const AttnLaunch& a = d[i].a;
-      if (2u * AT_TP * gl.hd * eb > MK_STAGE_MAX) fail(FZ_EINVAL, "step kernel: KV tile exceeds a ring stage");
-      m.kc = a.kcache;
-      m.vc = a.vcache;
-      m.out_runs = reinterpret_cast<XRun*>(a.ctx_runs);
-      m.ctx_run0 = a.ctx_run0;
-    }
-  }
-  int dev = 0, optin = 0;
-  CK(cudaGetDevice(&dev));
-  CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-  cudaFuncAttributes fa{};
-  CK(cudaFuncGetAttributes(&fa, k_step));
-  rec = (rec + 127) & ~127u;
-  const uint32_t fixed = rec + ((acc * 4 + 127) & ~127u) + 4 * (uint32_t)sizeof(MkPhase);
-  const int avail = (optin - (int)fa.sharedSizeBytes - (int)fixed) & ~127;
-  if (avail < 2 * (int)MK_STAGE_MAX) fail(FZ_EINVAL, "step kernel: shared memory too small for the ring");
-  const uint32_t ring = (uint32_t)avail;
-  k->smem = (size_t)ring + fixed;
-  // the largest size any step kernel may ask for (every build sets the same
-  // value, so a later build never lowers an earlier one's limit)
-  CK(cudaFuncSetAttribute(k_step, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes));
-  CK(cudaMalloc(&k->d_ph, ph.size() * sizeof(MkPhase)));
-  CK(cudaMemcpy(k->d_ph, ph.data(), ph.size() * sizeof(MkPhase), cudaMemcpyHostToDevice));
-  CK(cudaMalloc(&k->d_sync, (gl.nsync + 1) * sizeof(uint32_t)));
-  CK(cudaMemset(k->d_sync, 0, (gl.nsync + 1) * sizeof(uint32_t)));
-  MkParams& p = k->p;
-  p.ph = k->d_ph;
-  p.nph = (uint32_t)ph.size();
-  p.sync = k->d_sync;
-  p.nsync = gl.nsync + 1;
-  p.done_ctr = gl.done_ctr;
-  p.st = gl.st;
-  p.eps = gl.eps;
-  p.qkv = gl.qkv;
-  p.rope_cs = reinterpret_cast<const float2*>(gl.rope_cs);
-  p.partials = gl.partials;
-  p.ctx = gl.ctx;
-  p.nh = gl.nh;
-  p.nkv = gl.nkv;
-  p.hd = gl.hd;
-  p.max_ctx = gl.max_ctx;
-  p.splits = gl.splits;
-  p.kv_f16 = gl.kv_f16;
-  p.ring_bytes = ring;
-  p.rec_bytes = rec;
-  p.acc_floats = acc;
-  if (gl.done_ctr > gl.nsync) fail(FZ_EINVAL, "step kernel: reset counter out of range");
-  return k.release();
-}
-
-uint32_t step_kernel_phases(const StepKernel* k) { return k->p.nph; }
-
-// Cooperative launch: every CTA of the grid is resident at once, which the
-// phases' arrival counters need.
-void launch_step_kernel(const StepKernel* k, cudaStream_t s) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(step_grid());
-  cfg.blockDim = dim3(MK_THREADS);
-  cfg.dynamicSmemBytes = k->smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  CK(cudaLaunchKernelEx(&cfg, k_step, k->p));
 }
 
 // ---------------------------------------------------------------------------

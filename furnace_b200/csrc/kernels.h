@@ -46,9 +46,7 @@ struct StepState {
 enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_LOGITS = 3 };
 
 // Step-kernel timeline record (see trace_install): one per CTA per launch.
-// TR_GEMV + epilogue; TR_STEP + epilogue for the persistent step kernel's
-// GEMV phases, TR_STEP + 4 for its attention phases (aux = phase index)
-enum TraceTag : uint32_t { TR_GEMV = 0, TR_ATTN = 8, TR_COMBINE = 9, TR_STEP = 16 };
+enum TraceTag : uint32_t { TR_GEMV = 0, TR_ATTN = 8, TR_COMBINE = 9 };  // TR_GEMV + epilogue
 struct TraceRec {
   uint32_t tag, cta, aux, pad;
   uint64_t t[6];
@@ -98,6 +96,7 @@ struct GemvLaunch {
   uint32_t ar_w = 0, ar_rank = 0, ar_k = 0, ar_h = 0;
   const uint32_t* ar_base = nullptr;
   int ar_push = 0, ar_pull = 0;
+  uint64_t ar_spin_ns = 0;          // ar_pull wait limit (0: FURNACE_B200_WAIT_MS or 2 s)
 };
 
 void launch_gemv(const GemvLaunch& g, cudaStream_t s);
@@ -125,39 +124,6 @@ struct AttnLaunch {
 void launch_attention(const AttnLaunch& a, cudaStream_t s);
 uint32_t attention_splits(uint32_t n_kv);
 uint64_t attention_partial_floats(uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t splits);
-
-// ---- the whole decode step as one persistent kernel (step.cuh) --------------
-// Phases in execution order.  A GEMV phase reads its input as an RMS-
-// normalised f32 vector (g.x + g.norm_w) or as run records (g.in_runs); an
-// attention phase takes a.kcache / a.vcache / a.ctx_runs / a.ctx_run0 of its
-// layer.  Phase dependencies are arrival counters: a phase first waits until
-// counter wait_ctr reaches wait_target (0: no wait); every CTA adds one to
-// arrive_ctr when its GEMV outputs are written; an attention phase counts its
-// splits on att_ctr0 + KV head and its merges on arrive_ctr.
-struct StepPhaseDesc {
-  int kind = 0;  // 0: GEMV, 1: attention
-  GemvLaunch g;
-  AttnLaunch a{};
-  uint32_t wait_ctr = 0, wait_target = 0, arrive_ctr = 0, att_ctr0 = 0;
-};
-struct StepGlobals {
-  const float* qkv;
-  const float* rope_cs;
-  float* partials;
-  float* ctx;              // f32 attention output (optional)
-  uint32_t nh, nkv, hd, max_ctx, splits;
-  int kv_f16;
-  StepState* st;
-  float eps;
-  uint32_t nsync, done_ctr;  // counters used by the phases; the reset counter
-};
-struct StepKernel;
-StepKernel* step_kernel_build(const std::vector<StepPhaseDesc>& phases, const StepGlobals& gl);
-void step_kernel_free(StepKernel* k);
-void launch_step_kernel(const StepKernel* k, cudaStream_t s);
-uint32_t step_kernel_phases(const StepKernel* k);
-uint32_t step_splits(uint32_t n_kv);  // attention splits per KV head in the step kernel
-uint32_t step_grid();
 
 // Step bookkeeping after the logits (argmax -> ids_out, next token, pos++;
 // ar_base, when set, advances by ar_step: the step's exchanges).

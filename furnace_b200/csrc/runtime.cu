@@ -129,15 +129,11 @@ struct fz_kv {
   }
   DevBuf k, v, rope_cs, partials, state, forced, ids;
   cudaGraphExec_t g_full = nullptr, g_layers = nullptr;
-  StepKernel *mk_full = nullptr, *mk_layers = nullptr;  // persistent step kernels of the graphs
   // device memory and graphs back; the handle stays valid for fz_kv_free
   void release() {
     if (g_full) cudaGraphExecDestroy(g_full);
     if (g_layers) cudaGraphExecDestroy(g_layers);
     g_full = g_layers = nullptr;
-    step_kernel_free(mk_full);
-    step_kernel_free(mk_layers);
-    mk_full = mk_layers = nullptr;
     for (DevBuf* b : {&k, &v, &rope_cs, &partials, &state, &forced, &ids}) b->release();
   }
   ~fz_kv() { release(); }
@@ -172,18 +168,84 @@ uint64_t gguf_bytes(uint32_t dtype, uint64_t rows, uint32_t cols) {
   return rows * (cols / be) * bb;
 }
 
+// Host-to-device weight upload through two pinned host buffers and two device
+// staging buffers: while the GPU copies one chunk and repacks it into the
+// device layout, host threads gather the next chunk from the (memory-mapped)
+// GGUF bytes into the other pinned buffer.
+struct Uploader {
+  cudaStream_t s;
+  size_t cap;
+  uint8_t* host[2] = {nullptr, nullptr};
+  DevBuf dev[2];
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  bool busy[2] = {false, false};
+  int cur = 0;
+  unsigned nthreads;
+
+  Uploader(cudaStream_t st, size_t c) : s(st), cap(c) {
+    nthreads = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    for (int i = 0; i < 2; i++) {
+      CK(cudaMallocHost(&host[i], cap));
+      dev[i].alloc(cap);
+      CK(cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming));
+    }
+  }
+  ~Uploader() {
+    cudaStreamSynchronize(s);
+    for (int i = 0; i < 2; i++) {
+      if (host[i]) cudaFreeHost(host[i]);
+      if (ev[i]) cudaEventDestroy(ev[i]);
+    }
+  }
+  Uploader(const Uploader&) = delete;
+  Uploader& operator=(const Uploader&) = delete;
+
+  // Pack `segs` (host source, bytes) back to back into the free pinned
+  // buffer, copy it to the device and run post(device pointer) on the
+  // stream.  The segments' bytes must total at most cap.
+  template <class Post>
+  void push(const std::vector<std::pair<const uint8_t*, size_t>>& segs, Post post) {
+    if (busy[cur]) CK(cudaEventSynchronize(ev[cur]));
+    size_t total = 0;
+    for (auto& g : segs) total += g.second;
+    need(total <= cap, "upload chunk of %zu bytes exceeds the staging buffer", total);
+    // split the bytes evenly over the threads, each copying its byte range
+    // across segment boundaries
+    uint8_t* dst = host[cur];
+    auto work = [&](size_t b0, size_t b1) {
+      size_t off = 0;
+      for (auto& g : segs) {
+        const size_t a = std::max(b0, off), e = std::min(b1, off + g.second);
+        if (a < e) memcpy(dst + a, g.first + (a - off), e - a);
+        off += g.second;
+        if (off >= b1) break;
+      }
+    };
+    const unsigned T = total >= (4u << 20) ? nthreads : 1u;
+    std::vector<std::thread> th;
+    for (unsigned t = 1; t < T; t++) th.emplace_back(work, total * t / T, total * (t + 1) / T);
+    work(0, total / T);
+    for (auto& x : th) x.join();
+    CK(cudaMemcpyAsync(dev[cur].p, host[cur], total, cudaMemcpyHostToDevice, s));
+    post(dev[cur].as<uint8_t>());
+    CK(cudaEventRecord(ev[cur], s));
+    busy[cur] = true;
+    cur ^= 1;
+  }
+  void finish() { CK(cudaStreamSynchronize(s)); }
+};
+
 // Upload `rows` GGUF rows of a [rows, cols] weight (raw host bytes) into the
-// device layout at dst, through a bounded device staging buffer.
-void upload_rows(uint32_t dtype, const uint8_t* raw, uint64_t rows, uint32_t cols, uint8_t* dst, DevBuf& staging,
-                 cudaStream_t s) {
-  uint64_t row_raw = gguf_bytes(dtype, 1, cols);
-  uint64_t chunk_rows = staging.n / row_raw;
+// device layout at dst.
+void upload_rows(uint32_t dtype, const uint8_t* raw, uint64_t rows, uint32_t cols, uint8_t* dst, Uploader& up) {
+  const uint64_t row_raw = gguf_bytes(dtype, 1, cols);
+  const uint64_t chunk_rows = up.cap / row_raw;
   need(chunk_rows > 0, "staging buffer too small");
   for (uint64_t r0 = 0; r0 < rows; r0 += chunk_rows) {
-    uint64_t nr = std::min(chunk_rows, rows - r0);
-    CK(cudaMemcpyAsync(staging.p, raw + r0 * row_raw, nr * row_raw, cudaMemcpyHostToDevice, s));
-    launch_repack(dtype, staging.as<uint8_t>(), dst, (uint32_t)r0, (uint32_t)nr, (uint32_t)rows, cols, s);
-    CK(cudaStreamSynchronize(s));
+    const uint64_t nr = std::min(chunk_rows, rows - r0);
+    up.push({{raw + r0 * row_raw, nr * row_raw}}, [&](const uint8_t* d) {
+      launch_repack(dtype, d, dst, (uint32_t)r0, (uint32_t)nr, (uint32_t)rows, cols, up.s);
+    });
   }
 }
 
@@ -257,20 +319,20 @@ void nccl_comm_check(ncclComm_t* comm, ncclResult_t r, const char* what) {
 // Upload rows [0, rows) restricted to input columns [col0, col0 + ncols)
 // (block-aligned) of a [rows, cols] GGUF weight: rows are gathered on the host.
 void upload_cols(uint32_t dtype, const uint8_t* raw, uint64_t rows, uint32_t cols, uint32_t col0, uint32_t ncols,
-                 uint8_t* dst, DevBuf& staging, cudaStream_t s) {
+                 uint8_t* dst, Uploader& up) {
   uint32_t be, bb;
   block_geom(dtype, &be, &bb);
   need(col0 % be == 0 && ncols % be == 0 && col0 + ncols <= cols, "column slice not block-aligned");
   const uint64_t row_raw = gguf_bytes(dtype, 1, cols), sl_raw = gguf_bytes(dtype, 1, ncols);
   const uint64_t off = (uint64_t)(col0 / be) * bb;
-  const uint64_t chunk_rows = std::max<uint64_t>(1, staging.n / sl_raw);
-  std::vector<uint8_t> host(std::min(chunk_rows, rows) * sl_raw);
+  const uint64_t chunk_rows = std::max<uint64_t>(1, up.cap / sl_raw);
   for (uint64_t r0 = 0; r0 < rows; r0 += chunk_rows) {
     const uint64_t nr = std::min(chunk_rows, rows - r0);
-    for (uint64_t r = 0; r < nr; r++) memcpy(&host[r * sl_raw], raw + (r0 + r) * row_raw + off, sl_raw);
-    CK(cudaMemcpyAsync(staging.p, host.data(), nr * sl_raw, cudaMemcpyHostToDevice, s));
-    launch_repack(dtype, staging.as<uint8_t>(), dst, (uint32_t)r0, (uint32_t)nr, (uint32_t)rows, ncols, s);
-    CK(cudaStreamSynchronize(s));
+    std::vector<std::pair<const uint8_t*, size_t>> segs(nr);
+    for (uint64_t r = 0; r < nr; r++) segs[r] = {raw + (r0 + r) * row_raw + off, sl_raw};
+    up.push(segs, [&](const uint8_t* d) {
+      launch_repack(dtype, d, dst, (uint32_t)r0, (uint32_t)nr, (uint32_t)rows, ncols, up.s);
+    });
   }
 }
 
@@ -456,86 +518,6 @@ void record_step(fz_kv* kv, bool with_logits, cudaStream_t s, OpHook* hook = nul
   launch_finalize(st, kv->forced.as<uint32_t>(), kv->ids.as<uint32_t>(), with_logits, s,
                   xch ? m->ar_base.as<uint32_t>() : nullptr, xch ? 2 * c.n_layers : 0);
   H(FZ_OP_FINALIZE, false);
-}
-
-// The step as one persistent kernel (kernels.cu: step.cuh): the phases of
-// every layer and lm_head with their arrival counters.  Counter block of
-// layer l: 16 l + {0: q|k|v written, 1: attention merges, 2: o_proj, 3:
-// gate/up, 4: down, 8 + g: attention splits of KV head g}.
-bool step_kernel_enabled(const fz_model* m) {
-  if (m->world > 1) return false;  // the tensor-parallel exchange runs on the per-kernel path
-  const char* e = getenv("FURNACE_B200_STEP");
-  return e && e[0] == '1';
-}
-
-StepKernel* build_step_kernel(fz_kv* kv, bool with_logits) {
-  fz_model* m = kv->m;
-  const fz_config& c = m->cfg;
-  const std::vector<GemvLaunch> gl = step_gemvs(kv);
-  const uint32_t grid = step_grid(), S = step_splits(m->nkv_l), L = c.n_layers;
-  auto base = [](uint32_t l) { return 16 * l; };
-  std::vector<StepPhaseDesc> ph;
-  for (uint32_t l = 0; l < L; l++) {
-    StepPhaseDesc q, a, o, u, d;
-    q.g = gl[4 * l];
-    if (l) {
-      q.wait_ctr = base(l - 1) + 4;
-      q.wait_target = grid;
-    }
-    q.arrive_ctr = base(l);
-    a.kind = 1;
-    a.a = layer_attention(kv, l, S);
-    a.wait_ctr = base(l);
-    a.wait_target = grid;
-    a.arrive_ctr = base(l) + 1;
-    a.att_ctr0 = base(l) + 8;
-    o.g = gl[4 * l + 1];
-    o.wait_ctr = base(l) + 1;
-    o.wait_target = m->nkv_l * S;  // every attention CTA arrives after merging its share
-    o.arrive_ctr = base(l) + 2;
-    u.g = gl[4 * l + 2];
-    u.wait_ctr = base(l) + 2;
-    u.wait_target = grid;
-    u.arrive_ctr = base(l) + 3;
-    d.g = gl[4 * l + 3];
-    d.wait_ctr = base(l) + 3;
-    d.wait_target = grid;
-    d.arrive_ctr = base(l) + 4;
-    for (StepPhaseDesc* x : {&q, &a, &o, &u, &d}) ph.push_back(*x);
-  }
-  if (with_logits) {
-    StepPhaseDesc lm;
-    lm.g = gl[4 * L];
-    lm.wait_ctr = base(L - 1) + 4;
-    lm.wait_target = grid;
-    lm.arrive_ctr = 16 * L + 1;
-    ph.push_back(lm);
-  }
-  StepGlobals g{};
-  g.qkv = m->qkv.as<float>();
-  g.rope_cs = kv->rope_cs.as<float>();
-  g.partials = kv->partials.as<float>();
-  g.ctx = m->ctx.as<float>();
-  g.nh = m->nh_l;
-  g.nkv = m->nkv_l;
-  g.hd = c.head_dim;
-  g.max_ctx = kv->max_ctx;
-  g.splits = S;
-  g.kv_f16 = kv->eb == 2;
-  g.st = kv->state.as<StepState>();
-  g.eps = c.rms_eps;
-  g.nsync = 16 * L + 2;
-  g.done_ctr = 16 * L;
-  return step_kernel_build(ph, g);
-}
-
-// One step through the persistent kernel: embed, the step kernel, finalize.
-void record_step_mk(fz_kv* kv, bool with_logits, cudaStream_t s) {
-  fz_model* m = kv->m;
-  StepState* st = kv->state.as<StepState>();
-  launch_embed(m->embd, st, m->x.as<float>(), s);
-  launch_step_kernel(with_logits ? kv->mk_full : kv->mk_layers, s);
-  launch_finalize(st, kv->forced.as<uint32_t>(), kv->ids.as<uint32_t>(), with_logits, s);
 }
 
 // ---- batched prefill on the tensor cores ------------------------------------
@@ -770,19 +752,11 @@ uint32_t sample_device(fz_model* m, fz_sampler* s, const uint32_t* recent, uint3
 void build_graphs(fz_kv* kv) {
   if (kv->g_full) return;
   cudaStream_t s = kv->m->stream;
-  const bool mk = step_kernel_enabled(kv->m);
-  if (mk) {
-    kv->mk_full = build_step_kernel(kv, true);
-    kv->mk_layers = build_step_kernel(kv, false);
-  }
   for (int variant = 0; variant < 2; variant++) {
     cudaGraph_t g;
     CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
     try {
-      if (mk)
-        record_step_mk(kv, variant == 0, s);
-      else
-        record_step(kv, variant == 0, s);
+      record_step(kv, variant == 0, s);
     } catch (...) {
       cudaStreamEndCapture(s, &g);
       if (g) cudaGraphDestroy(g);
@@ -839,16 +813,6 @@ void check_state(fz_kv* kv) {
   CK(cudaStreamSynchronize(kv->m->stream));
   // codes 1-2: token >= vocab, position >= max_ctx; 3-5 and 7: a bounded
   // device wait (input records, ring slot, KV tile; residual exchange) ran out
-  if (st.error && kv->mk_full) {
-    // a step kernel that stopped early leaves its arrival counters behind:
-    // rebuild the graphs and step kernels (fresh counters) on the next use
-    if (kv->g_full) cudaGraphExecDestroy(kv->g_full);
-    if (kv->g_layers) cudaGraphExecDestroy(kv->g_layers);
-    kv->g_full = kv->g_layers = nullptr;
-    step_kernel_free(kv->mk_full);
-    step_kernel_free(kv->mk_layers);
-    kv->mk_full = kv->mk_layers = nullptr;
-  }
   if (st.error >= 3) fail(FZ_ETIMEOUT, "a bounded device wait ran out (code %u)", st.error);
   if (st.error) fail(FZ_EINVAL, "device step rejected its input (code %u)", st.error);
 }
@@ -870,87 +834,6 @@ void step_bytes(const fz_model* m, const fz_kv* kv, uint64_t pos, double* bytes)
     bytes[FZ_OP_DOWN] += L.wd.gguf_bytes + (F + 2 * H) * 4;
   }
   bytes[FZ_OP_LMHEAD] += m->lm_head.gguf_bytes + (2 * H + (uint64_t)c.vocab) * 4;
-}
-
-// fz_step_profile on the captured step (persistent kernel): the step kernel
-// records %globaltimer per CTA and phase; an op's time is the span from the
-// end of the previous phase (the last CTA to finish it) to the end of its own
-// phase, so the ops of a token add up to the kernel's span.  The rest of the
-// token period (embedding, step bookkeeping, launch gaps, from CUDA events
-// around the replays) is reported under FZ_OP_EMBED.
-void step_profile_graph(fz_model* m, fz_kv* kv, uint32_t first, uint32_t reps, double* ms, double* bytes,
-                        uint32_t* launches) {
-  for (int k = 0; k < FZ_OP_COUNT; k++) ms[k] = bytes[k] = launches[k] = 0;
-  if (!reps) return;
-  cudaStream_t s = m->stream;
-  build_graphs(kv);
-  const uint32_t nph = step_kernel_phases(kv->mk_full), grid = step_grid(), L = m->cfg.n_layers;
-  const uint64_t cap = 2ull * reps * nph * grid + 64;  // consumer and producer records
-  DevBuf tb(cap * sizeof(TraceRec));
-  trace_install(tb.as<TraceRec>(), (uint32_t)cap);
-  struct Restore {
-    fz_model* m;
-    ~Restore() {
-      try {
-        if (m->trace.p)
-          trace_install(m->trace.as<TraceRec>(), (uint32_t)(m->trace.n / sizeof(TraceRec)));
-        else
-          trace_install(nullptr, 0);
-      } catch (...) {
-      }
-    }
-  } restore{m};
-  cudaEvent_t e0, e1;
-  CK(cudaEventCreate(&e0));
-  CK(cudaEventCreate(&e1));
-  CK(cudaMemcpyAsync(kv->forced.p, &first, 4, cudaMemcpyHostToDevice, s));
-  set_state(kv, kv->len, first, 1);
-  CK(cudaEventRecord(e0, s));
-  for (uint32_t r = 0; r < reps; r++) CK(cudaGraphLaunch(kv->g_full, s));
-  CK(cudaEventRecord(e1, s));
-  CK(cudaStreamSynchronize(s));
-  float total = 0;
-  CK(cudaEventElapsedTime(&total, e0, e1));
-  cudaEventDestroy(e0);
-  cudaEventDestroy(e1);
-  check_state(kv);
-  const uint32_t n = std::min<uint32_t>(trace_count(), (uint32_t)cap);
-  std::vector<TraceRec> rec(n);
-  if (n) CK(cudaMemcpy(rec.data(), tb.p, (size_t)n * sizeof(TraceRec), cudaMemcpyDeviceToHost));
-  // consumer records (tags TR_STEP + 0..4; the producer's are TR_STEP + 8):
-  // nph * grid per token, tokens in launch order (kernel boundaries order
-  // them); inside one token, aux is the phase index
-  std::vector<const TraceRec*> cons;
-  cons.reserve(n);
-  for (uint32_t i = 0; i < n; i++)
-    if (rec[i].tag >= TR_STEP && rec[i].tag < TR_STEP + 8) cons.push_back(&rec[i]);
-  need(cons.size() == (uint64_t)reps * nph * grid, "step trace: %zu records, expected %llu", cons.size(),
-       (unsigned long long)reps * nph * grid);
-  double span_ms = 0;
-  for (uint32_t r = 0; r < reps; r++) {
-    std::vector<uint64_t> t0(nph, ~0ull), t4(nph, 0);
-    for (uint64_t i = (uint64_t)r * nph * grid; i < (uint64_t)(r + 1) * nph * grid; i++) {
-      const TraceRec& x = *cons[i];
-      need(x.aux < nph, "step trace: bad phase index");
-      t0[x.aux] = std::min(t0[x.aux], x.t[0]);
-      t4[x.aux] = std::max(t4[x.aux], x.t[4]);
-    }
-    uint64_t prev = t0[0];
-    for (uint32_t k = 0; k < nph; k++) {
-      static const int kLayerOps[5] = {FZ_OP_QKV, FZ_OP_ATTN, FZ_OP_OPROJ, FZ_OP_GATEUP, FZ_OP_DOWN};
-      const int op = k == L * 5 ? FZ_OP_LMHEAD : kLayerOps[k % 5];
-      const uint64_t end = std::max(t4[k], prev);
-      ms[op] += (double)(end - prev) * 1e-6;
-      launches[op] += 1;
-      prev = end;
-    }
-    span_ms += (double)(prev - t0[0]) * 1e-6;
-  }
-  ms[FZ_OP_EMBED] = std::max(0.0, (double)total - span_ms);
-  launches[FZ_OP_EMBED] = reps;
-  launches[FZ_OP_FINALIZE] = reps;
-  for (uint32_t r = 0; r < reps; r++) step_bytes(m, kv, kv->len + r, bytes);
-  kv->len += reps;
 }
 
 }  // namespace
@@ -1208,39 +1091,38 @@ std::unique_ptr<fz_model> load_model(const fz_file* f, int rank, int world, cons
   for (auto& o : order) o.first->ptr = base + o.second;
   uint64_t max_raw = 0;
   for (auto& u : ups) max_raw = std::max<uint64_t>(max_raw, u.dst->gguf_bytes);
-  DevBuf staging(std::min<uint64_t>(max_raw + 16, 256ull << 20));
+  Uploader up(m->stream, std::min<uint64_t>(max_raw + 16, 64ull << 20));
   for (auto& u : ups) {
     DevMat& d = *u.dst;
     uint64_t nb;
     const uint8_t* raw = g.tensor_data(*u.t, &nb);
     if (u.col0 == 0 && d.cols == u.in_d)
-      upload_rows(d.dtype, raw + u.row0 * gguf_bytes(d.dtype, 1, u.in_d), d.rows, d.cols, d.ptr, staging, m->stream);
+      upload_rows(d.dtype, raw + u.row0 * gguf_bytes(d.dtype, 1, u.in_d), d.rows, d.cols, d.ptr, up);
     else
-      upload_cols(d.dtype, raw, d.rows, u.in_d, u.col0, d.cols, d.ptr, staging, m->stream);
+      upload_cols(d.dtype, raw, d.rows, u.in_d, u.col0, d.cols, d.ptr, up);
   }
   if (share_embd) m->lm_head = m->embd;
   // gate/up interleaved by row: row 2i = gate_(ffn0+i), row 2i+1 = up_(ffn0+i)
-  {
-    DevBuf tmp(2 * gguf_bytes(gates[0]->dtype, 1, H) * 512 + 16);
-    for (uint32_t i = 0; i < c.n_layers; i++) {
-      DevMat& d = m->layers[i].wgu;
-      uint64_t nb;
-      const uint8_t* graw = g.tensor_data(*gates[i], &nb);
-      const uint8_t* uraw = g.tensor_data(*upsw[i], &nb);
-      uint64_t rb = gguf_bytes(d.dtype, 1, H);
-      std::vector<uint8_t> hbuf(rb * 2 * 512);
-      for (uint32_t r0 = 0; r0 < F_l; r0 += 512) {
-        uint32_t nr = std::min<uint32_t>(512, F_l - r0);
-        for (uint32_t r = 0; r < nr; r++) {
-          memcpy(&hbuf[(2 * r) * rb], graw + (uint64_t)(sl.ffn0 + r0 + r) * rb, rb);
-          memcpy(&hbuf[(2 * r + 1) * rb], uraw + (uint64_t)(sl.ffn0 + r0 + r) * rb, rb);
-        }
-        CK(cudaMemcpyAsync(tmp.p, hbuf.data(), 2 * nr * rb, cudaMemcpyHostToDevice, m->stream));
-        launch_repack(d.dtype, tmp.as<uint8_t>(), d.ptr, 2 * r0, 2 * nr, d.rows, H, m->stream);
-        CK(cudaStreamSynchronize(m->stream));
+  for (uint32_t i = 0; i < c.n_layers; i++) {
+    DevMat& d = m->layers[i].wgu;
+    uint64_t nb;
+    const uint8_t* graw = g.tensor_data(*gates[i], &nb);
+    const uint8_t* uraw = g.tensor_data(*upsw[i], &nb);
+    const uint64_t rb = gguf_bytes(d.dtype, 1, H);
+    const uint32_t per = (uint32_t)std::max<uint64_t>(1, up.cap / (2 * rb));
+    for (uint32_t r0 = 0; r0 < F_l; r0 += per) {
+      const uint32_t nr = std::min<uint32_t>(per, F_l - r0);
+      std::vector<std::pair<const uint8_t*, size_t>> segs(2 * nr);
+      for (uint32_t r = 0; r < nr; r++) {
+        segs[2 * r] = {graw + (uint64_t)(sl.ffn0 + r0 + r) * rb, rb};
+        segs[2 * r + 1] = {uraw + (uint64_t)(sl.ffn0 + r0 + r) * rb, rb};
       }
+      up.push(segs, [&](const uint8_t* dv) {
+        launch_repack(d.dtype, dv, d.ptr, 2 * r0, 2 * nr, d.rows, H, m->stream);
+      });
     }
   }
+  up.finish();
   // norms (replicated) and this rank's q/k/v bias slices
   std::vector<float> smalls;
   std::vector<std::pair<size_t, float**>> fix;
@@ -1713,10 +1595,6 @@ int fz_step_profile(fz_model* m, fz_kv* kv, uint32_t first, uint32_t reps, doubl
     need((uint64_t)kv->len + reps <= kv->max_ctx, "context overflow: %u + %u > max_ctx %u", kv->len, reps, kv->max_ctx);
     use_device(m);
     cudaStream_t s = m->stream;
-    if (step_kernel_enabled(m)) {
-      step_profile_graph(m, kv, first, reps, ms, bytes, launches);
-      return;
-    }
     struct Hook : OpHook {
       std::vector<cudaEvent_t> ev;
       std::vector<int> ops;
@@ -1754,6 +1632,58 @@ int fz_step_profile(fz_model* m, fz_kv* kv, uint32_t first, uint32_t reps, doubl
   });
 }
 
+int fz_selftest_exchange_timeout(int device, uint32_t limit_us) {
+  return guard([&] {
+    need(limit_us > 0, "zero wait limit");
+    CK(cudaSetDevice(device));
+    kernels_init();
+    cudaStream_t s;
+    CK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    struct Hold {
+      cudaStream_t s;
+      ~Hold() {
+        cudaStreamSynchronize(s);
+        cudaStreamDestroy(s);
+      }
+    } hold{s};
+    // a 32 x 256 Q8_0 weight of zero bytes whose RMS-normalised input is the
+    // exchanged residual of ranks {0, 1}; rank 1 never sends
+    const uint32_t H = 256, R = 32;
+    DevMat w;
+    w.dtype = FZ_Q8_0;
+    w.rows = R;
+    w.cols = H;
+    w.stride = dev_row_stride(FZ_Q8_0, H);
+    DevBuf wb((uint64_t)R * w.stride + 256), xb(H * 4), nb(H * 4), yb(R * 4), arb(ar_buffer_bytes(H, 2)), base(16),
+        st(sizeof(StepState));
+    for (DevBuf* b : {&wb, &xb, &yb, &arb, &base, &st}) CK(cudaMemsetAsync(b->p, 0, b->n, s));
+    std::vector<float> ones(H, 1.0f);
+    CK(cudaMemcpyAsync(nb.p, ones.data(), H * 4, cudaMemcpyHostToDevice, s));
+    w.ptr = wb.as<uint8_t>();
+    GemvLaunch g;
+    g.seg[0] = GemvSeg{w, nullptr, yb.as<float>()};
+    g.x = xb.as<float>();
+    g.norm_w = nb.as<float>();
+    g.eps = 1e-6f;
+    g.epilogue = EPI_STORE;
+    g.state = st.as<StepState>();
+    g.ar_peers.buf[0] = g.ar_peers.buf[1] = arb.as<float>();
+    g.ar_w = 2;
+    g.ar_rank = 0;
+    g.ar_k = 0;
+    g.ar_h = H;
+    g.ar_base = base.as<uint32_t>();
+    g.ar_pull = 1;
+    g.ar_spin_ns = (uint64_t)limit_us * 1000;
+    launch_gemv(g, s);
+    StepState out{};
+    CK(cudaMemcpyAsync(&out, st.p, sizeof out, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    if (out.error == 7) fail(FZ_ETIMEOUT, "exchange wait ran out after %u us per word (as intended)", limit_us);
+    fail(FZ_EINVAL, "the exchange wait did not run out (error word %u)", out.error);
+  });
+}
+
 // ---- kernel-level entry points -------------------------------------------
 int fz_weight_upload(uint32_t dtype, const void* raw, size_t nbytes, uint32_t d_out, uint32_t d_in, fz_weight** out) {
   return guard([&] {
@@ -1775,8 +1705,11 @@ int fz_weight_upload(uint32_t dtype, const void* raw, size_t nbytes, uint32_t d_
     w->m.ptr = w->buf.as<uint8_t>();
     w->runs.alloc((uint64_t)runs_for(d_in) * 64);
     CK(cudaMemset(w->runs.p, 0, w->runs.n));
-    DevBuf staging(std::min<uint64_t>(nbytes + 16, 256ull << 20));
-    upload_rows(dtype, (const uint8_t*)raw, d_out, d_in, w->m.ptr, staging, 0);
+    {
+      Uploader up(0, std::min<uint64_t>(nbytes + 16, 64ull << 20));
+      upload_rows(dtype, (const uint8_t*)raw, d_out, d_in, w->m.ptr, up);
+      up.finish();
+    }
     *out = w.release();
   });
 }

@@ -278,6 +278,17 @@ int fz_matmul_quant(const float* a, uint32_t seq, const void* raw, size_t nbytes
  * blocks of a [d_out, d_in] weight (its size follows from the type). */
 int fz_gemv(uint32_t dtype, const void* raw, uint32_t d_out, uint32_t d_in, const float* x, float* y);
 
+/* ---- Failure detection self-test ---------------------------------------- */
+/* No counterpart in the reference (which has no multi-rank path; it panics on
+ * misuse, src/model.rs:348-352).  Runs, on `device`, one GEMV whose input is
+ * the tensor-parallel exchange of a 2-rank group in which the peer never
+ * writes: every word it polls stays stale, the bounded wait runs out after
+ * `limit_us` microseconds per word, the kernel records error 7 and returns,
+ * and this call reports FZ_ETIMEOUT (FZ_EINVAL if the wait did not run out).
+ * The device stays usable.  The same limit applies to real exchanges through
+ * FURNACE_B200_WAIT_MS (default 2000). */
+int fz_selftest_exchange_timeout(int device, uint32_t limit_us);
+
 /* ---- Device-resident variants (inputs already in HBM) --------------------- */
 /* Same as fz_matmul_quant with device pointers and a CUDA stream
  * (cudaStream_t passed as void*).  `w_dev` must come from fz_weight_upload. */

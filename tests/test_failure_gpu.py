@@ -49,3 +49,22 @@ def test_peer_that_never_joins_ends_in_a_timeout(tmp_path, monkeypatch, orc):
     got, _ = dev.forward(ids, kd)
     want = ref.forward_cached(ids, ref.kv_new(16))
     assert np.abs(got - want).max() <= 1e-3
+
+
+def test_exchange_wait_runs_out_and_the_device_stays_usable(tmp_path, orc):
+    """The residual exchange of tensor parallelism polls peer words with a
+    bounded wait.  With a peer that never writes and a 20 ms limit, the GEMV
+    records error 7 and returns, the call reports FZ_ETIMEOUT, and the next
+    model on the device computes the oracle's logits."""
+    L = fz.load_library()
+    t0 = time.monotonic()
+    rc = L.fz_selftest_exchange_timeout(0, 20000)
+    assert rc == fz.FZ_ETIMEOUT, L.fz_last_error()
+    assert time.monotonic() - t0 < 30
+    path = synth.write(synth.spec("tiny"), str(tmp_path / "tiny.gguf"))
+    dev = fz.Model.load(fz.GgufFile.open(path))
+    ref = orc.Model(path)
+    ids = synth.prompt_ids(ref.vocab, 5, seed=4)
+    got, _ = dev.forward(ids, fz.KvCache(dev, 16))
+    want = ref.forward_cached(ids, ref.kv_new(16))
+    assert np.abs(got - want).max() <= 1e-3
