@@ -202,15 +202,20 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def ncu_traffic():
-    """DRAM bytes per GEMV launch from the committed ncu summary, if any."""
+def ncu_traffic(config: str, layers, tp: int):
+    """DRAM bytes of one decode token's k_gemv launches from the committed
+    ncu summary, when that summary was taken on this workload (same config,
+    full depth, one GPU); None otherwise."""
     p = os.path.join(ROOT, "profiles", "gemv_traffic.json")
-    if os.path.exists(p):
-        try:
-            return json.load(open(p))
-        except Exception:
-            return None
-    return None
+    if not os.path.exists(p):
+        return None
+    try:
+        d = json.load(open(p))
+    except Exception:
+        return None
+    if d.get("config") != config or layers is not None or tp != 1:
+        return None
+    return d
 
 
 def cpu_model() -> str:
@@ -389,7 +394,7 @@ def run_ours(args, dist):
     prof_ms = sum(v[0] for v in prof.values())
     ops = {o: {"ms_per_token": prof[o][0] / T, "share": prof[o][0] / prof_ms if prof_ms else None,
                "gbs": (prof[o][1] / (prof[o][0] / 1000.0) / 1e9) if prof[o][0] else None} for o in prof}
-    traffic = ncu_traffic()
+    traffic = ncu_traffic(args.config, args.layers, tp)
     roofline = {"kernel": "decode step (k_gemv x4, k_attn, k_attn_combine per layer; lm_head k_gemv)", "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": f"{peak_src} hbm_gbs (burst copy)",
                 "bytes_per_launch": bytes_tok, "launch_us": ms_tok * 1000.0,

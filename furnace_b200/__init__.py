@@ -47,6 +47,7 @@ EXPORTS = [
     "fz_generate", "fz_tokenizer_from_gguf", "fz_tokenizer_new", "fz_tokenizer_free", "fz_tokenizer_vocab_size",
     "fz_tokenizer_encode", "fz_tokenizer_decode", "fz_tokenizer_token_bytes", "fz_pretokenize", "fz_chat_template",
     "fz_utf8_stream_new", "fz_utf8_stream_free", "fz_utf8_stream_push", "fz_utf8_stream_flush",
+    "fz_selftest_exchange_timeout",
 ]
 
 OPS = ["embed", "qkv", "rope_append", "attention", "o_proj", "gate_up", "down", "lm_head", "finalize"]
