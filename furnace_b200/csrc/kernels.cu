@@ -464,6 +464,10 @@ constexpr int GV_CWARPS = 15;                      // consumer warps (16 warps p
 #define GV_RPW_DEF 2
 #endif
 constexpr int GV_RPW = GV_RPW_DEF;                 // rows per consumer warp per stage
+#ifndef GV_PAIRS_DEF
+#define GV_PAIRS_DEF 1
+#endif
+constexpr bool GV_PAIRS = GV_PAIRS_DEF;            // warp w: rows 2w, 2w+1 (else w, w + GV_CWARPS)
 constexpr int GV_ROWS = GV_CWARPS * GV_RPW;        // rows per stage
 constexpr int GV_THREADS = (GV_CWARPS + 1) * 32;   // + one producer warp
 constexpr int GV_NT = GV_CWARPS * 32;              // consumer threads
@@ -728,8 +732,8 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
 }
 
 // Consumer side of one CTA: all stages of the CTA's rows for format DT.
-// Warp w takes rows ra + w + GV_CWARPS*j (j < GV_RPW) of every stage; the
-// activation records of the whole input sit in shared memory (rec).
+// Warp w takes rows ra + 2w and ra + 2w + 1 of every stage; the activation
+// records of the whole input sit in shared memory (rec).
 // Chunk c's input records as record buffer use c (buffer c & 1, phase c / 2
 // of its mbarriers), once use c - 2 of that buffer has been released.  One
 // thread; the chunked-record mode of long inputs.
@@ -777,23 +781,28 @@ __device__ bool gv_consume(const GvParams& p, const StageIter& it, const ChunkIn
     for (uint32_t ra = it.r0; ra < it.r1; ra += GV_ROWS) {
       if (!mbar_wait(&full[slot], phase)) return false;
       const uint8_t* tile = ring + (size_t)slot * p.slot_bytes;
+      static_assert(GV_RPW == 2, "a warp takes two rows of a stage");
+      // warp w takes rows 2w and 2w + 1 of the stage; a warp past the stage's
+      // rows (short GEMVs: o_proj, down and qkv have 24-31 rows per CTA)
+      // skips the stage (warp-uniform), and an odd last row pairs with a
+      // clamped copy of itself whose sum is dropped
       const uint32_t last = it.r1 - 1 - ra;
-      float v[GV_RPW];
-#pragma unroll
-      for (int j = 0; j < GV_RPW; j++) {
-        const uint32_t rr = min(warp + GV_CWARPS * j, last);
-        v[j] = lane_on * unit_dot<DT>(tile + rr * tb, lu, nu, xr);
+      const uint32_t rw0 = GV_PAIRS ? 2 * warp : warp, rw1 = GV_PAIRS ? 2 * warp + 1 : warp + GV_CWARPS;
+      float v[2] = {0.f, 0.f};
+      if (!GV_PAIRS || rw0 <= last) {
+        v[0] = lane_on * unit_dot<DT>(tile + min(rw0, last) * tb, lu, nu, xr);
+        v[1] = lane_on * unit_dot<DT>(tile + min(rw1, last) * tb, lu, nu, xr);
       }
+      // both sums in one butterfly: the first step leaves row 0's pairs in
+      // lanes 0-15 and row 1's in lanes 16-31
+      const bool up = lane & 16;
+      float a = up ? v[1] : v[0];
+      a += __shfl_xor_sync(0xffffffffu, up ? v[0] : v[1], 16);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int j = 0; j < GV_RPW; j++) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
-      if (lane == 0) {
-#pragma unroll
-        for (int j = 0; j < GV_RPW; j++) {
-          uint32_t row = ra + warp + GV_CWARPS * j;
-          if (row < it.r1) acc[row - it.r0] += v[j];
-        }
+      for (int o = 8; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if ((lane & 15) == 0) {
+        const uint32_t rw = lane ? rw1 : rw0;
+        if (rw <= last) acc[ra - it.r0 + rw] += a;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
@@ -1355,35 +1364,12 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
   KT* tiles = reinterpret_cast<KT*>(smem);  // [NBUF][K|V][TP][HD]
   const KT* kvk = kc + (uint64_t)kvh * max_ctx * HD;
   const KT* kvv = vc + (uint64_t)kvh * max_ctx * HD;
-  Tracer tr;
-  if (tid == 0) {
-    tr.begin(TR_ATTN, gridDim.x * gridDim.y);
-    pdl_trigger();
-    // rows below the (possibly not yet advanced) position are final already:
-    // pull this block's share into L2 before waiting for the predecessor
-    uint32_t p0 = min(*((volatile uint32_t*)&st->pos), max_ctx - 1);
-    uint32_t per0 = (p0 + S) / S, a0 = min(split * per0, p0), a1 = min(p0, a0 + per0);
-    if (a1 > a0) {
-      bulk_prefetch(kvk + (uint64_t)a0 * HD, (a1 - a0) * HD * EB);
-      bulk_prefetch(kvv + (uint64_t)a0 * HD, (a1 - a0) * HD * EB);
-    }
-    for (int b = 0; b < AT_NBUF; b++) mbar_init(&bar[b], 1);
-    fence_barrier_init();
-  }
-  pdl_wait();
-  if (tid == 0) tr.mark(1);
-  const uint32_t pos = st->pos;
-  if (pos >= max_ctx) {
-    if (tid == 0) st->error = 2;
-    return;
-  }
-  const uint32_t total = pos + 1, per = (total + S - 1) / S;
-  const uint32_t t0 = min(split * per, total), t1 = min(total, t0 + per), n = t1 - t0;
-  const uint32_t ntiles = (n + AT_TP - 1) / AT_TP;
+  __shared__ uint32_t s_p0, s_pre;
   const uint64_t pol = policy_evict_first();
-  // tile j: positions [t0 + j*TP, ..); rows below pos come from the cache
-  auto issue = [&](uint32_t j) {
-    uint32_t b = j % AT_NBUF, a = t0 + j * AT_TP, e = min(min(t1, a + AT_TP), pos);
+  // tile j of a block owning positions [ta, tb) while the new position is pc:
+  // positions [ta + j*TP, ..) below pc come from the cache
+  auto issue = [&](uint32_t j, uint32_t ta, uint32_t tb, uint32_t pc) {
+    uint32_t b = j % AT_NBUF, a = ta + j * AT_TP, e = min(min(tb, a + AT_TP), pc);
     uint32_t rows = e > a ? e - a : 0;
     KT* kt = tiles + (size_t)b * 2 * AT_TP * HD;
     mbar_expect_tx(&bar[b], 2 * rows * HD * EB);
@@ -1392,9 +1378,58 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
       bulk_g2s(kt + AT_TP * HD, kvv + (uint64_t)a * HD, rows * HD * EB, &bar[b], pol);
     }
   };
+  Tracer tr;
+  if (tid == 0) {
+    tr.begin(TR_ATTN, gridDim.x * gridDim.y);
+    pdl_trigger();
+    for (int b = 0; b < AT_NBUF; b++) mbar_init(&bar[b], 1);
+    fence_barrier_init();
+  }
   __syncthreads();  // barrier init visible
+  if (tid == 0) {
+    // Rows below the position read here are final already (it is this step's
+    // position, or the previous step's if k_finalize has not published it
+    // yet): the first tiles of the share that position gives this block are
+    // copied before waiting for the predecessor, the rest of the share is
+    // pulled into L2.  After the wait, a block whose share moved (pos != p0)
+    // lets those copies land and starts over.
+    const uint32_t p0 = min(*((volatile uint32_t*)&st->pos), max_ctx - 1);
+    const uint32_t tot0 = p0 + 1, per0 = (tot0 + S - 1) / S;
+    const uint32_t a0 = min(split * per0, tot0), b0 = min(tot0, a0 + per0);
+    const uint32_t pre = min((b0 - a0 + AT_TP - 1) / AT_TP, (uint32_t)AT_NBUF);
+    for (uint32_t j = 0; j < pre; j++) issue(j, a0, b0, p0);
+    const uint32_t f0 = min(a0 + pre * AT_TP, p0), f1 = min(b0, p0);
+    if (f1 > f0) {
+      bulk_prefetch(kvk + (uint64_t)f0 * HD, (f1 - f0) * HD * EB);
+      bulk_prefetch(kvv + (uint64_t)f0 * HD, (f1 - f0) * HD * EB);
+    }
+    s_p0 = p0;
+    s_pre = pre;
+  }
+  pdl_wait();
+  if (tid == 0) tr.mark(1);
+  const uint32_t pos = st->pos;
+  __syncthreads();  // s_p0, s_pre
+  const uint32_t pre = s_pre;
+  const bool redo = pos != s_p0;  // block-uniform
+  if (redo || pos >= max_ctx) {
+    // the early copies land before their buffers are reused or the block exits
+    if (tid == 0)
+      for (uint32_t j = 0; j < pre; j++)
+        if (!mbar_wait(&bar[j], 0)) st->error = 5;
+    __syncthreads();
+  }
+  if (pos >= max_ctx) {
+    if (tid == 0) st->error = 2;
+    return;
+  }
+  const uint32_t total = pos + 1, per = (total + S - 1) / S;
+  const uint32_t t0 = min(split * per, total), t1 = min(total, t0 + per), n = t1 - t0;
+  const uint32_t ntiles = (n + AT_TP - 1) / AT_TP;
+  // parity of tile j's buffer: uses before it, plus the drained early copy
+  auto parity = [&](uint32_t j) { return ((j / AT_NBUF) + ((redo && (j % AT_NBUF) < pre) ? 1u : 0u)) & 1u; };
   if (tid == 0)
-    for (uint32_t j = 0; j < ntiles && j < (uint32_t)AT_NBUF; j++) issue(j);
+    for (uint32_t j = redo ? 0 : pre; j < ntiles && j < (uint32_t)AT_NBUF; j++) issue(j, t0, t1, pos);
   // rotated queries
   const float2* csp = cs + (uint64_t)pos * half;
   for (uint32_t idx = tid; idx < G * half; idx += AT_THREADS) {
@@ -1434,7 +1469,7 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
     const uint32_t b = j % AT_NBUF, a = t0 + j * AT_TP, tn = min(t1, a + AT_TP) - a;
     KT* kt = tiles + (size_t)b * 2 * AT_TP * HD;
     KT* vt = kt + AT_TP * HD;
-    if (!mbar_wait(&bar[b], (j / AT_NBUF) & 1)) {
+    if (!mbar_wait(&bar[b], parity(j))) {
       if (tid == 0) st->error = 5;
       return;
     }
@@ -1495,7 +1530,7 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
       }
     }
     __syncthreads();  // buffer b free
-    if (tid == 0 && j + AT_NBUF < ntiles) issue(j + AT_NBUF);
+    if (tid == 0 && j + AT_NBUF < ntiles) issue(j + AT_NBUF, t0, t1, pos);
   }
   // partials: stats [nkv][G][S] of (max, sum), then acc [nkv][G][HD][Spad]
   const uint32_t Spad = (S + 3) & ~3u;
