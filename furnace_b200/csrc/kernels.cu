@@ -1113,25 +1113,28 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
       s.out[row] = __fadd_rn(s.out[row], acc[i]);
     }
   } else if (p.epilogue == EPI_SWIGLU) {
-    // rows interleave gate/up: h = silu(gate) * up (src/tensor.rs:213-227)
-    float hv[4];
-    uint32_t np = nrows / 2;
-    for (uint32_t k = 0; k < 4; k++) {
-      uint32_t j = ctid + k * GV_NT;
-      hv[k] = 0.f;
-      if (j < np) {
-        float g = acc[2 * j], u = acc[2 * j + 1];
-        hv[k] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-        if (s.out) s.out[(it.r0 >> 1) + j] = hv[k];
+    // rows interleave gate/up: h = silu(gate) * up (src/tensor.rs:213-227).
+    // Thread i4 makes h of pairs 4 i4 .. 4 i4 + 3 and its quad turns them
+    // into one run record (the CTA's rows are whole 32-row units, so its h
+    // values are whole runs starting at run r0 / 32); warps past the CTA's
+    // pairs skip, the others run every lane through the quad shuffles
+    const uint32_t np = nrows / 2, n4 = np / 4;
+    for (uint32_t base = 0; base < n4; base += GV_NT) {
+      if (base + warp * 32 >= n4) break;  // warp-uniform
+      const uint32_t i4 = base + ctid;
+      const bool act = i4 < n4;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (act) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const uint32_t j = 4 * i4 + q;
+          const float g = acc[2 * j], u = acc[2 * j + 1];
+          v[q] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+          if (s.out) s.out[(it.r0 >> 1) + j] = v[q];
+        }
       }
+      if (p.out_runs) quad_to_run(v, i4 & 3, act ? p.out_runs : nullptr, it.r0 / 32 + (i4 >> 2));
     }
-    named_sync(1, GV_NT);
-    for (uint32_t k = 0; k < 4; k++) {
-      uint32_t j = ctid + k * GV_NT;
-      if (j < np) acc[j] = hv[k];
-    }
-    named_sync(1, GV_NT);
-    if (p.out_runs) values_to_runs(acc, np, nullptr, p.out_runs, it.r0 / 32, ctid, GV_NT);
   } else {
     unsigned long long best = 0;
     for (uint32_t i = ctid; i < nrows; i += GV_NT) {
@@ -1461,6 +1464,7 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
     kv_st(vdst + tid + half, vn[1]);
   }
   __syncthreads();
+  if (tid == 0) tr.mark(2);
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
   float m = -INFINITY, l = 0.f, acc[DPL];
 #pragma unroll
@@ -1532,6 +1536,7 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
     __syncthreads();  // buffer b free
     if (tid == 0 && j + AT_NBUF < ntiles) issue(j + AT_NBUF, t0, t1, pos);
   }
+  if (tid == 0) tr.mark(3);
   // partials: stats [nkv][G][S] of (max, sum), then acc [nkv][G][HD][Spad]
   const uint32_t Spad = (S + 3) & ~3u;
   if (warp < G) {
@@ -1595,23 +1600,25 @@ __global__ void k_attn_combine(const float* __restrict__ partials, float* __rest
   for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
   __syncwarp();
   const float* w = ws[warp];
-  float num = 0.f;
+  float n0 = 0.f, n1 = 0.f, n2 = 0.f, n3 = 0.f;  // four independent chains
 #pragma unroll
   for (int k = 0; k < AT_ACC_REGS; k++) {
     if (4u * k >= Spad) break;
-    num = fmaf(w[4 * k], av[k].x, num);
-    num = fmaf(w[4 * k + 1], av[k].y, num);
-    num = fmaf(w[4 * k + 2], av[k].z, num);
-    num = fmaf(w[4 * k + 3], av[k].w, num);
+    n0 = fmaf(w[4 * k], av[k].x, n0);
+    n1 = fmaf(w[4 * k + 1], av[k].y, n1);
+    n2 = fmaf(w[4 * k + 2], av[k].z, n2);
+    n3 = fmaf(w[4 * k + 3], av[k].w, n3);
   }
   for (uint32_t k = AT_ACC_REGS; 4 * k < Spad; k++) {
     float4 a4 = acc4[k];
-    num = fmaf(w[4 * k], a4.x, num);
-    num = fmaf(w[4 * k + 1], a4.y, num);
-    num = fmaf(w[4 * k + 2], a4.z, num);
-    num = fmaf(w[4 * k + 3], a4.w, num);
+    n0 = fmaf(w[4 * k], a4.x, n0);
+    n1 = fmaf(w[4 * k + 1], a4.y, n1);
+    n2 = fmaf(w[4 * k + 2], a4.z, n2);
+    n3 = fmaf(w[4 * k + 3], a4.w, n3);
   }
+  const float num = (n0 + n1) + (n2 + n3);
   const float v = __fdiv_rn(num, den);
+  if (threadIdx.x == 0) tr.mark(2);
   ctx[(uint64_t)h * hd + d] = v;
   // run records of ctx (the o_proj input): 8 runs per 128-wide head
   sv[d] = v;
