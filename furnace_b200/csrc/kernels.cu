@@ -29,6 +29,7 @@
 #include <cstring>
 #include <algorithm>
 #include <memory>
+#include <type_traits>
 #include <utility>
 #include <vector>
 
@@ -1466,9 +1467,13 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
   __syncthreads();
   if (tid == 0) tr.mark(2);
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
-  float m = -INFINITY, l = 0.f, acc[DPL];
+  float m = -INFINITY, l = 0.f, acc[DPL], qv[DPL];
 #pragma unroll
-  for (int d = 0; d < DPL; d++) acc[d] = 0.f;
+  for (int d = 0; d < DPL; d++) {
+    acc[d] = 0.f;
+    qv[d] = qs[warp < G ? warp : 0][lane * DPL + d];
+  }
+  (void)qv;
   for (uint32_t j = 0; j < ntiles; j++) {
     const uint32_t b = j % AT_NBUF, a = t0 + j * AT_TP, tn = min(t1, a + AT_TP) - a;
     KT* kt = tiles + (size_t)b * 2 * AT_TP * HD;
@@ -1489,20 +1494,35 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
     if (warp < G) {
       const uint32_t t = lane;
       float s = -INFINITY;
-      if (t < tn) {
-        const KT* kr = kt + (size_t)t * HD;
-        const float4* qr = reinterpret_cast<const float4*>(qs[warp]);
-        float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;  // four independent chains
-#pragma unroll 8
-        for (uint32_t c = 0; c < HD / 4; c++) {
-          uint32_t cc = (c + t) & (HD / 4 - 1);
-          float4 k4 = kv_ld4(kr, cc), q4 = qr[cc];
-          d0 = fmaf(q4.x, k4.x, d0);
-          d1 = fmaf(q4.y, k4.y, d1);
-          d2 = fmaf(q4.z, k4.z, d2);
-          d3 = fmaf(q4.w, k4.w, d3);
+      {
+        // lane L multiplies dims L*DPL.. of every row of the tile with its
+        // registers of q (each K row read once, 16 B per lane); then a
+        // transpose reduction over the 32 lanes leaves position t's score
+        // in lane t
+        float part[AT_TP];
+#pragma unroll
+        for (int r = 0; r < AT_TP; r++) {
+          part[r] = 0.f;
+          if ((uint32_t)r < tn) {  // warp-uniform
+            if constexpr (DPL == 4) {
+              const float4 k4 = kv_ld4(kt + (size_t)r * HD, lane);
+              part[r] = (qv[0] * k4.x + qv[1] * k4.y) + (qv[2] * k4.z + qv[3] * k4.w);
+            } else {
+              const KT* kr = kt + (size_t)r * HD + lane * DPL;
+              part[r] = qv[0] * kv_ld(kr) + qv[1] * kv_ld(kr + 1);
+            }
+          }
         }
-        s = __fmul_rn((d0 + d1) + (d2 + d3), scale);
+#pragma unroll
+        for (int o = AT_TP / 2; o > 0; o >>= 1) {
+          const bool up = lane & o;
+#pragma unroll
+          for (int i = 0; i < o; i++) {
+            const float keep = up ? part[i + o] : part[i], send = up ? part[i] : part[i + o];
+            part[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+          }
+        }
+        if (t < tn) s = __fmul_rn(part[0], scale);
       }
       float mt = s;
 #pragma unroll
@@ -1537,29 +1557,43 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
     if (tid == 0 && j + AT_NBUF < ntiles) issue(j + AT_NBUF, t0, t1, pos);
   }
   if (tid == 0) tr.mark(3);
-  // partials: stats [nkv][G][S] of (max, sum), then acc [nkv][G][HD][Spad]
-  const uint32_t Spad = (S + 3) & ~3u;
+  // partials: stats [nkv][G][S] of (max, sum), then acc [nkv][G][S][HD]
+  // (a split's weighted V is one contiguous row: coalesced stores here and
+  // coalesced loads in the combine)
   if (warp < G) {
     float2* stats = reinterpret_cast<float2*>(partials) + (uint64_t)kvh * G * S;
-    float* pacc = partials + ((2 * (uint64_t)nkv * G * S + 3) & ~3ull) + (uint64_t)kvh * G * HD * Spad;
+    float* pacc = partials + ((2 * (uint64_t)nkv * G * S + 3) & ~3ull) + (((uint64_t)kvh * G + warp) * S + split) * HD;
     if (lane == 0) stats[warp * S + split] = make_float2(m, l);
-#pragma unroll
-    for (int d = 0; d < DPL; d++) pacc[((uint64_t)warp * HD + lane * DPL + d) * Spad + split] = acc[d];
+    if constexpr (DPL == 4)
+      reinterpret_cast<float4*>(pacc)[lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    else
+      reinterpret_cast<float2*>(pacc)[lane] = make_float2(acc[0], acc[1]);
   }
   if (tid == 0) tr.mark(4);
 }
 
 // Merge the split partials: ctx[h][d] = sum_s w_s acc_s[d] / sum_s w_s l_s,
-// w_s = exp(m_s - max_s m_s).  Grid nh, block hd.  Every load of a thread --
-// its acc values and, per warp, the head's split statistics -- is issued
-// right after the wait, so the merge costs one L2 round trip; each warp
-// reduces the statistics itself (no block barrier before the sums).
+// w_s = exp(m_s - max_s m_s).  Grid nh, block AT_CB_THREADS (4 warps).  Warp
+// w takes splits w, w + 4, ...; lane L holds dims L*DPT .. L*DPT + DPT - 1
+// (DPT = hd / 32), so one load instruction of a warp reads one split's
+// contiguous row.  Every load of a thread -- its first AT_CB_REGS splits and,
+// per warp, the head's split statistics -- is issued right after the wait,
+// so the merge costs one L2 round trip; each warp reduces the statistics
+// itself.  The four warps' sums meet in shared memory, added in warp order
+// (split s mod 4 chains, then (c0 + c1) + (c2 + c3)).
 constexpr int AT_MAXS = 256;
-constexpr int AT_ACC_REGS = 24;  // float4 acc loads held in registers (splits <= 96 in one pass)
-__global__ void k_attn_combine(const float* __restrict__ partials, float* __restrict__ ctx, XRun* __restrict__ ctx_runs,
-                               uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t S, StepState* st, uint32_t run0) {
+constexpr int AT_CB_THREADS = 128;
+constexpr int AT_CB_REGS = 24;  // splits per warp whose rows are held in registers
+template <int DPT>
+__global__ void __launch_bounds__(AT_CB_THREADS) k_attn_combine(const float* __restrict__ partials,
+                                                                 float* __restrict__ ctx, XRun* __restrict__ ctx_runs,
+                                                                 uint32_t nh, uint32_t nkv, uint32_t S, StepState* st,
+                                                                 uint32_t run0) {
+  constexpr uint32_t HD = 32 * DPT;
+  using VecT = typename std::conditional<DPT == 4, float4, float2>::type;
   __shared__ float ws[4][AT_MAXS];
-  __shared__ float sv[128];
+  __shared__ __align__(16) float red[4][HD];
+  __shared__ float sv[HD];
   Tracer tr;
   if (threadIdx.x == 0) {
     tr.begin(TR_COMBINE, gridDim.x);
@@ -1568,15 +1602,17 @@ __global__ void k_attn_combine(const float* __restrict__ partials, float* __rest
   pdl_wait();
   if (threadIdx.x == 0) tr.mark(1);
   (void)st;
-  const uint32_t G = nh / nkv, h = blockIdx.x, kvh = h / G, hg = h % G, d = threadIdx.x;
-  const uint32_t lane = d & 31, warp = d >> 5;
-  const uint32_t Spad = (S + 3) & ~3u;
+  const uint32_t G = nh / nkv, h = blockIdx.x, kvh = h / G, hg = h % G;
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float2* stats = reinterpret_cast<const float2*>(partials) + ((uint64_t)kvh * G + hg) * S;
-  const float4* acc4 =
-      reinterpret_cast<const float4*>(partials + ((2 * (uint64_t)nkv * G * S + 3) & ~3ull) + (((uint64_t)h) * hd + d) * Spad);
-  float4 av[AT_ACC_REGS];
+  const VecT* rows = reinterpret_cast<const VecT*>(partials + ((2 * (uint64_t)nkv * G * S + 3) & ~3ull) +
+                                                   (uint64_t)h * S * HD) + lane;
+  VecT av[AT_CB_REGS];
 #pragma unroll
-  for (int k = 0; k < AT_ACC_REGS; k++) av[k] = (4u * k < Spad) ? acc4[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < AT_CB_REGS; k++) {
+    const uint32_t s2 = warp + 4 * k;
+    if (s2 < S) av[k] = rows[(uint64_t)s2 * (HD / DPT)];
+  }
   float2 sm[AT_MAXS / 32];
 #pragma unroll
   for (int k = 0; k < AT_MAXS / 32; k++) {
@@ -1591,39 +1627,47 @@ __global__ void k_attn_combine(const float* __restrict__ partials, float* __rest
   float den = 0.f;
 #pragma unroll
   for (int k = 0; k < AT_MAXS / 32; k++) {
-    const uint32_t s2 = lane + 32 * k;
     const float w = sm[k].x == -INFINITY ? 0.f : expf(sm[k].x - M);
-    if (s2 < Spad) ws[warp][s2] = w;
+    ws[warp][lane + 32 * k] = w;
     den = fmaf(w, sm[k].y, den);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
   __syncwarp();
   const float* w = ws[warp];
-  float n0 = 0.f, n1 = 0.f, n2 = 0.f, n3 = 0.f;  // four independent chains
+  float n[DPT];
 #pragma unroll
-  for (int k = 0; k < AT_ACC_REGS; k++) {
-    if (4u * k >= Spad) break;
-    n0 = fmaf(w[4 * k], av[k].x, n0);
-    n1 = fmaf(w[4 * k + 1], av[k].y, n1);
-    n2 = fmaf(w[4 * k + 2], av[k].z, n2);
-    n3 = fmaf(w[4 * k + 3], av[k].w, n3);
+  for (int i = 0; i < DPT; i++) n[i] = 0.f;
+#pragma unroll
+  for (int k = 0; k < AT_CB_REGS; k++) {
+    const uint32_t s2 = warp + 4 * k;
+    if (s2 >= S) break;
+    const float* a = reinterpret_cast<const float*>(&av[k]);
+#pragma unroll
+    for (int i = 0; i < DPT; i++) n[i] = fmaf(w[s2], a[i], n[i]);
   }
-  for (uint32_t k = AT_ACC_REGS; 4 * k < Spad; k++) {
-    float4 a4 = acc4[k];
-    n0 = fmaf(w[4 * k], a4.x, n0);
-    n1 = fmaf(w[4 * k + 1], a4.y, n1);
-    n2 = fmaf(w[4 * k + 2], a4.z, n2);
-    n3 = fmaf(w[4 * k + 3], a4.w, n3);
+  for (uint32_t s2 = warp + 4 * AT_CB_REGS; s2 < S; s2 += 4) {
+    const VecT v4 = rows[(uint64_t)s2 * (HD / DPT)];
+    const float* a = reinterpret_cast<const float*>(&v4);
+#pragma unroll
+    for (int i = 0; i < DPT; i++) n[i] = fmaf(w[s2], a[i], n[i]);
   }
-  const float num = (n0 + n1) + (n2 + n3);
-  const float v = __fdiv_rn(num, den);
-  if (threadIdx.x == 0) tr.mark(2);
-  ctx[(uint64_t)h * hd + d] = v;
-  // run records of ctx (the o_proj input): 8 runs per 128-wide head
-  sv[d] = v;
+#pragma unroll
+  for (int i = 0; i < DPT; i++) red[warp][lane * DPT + i] = n[i];
   __syncthreads();
-  values_to_runs(sv, hd, nullptr, ctx_runs, run0 + h * (hd / 16), d, hd);
+  // thread d < HD: the head's output element d
+  const uint32_t d = threadIdx.x;
+  float v = 0.f;
+  if (d < HD) {
+    const float num = (red[0][d] + red[1][d]) + (red[2][d] + red[3][d]);
+    v = __fdiv_rn(num, den);
+    ctx[(uint64_t)h * HD + d] = v;
+    sv[d] = v;
+  }
+  if (threadIdx.x == 0) tr.mark(2);
+  __syncthreads();
+  // run records of ctx (the o_proj input): HD / 16 runs per head
+  if (d < HD) values_to_runs(sv, HD, nullptr, ctx_runs, run0 + h * (HD / 16), d, HD);
   if (threadIdx.x == 0) tr.mark(4);
 }
 
@@ -1634,8 +1678,8 @@ uint32_t attention_splits(uint32_t n_kv) {
 }
 
 uint64_t attention_partial_floats(uint32_t nh, uint32_t nkv, uint32_t hd, uint32_t splits) {
-  uint32_t G = nh / nkv, Spad = (splits + 3) & ~3u;
-  return ((2ull * nkv * G * splits + 3) & ~3ull) + (uint64_t)nkv * G * hd * Spad;
+  uint32_t G = nh / nkv;
+  return ((2ull * nkv * G * splits + 3) & ~3ull) + (uint64_t)nkv * G * splits * hd;
 }
 
 static size_t attention_smem(uint32_t hd, uint32_t eb = 4) { return (size_t)AT_NBUF * 2 * AT_TP * hd * eb; }
@@ -1671,8 +1715,12 @@ void launch_attention(const AttnLaunch& a, cudaStream_t s) {
                a.n_heads, a.n_kv, a.max_ctx, a.state);
   else
     fail(FZ_EINVAL, "head_dim %u unsupported (64 or 128)", a.hd);
-  launch_pdl(k_attn_combine, dim3(a.n_heads), dim3(a.hd), 0, s, (const float*)a.partials, a.ctx,
-             reinterpret_cast<XRun*>(a.ctx_runs), a.n_heads, a.n_kv, a.hd, splits, a.state, a.ctx_run0);
+  if (a.hd == 128)
+    launch_pdl(k_attn_combine<4>, dim3(a.n_heads), dim3(AT_CB_THREADS), 0, s, (const float*)a.partials, a.ctx,
+               reinterpret_cast<XRun*>(a.ctx_runs), a.n_heads, a.n_kv, splits, a.state, a.ctx_run0);
+  else
+    launch_pdl(k_attn_combine<2>, dim3(a.n_heads), dim3(AT_CB_THREADS), 0, s, (const float*)a.partials, a.ctx,
+               reinterpret_cast<XRun*>(a.ctx_runs), a.n_heads, a.n_kv, splits, a.state, a.ctx_run0);
 }
 
 // ---------------------------------------------------------------------------
