@@ -1360,7 +1360,6 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
   constexpr uint32_t EB = sizeof(KT);
   constexpr int DPL = HD / 32;
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ __align__(16) float qs[AT_MAXG][HD];
   __shared__ __align__(8) uint64_t bar[AT_NBUF];
   const uint32_t G = nh / nkv, kvh = blockIdx.y, split = blockIdx.x, S = gridDim.x;
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1434,15 +1433,21 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
   auto parity = [&](uint32_t j) { return ((j / AT_NBUF) + ((redo && (j % AT_NBUF) < pre) ? 1u : 0u)) & 1u; };
   if (tid == 0)
     for (uint32_t j = redo ? 0 : pre; j < ntiles && j < (uint32_t)AT_NBUF; j++) issue(j, t0, t1, pos);
-  // rotated queries
+  // rotated query of warp w's head, dims lane*DPL .. lane*DPL + DPL - 1, in
+  // registers: dim i < half is a*c - b*s, dim i + half is a*s + b*c, with
+  // (a, b) = (q[i], q[i + half]) and (c, s) = the table's row pos, entry i
   const float2* csp = cs + (uint64_t)pos * half;
-  for (uint32_t idx = tid; idx < G * half; idx += AT_THREADS) {
-    uint32_t h = idx / half, i = idx % half;
-    const float* x = qkv + (uint64_t)(kvh * G + h) * HD;
-    float a = x[i], b = x[i + half];
-    float2 c = csp[i];
-    qs[h][i] = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
-    qs[h][i + half] = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
+  float qv[DPL];
+  if (warp < G) {
+    const float* x = qkv + (uint64_t)(kvh * G + warp) * HD;
+    const uint32_t i0 = lane * DPL, j0 = i0 < half ? i0 : i0 - half;
+#pragma unroll
+    for (int d = 0; d < DPL; d++) {
+      const float a = x[j0 + d], b = x[j0 + d + half];
+      const float2 c = csp[j0 + d];
+      qv[d] = i0 < half ? __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y))
+                        : __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
+    }
   }
   const bool owns_pos = n && t1 == total;
   float kn[2] = {0.f, 0.f}, vn[2] = {0.f, 0.f};
@@ -1464,16 +1469,11 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn(const float* __restrict__ q
     kv_st(vdst + tid, vn[0]);
     kv_st(vdst + tid + half, vn[1]);
   }
-  __syncthreads();
   if (tid == 0) tr.mark(2);
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
-  float m = -INFINITY, l = 0.f, acc[DPL], qv[DPL];
+  float m = -INFINITY, l = 0.f, acc[DPL];
 #pragma unroll
-  for (int d = 0; d < DPL; d++) {
-    acc[d] = 0.f;
-    qv[d] = qs[warp < G ? warp : 0][lane * DPL + d];
-  }
-  (void)qv;
+  for (int d = 0; d < DPL; d++) acc[d] = 0.f;
   for (uint32_t j = 0; j < ntiles; j++) {
     const uint32_t b = j % AT_NBUF, a = t0 + j * AT_TP, tn = min(t1, a + AT_TP) - a;
     KT* kt = tiles + (size_t)b * 2 * AT_TP * HD;
