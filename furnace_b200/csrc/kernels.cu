@@ -234,79 +234,134 @@ void launch_repack(uint32_t dtype, const uint8_t* raw, uint8_t* dst, uint32_t r0
 // the last unit of a row of 32 mod 64 Q8_0 / Q5_0 columns).  Inlined with
 // constant indices, so o may be a register array.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void dequant_unit(uint32_t dt, const uint8_t* base, uint32_t rows, uint32_t r,
-                                             uint32_t cols, uint32_t u, float* o) {
-  uint32_t c = lay_chunk_of(dt, cols, u);
-  uint32_t cu0 = lay_cu0(dt, cols, c), nu = lay_cu0(dt, cols, c + 1) - cu0, lu = u - cu0;
+// One 64-element unit's bytes in registers (fetch_unit), decoded by
+// decode_unit.  Q4_K: a = the super-block's header (d, dmin, 12 scale bytes),
+// b, c = the unit's 32 quant bytes.  Q6_K: a, b = nibble bytes, c = high-bit
+// bytes, x0 = the unit's 4 scales, x1 = d.  Q8_0: a..d = 64 quants, x0 = the
+// two blocks' d.  Q5_0: a, b = nibble bytes, x0, x1 = the two blocks' high
+// bits, c.x = the two blocks' d.
+struct RawUnit {
+  uint4 a, b, c, d;
+  uint32_t x0, x1;
+};
+__device__ __forceinline__ uint32_t byte_of(const uint4& v, uint32_t k) {
+  const uint32_t w = k < 4 ? v.x : k < 8 ? v.y : k < 12 ? v.z : v.w;
+  return (w >> (8 * (k & 3))) & 0xFFu;
+}
+__device__ __forceinline__ uint32_t byte_of2(const uint4& lo, const uint4& hi, uint32_t k) {
+  return k < 16 ? byte_of(lo, k) : byte_of(hi, k - 16);
+}
+
+__device__ __forceinline__ RawUnit fetch_unit(uint32_t dt, const uint8_t* base, uint32_t rows, uint32_t r,
+                                              uint32_t cols, uint32_t u) {
+  const uint32_t c = lay_chunk_of(dt, cols, u);
+  const uint32_t cu0 = lay_cu0(dt, cols, c), nu = lay_cu0(dt, cols, c + 1) - cu0, lu = u - cu0;
   const uint8_t* ch = base + lay_tile_off(dt, cols, rows, r, c);
+  RawUnit w{};
   if (dt == FZ_Q4_K) {
-    uint32_t j64 = u & 3;
     const uint8_t* blk = ch + 144 * (lu >> 2);
-    float d = h2f(blk[0] | (blk[1] << 8)), dmin = h2f(blk[2] | (blk[3] << 8));
-    const uint8_t* s = blk + 4;
+    w.a = *reinterpret_cast<const uint4*>(blk);
+    w.b = *reinterpret_cast<const uint4*>(blk + 16 + 32 * (u & 3));
+    w.c = *reinterpret_cast<const uint4*>(blk + 32 + 32 * (u & 3));
+  } else if (dt == FZ_Q6_K) {
+    const uint32_t k = u & 3;
+    const uint8_t* body = ch + 208 * (lu >> 2);
+    w.a = *reinterpret_cast<const uint4*>(body + 32 * k);
+    w.b = *reinterpret_cast<const uint4*>(body + 32 * k + 16);
+    w.c = *reinterpret_cast<const uint4*>(body + 128 + 16 * k);
+    w.x0 = *reinterpret_cast<const uint32_t*>(body + 192 + 4 * k);
+    w.x1 = *reinterpret_cast<const uint16_t*>(ch + 208 * (nu >> 2) + 2 * (lu >> 2));
+  } else if (dt == FZ_Q8_0) {
+    const uint4* q = reinterpret_cast<const uint4*>(ch + 64 * lu);
+    w.a = q[0];
+    w.b = q[1];
+    if (2 * u + 1 < cols / 32) {  // a last half unit holds one block
+      w.c = q[2];
+      w.d = q[3];
+    }
+    w.x0 = *reinterpret_cast<const uint32_t*>(ch + 64 * nu + 4 * lu);
+  } else {
+    const uint4* q = reinterpret_cast<const uint4*>(ch + 32 * lu);
+    w.a = q[0];
+    if (2 * u + 1 < cols / 32) w.b = q[1];
+    const uint2 h = *reinterpret_cast<const uint2*>(ch + 32 * nu + 8 * lu);
+    w.x0 = h.x;
+    w.x1 = h.y;
+    w.c.x = *reinterpret_cast<const uint32_t*>(ch + 32 * nu + round16u(8 * nu) + 4 * lu);
+  }
+  return w;
+}
+
+// The unit's 64 values, in the reference's arithmetic (src/quant.rs:17-133).
+// A last half unit (Q8_0 / Q5_0 with an odd block count) writes o[0..31] only.
+__device__ __forceinline__ void decode_unit(uint32_t dt, uint32_t cols, uint32_t u, const RawUnit& w, float* o) {
+  if (dt == FZ_Q4_K) {
+    const uint32_t j64 = u & 3;
+    const float d = h2f(w.a.x & 0xFFFFu), dmin = h2f(w.a.x >> 16);
     float scv[2], mv[2];
+#pragma unroll
     for (int t = 0; t < 2; t++) {
-      int j = 2 * j64 + t;
+      const uint32_t j = 2 * j64 + t;  // scale byte s[k] is header byte 4 + k
       uint32_t sc, m;
       if (j < 4) {
-        sc = s[j] & 63;
-        m = s[j + 4] & 63;
+        sc = byte_of(w.a, 4 + j) & 63;
+        m = byte_of(w.a, 8 + j) & 63;
       } else {
-        sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
-        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+        sc = (byte_of(w.a, 8 + j) & 0x0F) | ((byte_of(w.a, j) >> 6) << 4);
+        m = (byte_of(w.a, 8 + j) >> 4) | ((byte_of(w.a, 4 + j) >> 6) << 4);
       }
       scv[t] = (float)sc;
       mv[t] = (float)m;
     }
-    float d1 = __fmul_rn(d, scv[0]), min1 = __fmul_rn(dmin, mv[0]);
-    float d2 = __fmul_rn(d, scv[1]), min2 = __fmul_rn(dmin, mv[1]);
-    const uint8_t* q = blk + 16 + 32 * j64;
+    const float d1 = __fmul_rn(d, scv[0]), min1 = __fmul_rn(dmin, mv[0]);
+    const float d2 = __fmul_rn(d, scv[1]), min2 = __fmul_rn(dmin, mv[1]);
 #pragma unroll
-    for (int l = 0; l < 32; l++) {
-      o[l] = __fsub_rn(__fmul_rn(d1, (float)(q[l] & 0x0F)), min1);
-      o[32 + l] = __fsub_rn(__fmul_rn(d2, (float)(q[l] >> 4)), min2);
+    for (uint32_t l = 0; l < 32; l++) {
+      const uint32_t q = byte_of2(w.b, w.c, l);
+      o[l] = __fsub_rn(__fmul_rn(d1, (float)(q & 0x0F)), min1);
+      o[32 + l] = __fsub_rn(__fmul_rn(d2, (float)(q >> 4)), min2);
     }
   } else if (dt == FZ_Q6_K) {
-    const uint32_t k = u & 3;
-    const uint8_t* body = ch + 208 * (lu >> 2);
-    const uint8_t* dp = ch + 208 * (nu >> 2) + 2 * (lu >> 2);
-    float d = h2f(dp[0] | (dp[1] << 8));
+    const float d = h2f(w.x1);
 #pragma unroll
     for (uint32_t i = 0; i < 64; i++) {
-      uint32_t nib = (body[32 * k + (i & 31)] >> (i < 32 ? 0 : 4)) & 15;
-      uint32_t hb = (body[128 + 16 * k + (i & 15)] >> (2 * (i >> 4))) & 3;
-      int q = (int)(nib | (hb << 4)) - 32;
-      float sc = (float)(int8_t)body[192 + 4 * k + (i >> 4)];
+      const uint32_t nib = (byte_of2(w.a, w.b, i & 31) >> (i < 32 ? 0 : 4)) & 15;
+      const uint32_t hb = (byte_of(w.c, i & 15) >> (2 * (i >> 4))) & 3;
+      const int q = (int)(nib | (hb << 4)) - 32;
+      const float sc = (float)(int8_t)((w.x0 >> (8 * (i >> 4))) & 0xFFu);
       o[i] = __fmul_rn(__fmul_rn(d, sc), (float)q);  // (d * sc) * q, src/quant.rs:127-130
     }
   } else {
-    uint32_t nb = cols / 32;
+    const uint32_t nb = cols / 32;
 #pragma unroll
     for (uint32_t k = 0; k < 2; k++) {
-      uint32_t blk = 2 * u + k;
-      if (blk >= nb) break;
+      if (2 * u + k >= nb) break;
       float* ob = o + 32 * k;
       if (dt == FZ_Q8_0) {
-        const uint8_t* dp = ch + 64 * nu + 4 * lu + 2 * k;
-        float d = h2f(dp[0] | (dp[1] << 8));
-        const uint8_t* q = ch + 64 * lu + 32 * k;
+        const float d = h2f((w.x0 >> (16 * k)) & 0xFFFFu);
+        const uint4& lo = k ? w.c : w.a;
+        const uint4& hi = k ? w.d : w.b;
 #pragma unroll
-        for (int i = 0; i < 32; i++) ob[i] = __fmul_rn(d, (float)(int8_t)q[i]);
+        for (uint32_t i = 0; i < 32; i++) ob[i] = __fmul_rn(d, (float)(int8_t)byte_of2(lo, hi, i));
       } else {
-        const uint8_t* qs = ch + 32 * lu + 16 * k;
-        const uint8_t* hp = ch + 32 * nu + 8 * lu + 4 * k;
-        uint32_t qh = hp[0] | (hp[1] << 8) | (hp[2] << 16) | ((uint32_t)hp[3] << 24);
-        const uint8_t* dp = ch + 32 * nu + round16u(8 * nu) + 4 * lu + 2 * k;
-        float d = h2f(dp[0] | (dp[1] << 8));
+        const uint4& qs = k ? w.b : w.a;
+        const uint32_t qh = k ? w.x1 : w.x0;
+        const float d = h2f((w.c.x >> (16 * k)) & 0xFFFFu);
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-          uint32_t hi0 = ((qh >> j) & 1) << 4, hi1 = ((qh >> (j + 16)) & 1) << 4;
-          ob[j] = __fmul_rn(d, (float)((int)((qs[j] & 0x0F) | hi0) - 16));
-          ob[j + 16] = __fmul_rn(d, (float)((int)((qs[j] >> 4) | hi1) - 16));
+        for (uint32_t j = 0; j < 16; j++) {
+          const uint32_t hi0 = ((qh >> j) & 1) << 4, hi1 = ((qh >> (j + 16)) & 1) << 4;
+          const uint32_t qb = byte_of(qs, j);
+          ob[j] = __fmul_rn(d, (float)((int)((qb & 0x0F) | hi0) - 16));
+          ob[j + 16] = __fmul_rn(d, (float)((int)((qb >> 4) | hi1) - 16));
         }
       }
     }
   }
+}
+
+__device__ __forceinline__ void dequant_unit(uint32_t dt, const uint8_t* base, uint32_t rows, uint32_t r,
+                                             uint32_t cols, uint32_t u, float* o) {
+  decode_unit(dt, cols, u, fetch_unit(dt, base, rows, r, cols, u), o);
 }
 
 __global__ void k_dequant(uint32_t dt, const uint8_t* __restrict__ base, uint32_t total_rows, uint32_t cols, uint32_t r0,
@@ -1331,7 +1386,13 @@ void launch_embed(const DevMat& emb, StepState* st, float* x, cudaStream_t s) {
 constexpr int AT_THREADS = 256;
 constexpr int AT_MAXG = 8;
 constexpr int AT_TP = 32;    // positions per tile
-constexpr int AT_NBUF = 3;   // tiles in flight
+#ifndef AT_NBUF_DEF
+#define AT_NBUF_DEF 3
+#endif
+#ifndef AT_CTAS_PER_SM
+#define AT_CTAS_PER_SM 2
+#endif
+constexpr int AT_NBUF = AT_NBUF_DEF;  // tiles in flight
 
 // KV cache elements: f32 (the reference's KvCache) or f16 (FZ_KV_F16: values
 // rounded to nearest even when appended, read back exactly).
@@ -1673,7 +1734,7 @@ __global__ void __launch_bounds__(AT_CB_THREADS) k_attn_combine(const float* __r
 
 // Two CTAs per SM: more warps in flight hide the latency-bound tile loop.
 uint32_t attention_splits(uint32_t n_kv) {
-  uint32_t s = (2 * (uint32_t)num_sms() + n_kv - 1) / n_kv;
+  uint32_t s = (AT_CTAS_PER_SM * (uint32_t)num_sms() + n_kv - 1) / n_kv;
   return s < 1 ? 1 : s > AT_MAXS ? AT_MAXS : s;
 }
 
