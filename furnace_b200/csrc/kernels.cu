@@ -516,10 +516,7 @@ uint32_t runs_for(uint32_t cols) { return runs_for_dev(cols); }
 // GEMV
 // ---------------------------------------------------------------------------
 constexpr int GV_CWARPS = 15;                      // consumer warps (16 warps per block with the producer)
-#ifndef GV_RPW_DEF
-#define GV_RPW_DEF 2
-#endif
-constexpr int GV_RPW = GV_RPW_DEF;                 // rows per consumer warp per stage
+constexpr int GV_RPW = 2;                          // rows per consumer warp per stage
 #ifndef GV_PAIRS_DEF
 #define GV_PAIRS_DEF 1
 #endif
@@ -1386,6 +1383,9 @@ void launch_embed(const DevMat& emb, StepState* st, float* x, cudaStream_t s) {
 constexpr int AT_THREADS = 256;
 constexpr int AT_MAXG = 8;
 constexpr int AT_TP = 32;    // positions per tile
+// Build parameters: tiles in flight per block, and blocks per SM that the
+// split count is sized for (3 blocks need AT_NBUF_DEF=2 to fit in shared
+// memory; measured slower on C3)
 #ifndef AT_NBUF_DEF
 #define AT_NBUF_DEF 3
 #endif
@@ -1732,7 +1732,7 @@ __global__ void __launch_bounds__(AT_CB_THREADS) k_attn_combine(const float* __r
   if (threadIdx.x == 0) tr.mark(4);
 }
 
-// Two CTAs per SM: more warps in flight hide the latency-bound tile loop.
+// AT_CTAS_PER_SM blocks per SM (2): more warps in flight hide the latency-bound tile loop.
 uint32_t attention_splits(uint32_t n_kv) {
   uint32_t s = (AT_CTAS_PER_SM * (uint32_t)num_sms() + n_kv - 1) / n_kv;
   return s < 1 ? 1 : s > AT_MAXS ? AT_MAXS : s;
