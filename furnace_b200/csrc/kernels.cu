@@ -1215,8 +1215,14 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
 
 // ---- host side ---------------------------------------------------------------
 constexpr uint32_t GV_SMEM = 200 * 1024;   // one block per SM
-constexpr uint32_t GV_PF_AHEAD = 96 * 1024;
-constexpr uint32_t GV_PF_NEXT = 64 * 1024;
+#ifndef GV_PF_AHEAD_KB
+#define GV_PF_AHEAD_KB 96
+#endif
+#ifndef GV_PF_NEXT_KB
+#define GV_PF_NEXT_KB 64
+#endif
+constexpr uint32_t GV_PF_AHEAD = GV_PF_AHEAD_KB * 1024;  // L2 prefetch distance ahead of the copies
+constexpr uint32_t GV_PF_NEXT = GV_PF_NEXT_KB * 1024;    // of the next kernel's stream, per CTA
 
 // Install (cap > 0) or remove (cap == 0) the decode-step trace buffer.
 void trace_install(TraceRec* buf, uint32_t cap) {
