@@ -1214,7 +1214,10 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const __grid_constant__ 
 }
 
 // ---- host side ---------------------------------------------------------------
-constexpr uint32_t GV_SMEM = 200 * 1024;   // one block per SM
+#ifndef GV_SMEM_KB
+#define GV_SMEM_KB 200
+#endif
+constexpr uint32_t GV_SMEM = GV_SMEM_KB * 1024;  // one block per SM
 #ifndef GV_PF_AHEAD_KB
 #define GV_PF_AHEAD_KB 96
 #endif
