@@ -388,6 +388,15 @@ def test_greedy_128_steps_tiny(tiny):
     _greedy_parity(tiny, 9, 128, seed=4)
 
 
+def test_greedy_one_kv_head_256_splits(tmp_path):
+    """One KV head shared by 8 query heads: the decode attention then runs the
+    most splits per KV head (256), as every tensor-parallel rank does that
+    holds a single KV head (C3 at TP4, C4/C5 at TP8).  A 300-token prompt
+    spreads the cache over all splits; 48 greedy steps against the oracle."""
+    path = synth.write(synth.spec("tiny", n_kv_heads=1), str(tmp_path / "kv1.gguf"))
+    _greedy_parity(path, 300, 48, seed=8)
+
+
 def test_greedy_stop_ids(tiny, orc):
     ref = orc.Model(tiny)
     ids = synth.prompt_ids(ref.vocab, 5, seed=6)
