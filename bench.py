@@ -41,6 +41,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 # rank 0 prints exactly one JSON line: keep NCCL's version banner off stdout
 os.environ["NCCL_DEBUG"] = "WARN"
+# Under tensor parallelism the decode step's NCCL traffic is setup and an
+# 8-byte argmax all-reduce per token (the residual exchange runs over peer
+# memory); only the batched prefill all-reduces [T, H] partials.  NVLink
+# SHARP (NVLS) stays off unless the caller sets it, as in the measured runs.
+os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
 
 STEP_TOKENS = 16
 CONFIG = "c3"
