@@ -18,12 +18,14 @@ e2e   : the same metric through the public C-ABI call (fz_decode_greedy)
         timed on the host cores, one decode token per step.
 
 With --gpus N > 1 (torchrun, one process per GPU) the ranks form N / TP
-groups of --tp TP consecutive ranks (default 1).  A group decodes one stream,
+groups of --tp TP consecutive ranks.  A group decodes one stream,
 tensor-parallel over its TP GPUs (one NCCL communicator per group), and the
 groups decode independent streams: value = total tokens/s of all groups;
 scaling "strong" when one group spans all N GPUs, else "weak".  The default
-(independent replicas) is the highest whole-job throughput for a model that
-fits one GPU; --tp N measures one stream split over all N GPUs.
+TP is the largest degree <= N that divides N and both head counts: one
+group over all N GPUs where the model allows it (C3 at N = 2 and 4), two
+TP4 groups for C3 at N = 8 (28 query heads do not split 8 ways); --tp 1
+gives N independent replicas.
 """
 
 from __future__ import annotations
